@@ -1,0 +1,95 @@
+// plattice_layout.h -- host+device description of the lattice and scratch
+// buffers used by the sm_100a permutohedral-lattice filter.
+//
+// Geometry.  The image (h x w pixels, n = h*w) is cut into tiles of P pixels
+// (32 wide, P/32 high).  One CTA owns one tile in every per-pixel kernel, so
+// each tile's distinct lattice vertices (at most P*K, K = pd+1) can be
+// deduplicated in shared memory and addressed by a 16-bit local id.
+//
+// Lattice blob (kept from forward to backward):
+//   hdr            LatticeHeader (status word, vertex count m, staged count)
+//   tile_off/cnt   per tile: offset and length of its unique-vertex list
+//   slot_lid       [tile][K][P] uint16   local id of each (pixel, simplex corner)
+//   slot_w         [tile][K][P] float    barycentric weight of the same slot
+//   staged_vid     [U]          int32    global vertex id of each staged key
+//   nbr            [K][m]       int2     blur neighbours (+, -) per axis, -1 absent
+//   vb0, vb1       [m][CPb]     float    backward lattice values (ping-pong)
+// Scratch blob (forward build only):
+//   staged_keys    [U][CW]      uint4    each tile's unique keys (word 0: hash)
+//   staged_vals    [U][CPf]     float    each tile's partial splat sums
+//   table          [cap][CW]    uint4    open-addressed hash table, word 0 = state
+//   vkeys          [m][CW]      uint4    key of every vertex
+//   vf0, vf1       [m][CPf]     float    forward lattice values (ping-pong)
+// U, m <= slots = tiles*K*P: buffers are sized for that bound, but every kernel
+// reads the live counts from the header and touches only what is used.
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#define PL_MAX_PD 16
+#define PL_MAX_VD 8
+
+// status bits (LatticeHeader::status)
+#define PL_ST_SMEM_PROBE 1   /* tile-local table exhausted (cannot happen: sized 2x) */
+#define PL_ST_TABLE_FULL 2   /* global hash table probe limit reached */
+#define PL_ST_SPIN 4         /* a bounded wait on a tile-local insert gave up */
+#define PL_ST_ROUNDS 8       /* global insert did not settle within the round limit */
+
+typedef struct {
+    int status;
+    int m;           /* distinct vertices */
+    int u_total;     /* staged (tile-unique) keys */
+    int cap_log2;    /* hash table capacity in use (log2 of cells) */
+    int n, pd, vd, tiles;
+    int pad[56];     /* header is 256 bytes */
+} LatticeHeader;
+
+static inline int pl_tile_pixels(int pd) { return pd <= 6 ? 256 : (pd <= 10 ? 128 : 64); }
+static inline int pl_key_words(int pd) { return (4 + 2 * pd + 15) / 16; }   /* 16-byte words */
+static inline int pl_pad_ch(int c) { return c <= 2 ? c : ((c + 3) / 4) * 4; }
+static inline size_t pl_align(size_t x) { return (x + 255) & ~(size_t)255; }
+
+typedef struct {
+    int h, w, pd, vd, K, P, TH, tiles_x, tiles_y, tiles;
+    int CW, CPf, CPb;
+    long long slots;      /* tiles*K*P: bound on staged keys and on vertices */
+    int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
+    size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_staged_vid, off_nbr,
+        off_vb0, off_vb1, lattice_bytes;
+    size_t off_skeys, off_svals, off_table, off_vkeys, off_vf0, off_vf1, scratch_bytes;
+} PlLayout;
+
+static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
+    L->h = h; L->w = w; L->pd = pd; L->vd = vd; L->K = pd + 1;
+    L->P = pl_tile_pixels(pd);
+    L->TH = L->P / 32;
+    L->tiles_x = (w + 31) / 32;
+    L->tiles_y = (h + L->TH - 1) / L->TH;
+    L->tiles = L->tiles_x * L->tiles_y;
+    L->CW = pl_key_words(pd);
+    L->CPf = pl_pad_ch(vd + 1);
+    L->CPb = pl_pad_ch(vd);
+    L->slots = (long long)L->tiles * L->K * L->P;
+    int lg = 6;
+    while ((1ll << lg) < 2 * L->slots) lg++;
+    L->cap_max_log2 = lg;
+    const size_t S = (size_t)L->slots, T = (size_t)L->tiles;
+    size_t o = pl_align(sizeof(LatticeHeader));
+    L->off_tile_off = o;   o = pl_align(o + T * 4);
+    L->off_tile_cnt = o;   o = pl_align(o + T * 4);
+    L->off_slot_lid = o;   o = pl_align(o + S * 2);
+    L->off_slot_w = o;     o = pl_align(o + S * 4);
+    L->off_staged_vid = o; o = pl_align(o + S * 4);
+    L->off_nbr = o;        o = pl_align(o + S * L->K * 8);
+    L->off_vb0 = o;        o = pl_align(o + S * L->CPb * 4);
+    L->off_vb1 = o;        o = pl_align(o + S * L->CPb * 4);
+    L->lattice_bytes = o;
+    o = 0;
+    L->off_skeys = o;      o = pl_align(o + S * L->CW * 16);
+    L->off_svals = o;      o = pl_align(o + S * L->CPf * 4);
+    L->off_table = o;      o = pl_align(o + ((size_t)1 << lg) * L->CW * 16);
+    L->off_vkeys = o;      o = pl_align(o + S * L->CW * 16);
+    L->off_vf0 = o;        o = pl_align(o + S * L->CPf * 4);
+    L->off_vf1 = o;        o = pl_align(o + S * L->CPf * 4);
+    L->scratch_bytes = o;
+}
