@@ -1,0 +1,495 @@
+#!/usr/bin/env python
+"""Throughput of the permutohedral-lattice filter, forward + backward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = forward + value-gradient backward of one 1024x1024 image, pd = 5
+(x/32, y/32, rgb/0.08 of a seeded 200-cell Voronoi image), vd = 3, through
+the public autograd API (PermutoLatticeFunction).  Each rank of a torchrun
+job filters its own image(s) (weak scaling, no collective on the data path);
+``value`` is all pixels of all ranks over the slowest rank's device time.
+
+``--impl ours`` (default) times this repository's sm_100a library;
+``--impl reference`` times the reference CUDA extension (PLOO, built from the
+reference sources for sm_100a into oracle/_ref) through its own forward /
+backward with the same protocol, on rank 0 only.
+
+Timing: W untimed warm-up steps, then exactly K steps, each bracketed by CUDA
+events on the launching stream; L2 is flushed (256 MiB write) between steps,
+outside the events.  ``e2e`` repeats the K steps from pinned host buffers:
+H2D of features/values/grad and D2H of out/grad inside the timed region.
+Prints one JSON line (rank 0).
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "Mpixel/s fwd+bwd (1024², pd=5, vd=3) at 1/2/4/8 B200; % of HBM roofline"
+UNIT = "Mpixel/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="voronoi1024_pd5_vd3")
+    ap.add_argument("--images-per-gpu", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=2048, help="output pixels of the CPU sample")
+    ap.add_argument("--profile-steps", type=int, default=10)
+    ap.add_argument("--soak-seconds", type=float, default=1.0,
+                    help="untimed steps before warm-up so that clocks settle under load")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- distributed plumbing
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def dist_init(world, local):
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world <= 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of this GPU's clocks and throttle reasons."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.proc = None
+        self.path = None
+        sel = []
+        try:
+            p = torch.cuda.get_device_properties(device)
+            sel = ["-i", f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"]
+        except Exception:
+            sel = []
+        self.cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "100"] + sel
+
+    def start(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(prefix="plattice_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(self.cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        pw = [num(r[3]) for r in rows if num(r[3]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        top = max(mx) if mx else None
+        loaded = [s for s in sm if top and s >= 0.5 * top] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": top,
+                "power_w_max": max(pw) if pw else None, "samples": len(rows), "reasons": reasons}
+
+
+# ---------------------------------------------------------------- implementations
+
+def ours_impl():
+    from plattice_pytorch_b200 import PermutoLatticeFunction, _lib
+    _lib.lib()   # the CUDA library must load: there is no fallback
+    return PermutoLatticeFunction
+
+
+def reference_impl():
+    from oracle import ref as oref
+    if not oref.ploo_available():
+        return None, "reference extension not built (make -C oracle ref)"
+    P = oref.load_ploo()
+
+    class RefFunction(torch.autograd.Function):
+        """The reference's own plattice.py Function (plattice.py:7-19) over its PLOO."""
+
+        @staticmethod
+        def forward(ctx, feature, values):
+            weight, out = P.forward(feature, values)
+            ctx.save_for_backward(weight, feature)
+            return out
+
+        @staticmethod
+        @torch.autograd.function.once_differentiable
+        def backward(ctx, grad_output):
+            weight, feature = ctx.saved_tensors
+            return None, P.backward(feature, grad_output.contiguous(), weight)
+
+    return RefFunction, None
+
+
+def step(fn, f, v, g):
+    out = fn.apply(f, v)
+    (gv,) = torch.autograd.grad(out, (v,), (g,))
+    return out, gv
+
+
+# ---------------------------------------------------------------- measurement
+
+def load_inputs(args, rank, dev):
+    from plattice_pytorch_b200.workloads import make_workload
+    imgs = []
+    for i in range(args.images_per_gpu):
+        w = make_workload(args.workload, seed=rank * args.images_per_gpu + i)
+        imgs.append(w)
+    return imgs
+
+
+def timed_device(fn, batch, steps, flush):
+    """Per-step CUDA-event time (ms) summed over `steps`; L2 flushed between steps."""
+    evs = []
+    for _ in range(steps):
+        flush.fill_(1.0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for (f, v, g) in batch:
+            step(fn, f, v, g)
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def timed_e2e(fn, host, steps, dev):
+    """Whole-loop CUDA-event time (ms) of `steps` end-to-end steps from pinned
+    host buffers, including H2D of the inputs and D2H of out and grad."""
+    outs = [(torch.empty(h[1].shape, pin_memory=True), torch.empty(h[1].shape, pin_memory=True))
+            for h in host]
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        for (hf, hv, hg), (ho, hgr) in zip(host, outs):
+            f = hf.to(dev, non_blocking=True)
+            v = hv.to(dev, non_blocking=True).requires_grad_(True)
+            g = hg.to(dev, non_blocking=True)
+            out, gv = step(fn, f, v, g)
+            ho.copy_(out.detach(), non_blocking=True)
+            hgr.copy_(gv, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def kernel_bytes(stage, n, pd, vd, m, u, cap_log2):
+    """Compulsory HBM bytes of one launch of a stage of this implementation."""
+    K = pd + 1
+    CW = (4 + 2 * pd + 15) // 16
+    pad = (lambda c: c if c <= 2 else ((c + 3) // 4) * 4)
+    CPF, CPB = pad(vd + 1), pad(vd)
+    slot = 6 * K * n   # uint16 local id + float weight per slot
+    return {
+        "tile_build": n * 4 * (pd + vd) + slot + u * (16 * CW + 4 * CPF),
+        "clear": (1 << cap_log2) * 16 * CW + u * 4 * (CPF + CPB),
+        "insert": u * (16 * CW + 4 * CPF + 4) + m * (2 * 16 * CW + 4 * CPF),
+        "neighbors": m * (16 * CW + 8 * K),
+        "blur_fwd": m * (8 * CPF + 8),
+        "slice_fwd": slot + m * 4 * CPF + n * 4 * (vd + 1),
+        "zero": m * 4 * CPB,
+        "splat_bwd": slot + n * 4 * (vd + 1) + m * 4 * CPB,
+        "blur_bwd": m * (8 * CPB + 8),
+        "slice_bwd": slot + m * 4 * CPB + n * 4 * vd,
+    }[stage]
+
+
+def stage_bytes(n, pd, vd, m):
+    """Algorithmic bytes of splat + blur + slice (lattice build excluded):
+    B_fwd = N(8V+16K+4) + M(8(V+1)(K+1) + 8K), B_bwd = N(8V+16K+4) + M(8V(K+1) + 8K)."""
+    K = pd + 1
+    b_fwd = n * (8 * vd + 16 * K + 4) + m * (8 * (vd + 1) * (K + 1) + 8 * K)
+    b_bwd = n * (8 * vd + 16 * K + 4) + m * (8 * vd * (K + 1) + 8 * K)
+    return b_fwd, b_bwd
+
+
+def profile_ours(fn, batch, steps, flush, n, pd, vd):
+    """Per-stage device times from CUDA events around every launch (untimed run)."""
+    from plattice_pytorch_b200 import PLOO, _lib
+    f, v, g = batch[0]
+    _, _, lat = PLOO.lattice_forward(f, v.detach())
+    info = PLOO.lattice_info(lat)
+    del lat
+    _lib.profile_read()
+    _lib.profile_enable(True)
+    try:
+        for _ in range(steps):
+            flush.fill_(1.0)
+            step(fn, f, v, g)
+        torch.cuda.synchronize()
+        prof = _lib.profile_read()
+    finally:
+        _lib.profile_enable(False)
+    return info, prof
+
+
+def traffic_from_profiles(kernel):
+    """ncu DRAM bytes per launch recorded for `kernel` in profiles/traffic.txt
+    ('<stage> <bytes per launch>' lines), or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.txt")
+    try:
+        with open(path) as fh:
+            for line in fh:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == kernel:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline(f_np, v_np, g_np, sample):
+    """The brute-force dense Gaussian (oracle port of the reference test's
+    brute_force_bilateral, generalised) on `sample` output pixels forward and
+    `sample` backward, all host threads."""
+    import oracle
+    threads = len(os.sched_getaffinity(0))
+    n = f_np.shape[0] * f_np.shape[1]
+    rows = range(0, min(sample, n))
+    t0 = time.perf_counter()
+    oracle.brute_gaussian(f_np, v_np, rows=rows, threads=threads)
+    t1 = time.perf_counter()
+    wt = np.full(n, 1.0 / n, np.float32)
+    oracle.brute_gaussian(f_np, g_np, rows=rows, threads=threads, weight=wt)
+    t2 = time.perf_counter()
+    px = rows.stop - rows.start
+    cpu = "unknown"
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    cpu = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"value": px / (t2 - t0) / 1e6, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"brute-force O(N^2) Gaussian: {px} output pixels forward + {px} backward "
+                      f"of the {n}-pixel image ({t1 - t0:.2f} s + {t2 - t1:.2f} s)",
+            "cpu": cpu}
+
+
+def cpu_lattice_oracle(f_np, v_np, g_np):
+    """The sequential C restatement of the lattice filter on one core (whole image)."""
+    import oracle
+    t0 = time.perf_counter()
+    wo, _, _ = oracle.forward(f_np, v_np)
+    oracle.backward(f_np, g_np, wo)
+    dt = time.perf_counter() - t0
+    n = f_np.shape[0] * f_np.shape[1]
+    return {"value": n / dt / 1e6, "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"lattice oracle, whole image forward + backward ({dt:.2f} s)"}
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_setup()
+    dev = torch.device("cuda", local)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        fn, why = reference_impl()
+        if fn is None:
+            print(json.dumps({"impl": "reference", "unavailable": why}))
+            return
+        world_eff = 1
+    else:
+        fn = ours_impl()
+        dist_init(world, local)
+        world_eff = world
+
+    imgs = load_inputs(args, rank, dev)
+    h, w, pd = imgs[0]["features"].shape
+    vd = imgs[0]["values"].shape[2]
+    n = h * w
+    batch = []
+    for im in imgs:
+        f = torch.from_numpy(im["features"]).to(dev)
+        v = torch.from_numpy(im["values"]).to(dev).requires_grad_(True)
+        g = torch.from_numpy(im["grad"]).to(dev)
+        batch.append((f, v, g))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    clocks = ClockSampler(dev)
+    clocks.start()
+    # soak: untimed steps until clocks settle under load
+    t_end = time.perf_counter() + args.soak_seconds
+    while time.perf_counter() < t_end:
+        for (f, v, g) in batch:
+            step(fn, f, v, g)
+        torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        for (f, v, g) in batch:
+            step(fn, f, v, g)
+    torch.cuda.synchronize()
+    barrier(world_eff)
+    torch.cuda.synchronize()
+    t_dev = timed_device(fn, batch, args.steps, flush)
+    torch.cuda.synchronize()
+    barrier(world_eff)
+    t_dev = max_over_ranks(t_dev, world_eff)
+
+    # end to end from pinned host buffers
+    host = [(torch.from_numpy(im["features"]).pin_memory(), torch.from_numpy(im["values"]).pin_memory(),
+             torch.from_numpy(im["grad"]).pin_memory()) for im in imgs]
+    for _ in range(max(1, args.warmup // 2)):
+        timed_e2e(fn, host, 1, dev)
+    barrier(world_eff)
+    t_e2e = timed_e2e(fn, host, args.steps, dev)
+    barrier(world_eff)
+    t_e2e = max_over_ranks(t_e2e, world_eff)
+    clk = clocks.stop()
+
+    px_total = world_eff * len(batch) * n * args.steps
+    value = px_total / (t_dev * 1e-3) / 1e6
+    h2d = sum(int(x.numel()) * 4 for hh in host for x in hh)
+    d2h = sum(2 * int(hh[1].numel()) * 4 for hh in host)
+    res = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_eff, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t_dev / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "h": h, "w": w, "pd": pd, "vd": vd,
+                   "images_per_gpu": len(batch),
+                   "l2": "flushed between timed steps (256 MiB write, outside the events)",
+                   "parallelism": "one image lattice per rank, no collective" if world_eff > 1 else "1 GPU",
+                   "api": "PermutoLatticeFunction forward + torch.autograd.grad backward"},
+        "e2e": {"value": px_total / (t_e2e * 1e-3) / 1e6, "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "clocks": clk,
+    }
+    if args.impl == "reference":
+        res["impl"] = "reference"
+        res["reference_build"] = "reference permuto.cpp + permutohedral.cu, unmodified, nvcc sm_100a"
+
+    if args.impl == "ours":
+        info, prof = profile_ours(fn, batch, args.profile_steps, flush, n, pd, vd)
+        m, u, cap = info["m"], info["u_total"], info["cap_log2"]
+        peak, peak_kind = hbm_peak()
+        per_stage = {}
+        launches_per_step = 0
+        for st, (ms, cnt) in prof.items():
+            if cnt == 0:
+                continue
+            launches_per_step += cnt / args.profile_steps
+            kb = kernel_bytes(st, n, pd, vd, m, u, cap)
+            avg_ms = ms / cnt
+            per_stage[st] = {"ms_per_step": ms / args.profile_steps, "launches_per_step": cnt / args.profile_steps,
+                             "avg_launch_us": avg_ms * 1e3, "bytes_per_launch": kb,
+                             "gbs": kb / (avg_ms * 1e-3) / 1e9}
+        dom = max(per_stage, key=lambda k: per_stage[k]["ms_per_step"])
+        d = per_stage[dom]
+        ach = d["gbs"]
+        res["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
+                           "frac": ach / peak, "peak_kind": peak_kind,
+                           "traffic": traffic_from_profiles(dom),
+                           "bytes_per_launch": d["bytes_per_launch"]}
+        b_fwd, b_bwd = stage_bytes(n, pd, vd, m)
+        stage_ms = sum(per_stage[s]["ms_per_step"] for s in per_stage
+                       if s in ("tile_build", "insert", "blur_fwd", "slice_fwd", "zero", "splat_bwd",
+                                "blur_bwd", "slice_bwd"))
+        all_ms = sum(per_stage[s]["ms_per_step"] for s in per_stage)
+        res["roofline_stages"] = {
+            "definition": "(B_fwd + B_bwd) of splat+blur+slice / summed device time of those kernels "
+                          "(tile_build, insert, blur, slice, splat_bwd); B per the lattice byte formula",
+            "bytes": b_fwd + b_bwd, "kernel_ms": stage_ms,
+            "achieved": (b_fwd + b_bwd) / (stage_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+            "frac": (b_fwd + b_bwd) / (stage_ms * 1e-3) / 1e9 / peak,
+            "frac_end_to_end": (b_fwd + b_bwd) / ((t_dev / args.steps) * 1e-3) / 1e9 / peak,
+            "frac_all_kernels": (b_fwd + b_bwd) / (all_ms * 1e-3) / 1e9 / peak}
+        res["stages"] = per_stage
+        res["lattice"] = {"m": m, "u_total": u, "cap_log2": cap}
+        res["gpu_launches"] = int(round(launches_per_step * args.steps * len(batch)))
+
+    if rank == 0 and world_eff == 1 and not args.no_cpu_baseline:
+        im = imgs[0]
+        res["cpu_baseline"] = cpu_baseline(im["features"], im["values"], im["grad"], args.cpu_sample)
+        res["cpu_lattice_oracle"] = cpu_lattice_oracle(im["features"], im["values"], im["grad"])
+    if rank == 0:
+        print(json.dumps(res))
+    if world_eff > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

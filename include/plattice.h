@@ -1,0 +1,118 @@
+/*
+ * plattice.h -- C ABI of the sm_100a permutohedral-lattice filter
+ * (libplattice_b200.so, built from plattice_pytorch_b200/csrc).
+ *
+ * Drop-in boundary for the reference OliveMY/plattice_pytorch, whose CUDA
+ * entry points are
+ *   permuto_filter      (permutohedral.cu:685-715, declared permuto.cpp:11-20)
+ *   permuto_filter_grad (permutohedral.cu:717-748, declared permuto.cpp:21-31)
+ * and whose workspace is sized by allocate_workspace (permuto.cpp:51-69).
+ * The reference binds them to Python through a torch extension (permuto.cpp);
+ * here the boundary is plain C: device pointers, sizes, an explicit CUDA
+ * stream (passed as void*) and an int status.  No call synchronises the stream
+ * except plattice_lattice_info and plattice_vertex_keys.
+ *
+ * Tensors: features [h][w][pd], values / grad / out [h][w][vd],
+ * weight [h][w] (one float per pixel), all float32, contiguous, on the current
+ * CUDA device.  1 <= pd <= 16, 1 <= vd <= 8 (permuto.cpp:37-40).
+ *
+ * Memory.  The caller allocates two device buffers, sized by
+ * plattice_workspace_sizes:
+ *   lattice  -- the built lattice; kept from a forward call to the backward
+ *               calls that reuse it.
+ *   scratch  -- transient; only needed during a call.
+ * Calls that overlap in time must not share either buffer.
+ */
+#ifndef PLATTICE_H
+#define PLATTICE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PLATTICE_ABI_VERSION 1
+
+/* status codes */
+#define PLATTICE_OK 0
+#define PLATTICE_ERR_INVALID 1   /* bad dimensions, null pointer, or image too large */
+#define PLATTICE_ERR_WORKSPACE 2 /* lattice or scratch buffer smaller than required */
+#define PLATTICE_ERR_CUDA 3      /* a CUDA runtime call or kernel launch failed */
+#define PLATTICE_ERR_DEVICE 4    /* the lattice's device status word reports a failure */
+
+/* device status bits reported by plattice_lattice_info */
+#define PLATTICE_DEV_TABLE_FULL 2 /* hash-table probe limit reached (table too small) */
+#define PLATTICE_DEV_WAIT_LIMIT 4 /* a bounded wait on a concurrent insert gave up */
+#define PLATTICE_DEV_ROUND_LIMIT 8
+
+/* Version of this ABI (PLATTICE_ABI_VERSION). */
+int plattice_abi_version(void);
+
+/* Human-readable text of a status code. */
+const char* plattice_error_string(int status);
+
+/* Bytes of the lattice and scratch buffers for an h x w image.  Replaces the
+ * workspace sizing of permuto.cpp:51-69. */
+int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes,
+                             size_t* scratch_bytes);
+
+/* Forward filter: builds the lattice of `features` into `lattice`, splats
+ * `values`, blurs along the pd+1 lattice axes in order 0..pd and slices:
+ *   out[p] = sum_i w_pi L[v_pi][0:vd] / sum_i w_pi L[v_pi][vd],
+ *   weight_out[p] = 1 / sum_i w_pi L[v_pi][vd].
+ * Replaces permuto_filter (permutohedral.cu:685); same argument order, plus
+ * buffer sizes and the stream. */
+int plattice_forward(float* weight_out, float* out, const float* values, const float* features,
+                     void* lattice, size_t lattice_bytes, void* scratch, size_t scratch_bytes,
+                     int pd, int vd, int w, int h, void* stream);
+
+/* Value gradient: grad_values_out = S^T B^T S'(grad * weight_in), the blur in
+ * axis order pd..0.  lattice_state: 0 = `lattice` does not hold the lattice of
+ * `features` (it is rebuilt, `scratch` required); 1 = it holds the lattice
+ * built by the last plattice_forward on these features and no backward has
+ * used it yet; 2 = it holds that lattice and was used by an earlier backward.
+ * Replaces permuto_filter_grad (permutohedral.cu:717), which always rebuilds. */
+int plattice_backward(float* grad_values_out, const float* grad, const float* weight_in,
+                      const float* features, void* lattice, size_t lattice_bytes,
+                      int lattice_state, void* scratch, size_t scratch_bytes, int pd, int vd,
+                      int w, int h, void* stream);
+
+/* Synchronises `stream` and reads the lattice header: device status bits,
+ * vertex count m, number of tile-unique keys staged, log2 of the hash-table
+ * capacity used.  Any pointer may be NULL.  Returns PLATTICE_ERR_DEVICE when
+ * the status word is non-zero.  No reference counterpart (the reference has
+ * no error reporting). */
+int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total, int* cap_log2,
+                          void* stream);
+
+/* Copies the vertex keys of the lattice just built (before `scratch` is
+ * reused) into keys_dev [max_keys][pd] int16 on the device, in vertex-id
+ * order; synchronises `stream` and stores the vertex count in *m.  Test
+ * support: the reference keeps its keys inside its workspace
+ * (permutohedral.cu:84) and exposes none. */
+int plattice_vertex_keys(const void* lattice, const void* scratch, int pd, int vd, int w, int h,
+                         int16_t* keys_dev, int max_keys, int* m, void* stream);
+
+/* Test support: force the hash-table capacity to 2^log2 cells (0 = automatic,
+ * >= twice the staged keys).  A capacity below the vertex count makes the
+ * build report PLATTICE_DEV_TABLE_FULL instead of looping. */
+void plattice_debug_set_table_cap_log2(int log2_cells);
+
+/* Profiling (no reference counterpart): when enabled, every kernel launch is
+ * bracketed by CUDA events recorded on its stream.  plattice_profile_read
+ * waits for the recorded events, writes per stage the summed milliseconds and
+ * the launch count (stage order as plattice_profile_stage_name), and clears
+ * the record.  Stages: 0 tile_build, 1 clear, 2 insert, 3 neighbors,
+ * 4 blur_fwd, 5 slice_fwd, 6 zero, 7 splat_bwd, 8 blur_bwd, 9 slice_bwd. */
+#define PLATTICE_PROFILE_STAGES 10
+void plattice_profile_enable(int on);
+int plattice_profile_read(double* ms_total, int* launches, int n_stages);
+const char* plattice_profile_stage_name(int stage);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PLATTICE_H */

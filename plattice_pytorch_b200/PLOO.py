@@ -1,0 +1,225 @@
+"""Drop-in replacement of the reference's extension module ``PLOO``.
+
+The reference builds ``PLOO`` from permuto.cpp (setup.py:5-7) and calls it as
+``PLOO.forward(features, values) -> [weight, out]`` and
+``PLOO.backward(features, grad_values, weight) -> grad`` (permuto.cpp:71-158,
+plattice.py:10,16).  This module keeps those names, argument meanings, return
+order, input checks and error messages (permuto.cpp:33-40, 72-85, 113-132;
+a failed check raises RuntimeError as TORCH_CHECK does) and runs the sm_100a
+library through its C ABI (include/plattice.h).
+
+Differences that a caller can observe only as speed:
+  * ``backward`` reuses the lattice that ``forward`` built for the same
+    ``features`` tensor (same object, unmodified since), instead of rebuilding
+    it as permutohedral.cu:615-635 does; otherwise it rebuilds.
+  * kernels run on PyTorch's current stream of the tensors' device, not on the
+    legacy default stream, and no call synchronises the host.
+
+Set the environment variable PLATTICE_CHECK=1 to synchronise after every call
+and raise if the device reports a failure.
+"""
+import ctypes
+import os
+import weakref
+
+import torch
+
+from . import _lib
+
+__all__ = ["forward", "backward", "Lattice", "lattice_forward", "lattice_backward",
+           "lattice_info", "vertex_keys"]
+
+_CHECK = os.environ.get("PLATTICE_CHECK", "0") not in ("", "0")
+
+
+def _require(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_input(t, name):
+    # CHECK_CUDA / CHECK_CONTIGUOUS of permuto.cpp:33-35
+    _require(isinstance(t, torch.Tensor) and t.is_cuda, f"{name} must be CUDA")
+    _require(t.is_contiguous(), f"{name} must be contiguous")
+
+
+def _check_dims(pd, vd):
+    # permuto.cpp:37-40
+    _require(1 <= pd <= 16, "feature dimension pd must be in [1, 16]")
+    _require(1 <= vd <= 8, "value dimension vd must be in [1, 8]")
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+class Lattice:
+    """A lattice built on the device for one ``features`` tensor.
+
+    Holds the lattice buffer (kept for backward calls), optionally the scratch
+    buffer of the build (needed by :func:`vertex_keys`), and whether a
+    backward pass has already used its value buffers."""
+
+    __slots__ = ("buf", "scratch", "h", "w", "pd", "vd", "device", "used", "_feat_ref",
+                 "_feat_version", "_feat_ptr", "__weakref__")
+
+    def __init__(self, features, vd, buf, scratch):
+        self.buf = buf
+        self.scratch = scratch
+        self.h, self.w, self.pd = (int(s) for s in features.shape)
+        self.vd = int(vd)
+        self.device = features.device
+        self.used = False
+        self._feat_ref = weakref.ref(features)
+        self._feat_version = features._version
+        self._feat_ptr = features.data_ptr()
+
+    def matches(self, features, vd, same_object=True):
+        """True when this lattice was built from ``features`` as it is now.
+        ``same_object=False`` drops the identity test, for callers (autograd's
+        saved tensors) that hand back a new tensor object over the same,
+        version-checked storage."""
+        if same_object and self._feat_ref() is not features:
+            return False
+        return (features.data_ptr() == self._feat_ptr and int(vd) == self.vd
+                and tuple(features.shape) == (self.h, self.w, self.pd)
+                and features.device == self.device
+                and (not same_object or features._version == self._feat_version))
+
+
+def _sync_check(lat, call):
+    st = ctypes.c_int(0)
+    rc = _lib.lib().plattice_lattice_info(_ptr(lat.buf), ctypes.byref(st), None, None, None,
+                                          _stream(lat.device))
+    if rc != _lib.OK:
+        raise _lib.PlatticeError(call, rc, f"device status bits {st.value:#x}")
+
+
+def lattice_forward(features, values, keep_scratch=False):
+    """Forward filter; returns ``(weight [H,W,1], out [H,W,vd], Lattice)``."""
+    _check_input(features, "features")
+    _check_input(values, "values")
+    _require(features.dim() == 3, "features must be [H, W, pd]")
+    _require(values.dim() == 3, "values must be [H, W, vd]")
+    _require(features.dtype == torch.float32, "features must be float32")
+    _require(values.dtype == torch.float32, "values must be float32")
+    _require(features.shape[0] == values.shape[0] and features.shape[1] == values.shape[1],
+             "features and values must have matching H, W")
+    h, w, pd = (int(s) for s in features.shape)
+    vd = int(values.shape[2])
+    _check_dims(pd, vd)
+    _require(values.device == features.device, "features and values must be on the same device")
+    dev = features.device
+    with torch.cuda.device(dev):
+        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
+        weight = torch.empty((h, w, 1), dtype=torch.float32, device=dev)
+        lb, sb = _lib.workspace_sizes(h, w, pd, vd)
+        buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+        scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+        rc = _lib.lib().plattice_forward(_ptr(weight), _ptr(out), _ptr(values), _ptr(features),
+                                         _ptr(buf), lb, _ptr(scratch), sb, pd, vd, w, h,
+                                         _stream(dev))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError("plattice_forward", rc, f"h={h} w={w} pd={pd} vd={vd}")
+        lat = Lattice(features, vd, buf, scratch if keep_scratch else None)
+        if _CHECK and h * w > 0:
+            _sync_check(lat, "plattice_forward")
+    return weight, out, lat
+
+
+def lattice_backward(features, grad_values, weight_saved, lattice=None, saved=False):
+    """Value gradient; reuses ``lattice`` when it was built from ``features``
+    as they are now, else rebuilds.  ``saved=True`` when ``features`` comes
+    from autograd's saved tensors (whose version check already guarantees
+    they are unmodified).  Returns ``grad [H,W,vd]``."""
+    _check_input(features, "features")
+    _check_input(grad_values, "grad_values")
+    _check_input(weight_saved, "weight_saved")
+    _require(features.dim() == 3, "features must be [H, W, pd]")
+    _require(grad_values.dim() == 3, "grad_values must be [H, W, vd]")
+    _require(weight_saved.dim() == 3 and weight_saved.shape[2] == 1, "weight_saved must be [H, W, 1]")
+    _require(features.dtype == torch.float32, "features must be float32")
+    _require(grad_values.dtype == torch.float32, "grad_values must be float32")
+    _require(weight_saved.dtype == torch.float32, "weight_saved must be float32")
+    _require(features.shape[0] == grad_values.shape[0] and features.shape[1] == grad_values.shape[1],
+             "features and grad_values must have matching H, W")
+    _require(features.shape[0] == weight_saved.shape[0] and features.shape[1] == weight_saved.shape[1],
+             "features and weight_saved must have matching H, W")
+    h, w, pd = (int(s) for s in features.shape)
+    vd = int(grad_values.shape[2])
+    _check_dims(pd, vd)
+    _require(grad_values.device == features.device and weight_saved.device == features.device,
+             "features, grad_values and weight_saved must be on the same device")
+    dev = features.device
+    with torch.cuda.device(dev):
+        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
+        lb, sb = _lib.workspace_sizes(h, w, pd, vd)
+        if lattice is not None and lattice.matches(features, vd, same_object=not saved):
+            state = 2 if lattice.used else 1
+            buf, scratch, sbytes = lattice.buf, None, 0
+        else:
+            state = 0
+            lattice = None
+            buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+            scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+            sbytes = sb
+        rc = _lib.lib().plattice_backward(_ptr(out), _ptr(grad_values), _ptr(weight_saved),
+                                          _ptr(features), _ptr(buf), lb, state, _ptr(scratch), sbytes,
+                                          pd, vd, w, h, _stream(dev))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError("plattice_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
+        if lattice is not None:
+            lattice.used = True
+        if _CHECK and h * w > 0:
+            chk = lattice if lattice is not None else Lattice(features, vd, buf, None)
+            _sync_check(chk, "plattice_backward")
+    return out
+
+
+# The most recent forward's lattice, for a standalone backward on the same
+# features (the reference's tests call forward then backward directly).
+_last = None
+
+
+def forward(features, values):
+    """``PLOO.forward(features, values) -> [weight_out [H,W,1], out [H,W,vd]]``."""
+    global _last
+    weight, out, lat = lattice_forward(features, values)
+    _last = lat
+    return [weight, out]
+
+
+def backward(features, grad_values, weight_saved):
+    """``PLOO.backward(features, grad_values, weight_saved) -> grad [H,W,vd]``."""
+    return lattice_backward(features, grad_values, weight_saved, _last)
+
+
+def lattice_info(lattice):
+    """Synchronise and read the lattice header: dict(status, m, u_total, cap_log2)."""
+    st, m, u, cap = (ctypes.c_int(0) for _ in range(4))
+    rc = _lib.lib().plattice_lattice_info(_ptr(lattice.buf), ctypes.byref(st), ctypes.byref(m),
+                                          ctypes.byref(u), ctypes.byref(cap), _stream(lattice.device))
+    if rc not in (_lib.OK, _lib.ERR_DEVICE):
+        raise _lib.PlatticeError("plattice_lattice_info", rc)
+    return {"status": st.value, "m": m.value, "u_total": u.value, "cap_log2": cap.value}
+
+
+def vertex_keys(lattice):
+    """Vertex keys [m, pd] int16 (device tensor) of a lattice built with
+    ``lattice_forward(..., keep_scratch=True)``."""
+    _require(lattice.scratch is not None, "vertex_keys needs a lattice built with keep_scratch=True")
+    info = lattice_info(lattice)
+    m = info["m"]
+    keys = torch.empty((max(m, 1), lattice.pd), dtype=torch.int16, device=lattice.device)
+    mm = ctypes.c_int(0)
+    with torch.cuda.device(lattice.device):
+        rc = _lib.lib().plattice_vertex_keys(_ptr(lattice.buf), _ptr(lattice.scratch), lattice.pd,
+                                             lattice.vd, lattice.w, lattice.h, _ptr(keys), m,
+                                             ctypes.byref(mm), _stream(lattice.device))
+    if rc != _lib.OK:
+        raise _lib.PlatticeError("plattice_vertex_keys", rc)
+    return keys[:mm.value]

@@ -1,0 +1,283 @@
+// plattice_capi.cu -- the C ABI declared in include/plattice.h: argument
+// checks, buffer sizing, run-time pd dispatch to the per-pd instantiations.
+#include <cuda_runtime.h>
+#include <limits.h>
+#include <stdio.h>
+
+#include <mutex>
+#include <vector>
+
+#include "../../include/plattice.h"
+#include "plattice_impl.cuh"
+
+namespace pl {
+#define PL_DECLARE_PD(N)                                                                    \
+    extern template cudaError_t run_forward<N>(const CallArgs&);                             \
+    extern template cudaError_t run_backward<N>(const CallArgs&);                            \
+    extern template cudaError_t run_export_keys<N>(const void*, const void*, const PlLayout&, \
+                                                   int16_t*, int, cudaStream_t);
+PL_DECLARE_PD(1) PL_DECLARE_PD(2) PL_DECLARE_PD(3) PL_DECLARE_PD(4)
+PL_DECLARE_PD(5) PL_DECLARE_PD(6) PL_DECLARE_PD(7) PL_DECLARE_PD(8)
+PL_DECLARE_PD(9) PL_DECLARE_PD(10) PL_DECLARE_PD(11) PL_DECLARE_PD(12)
+PL_DECLARE_PD(13) PL_DECLARE_PD(14) PL_DECLARE_PD(15) PL_DECLARE_PD(16)
+}  // namespace pl
+
+static int g_cap_override_log2 = 0;
+
+// ---------------------------------------------------------------- profiling
+
+namespace {
+struct ProfRec {
+    int stage;
+    cudaEvent_t begin, end;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<cudaEvent_t> g_prof_pool;
+std::vector<ProfRec> g_prof_done;
+ProfRec g_prof_open[pl::STAGE_COUNT];
+
+cudaEvent_t prof_event() {
+    if (!g_prof_pool.empty()) {
+        cudaEvent_t e = g_prof_pool.back();
+        g_prof_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    return e;
+}
+}  // namespace
+
+namespace pl {
+bool prof_enabled() { return g_prof_on; }
+
+void prof_mark(int stage, cudaStream_t s, bool begin) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on || stage < 0 || stage >= STAGE_COUNT) return;
+    cudaEvent_t e = prof_event();
+    if (!e) return;
+    cudaEventRecord(e, s);
+    if (begin) {
+        g_prof_open[stage].stage = stage;
+        g_prof_open[stage].begin = e;
+    } else {
+        ProfRec r = g_prof_open[stage];
+        r.end = e;
+        if (r.begin) g_prof_done.push_back(r);
+        g_prof_open[stage].begin = nullptr;
+    }
+}
+}  // namespace pl
+
+#define PL_PD_SWITCH(PD, CALL)          \
+    switch (PD) {                       \
+        case 1: return CALL(1);         \
+        case 2: return CALL(2);         \
+        case 3: return CALL(3);         \
+        case 4: return CALL(4);         \
+        case 5: return CALL(5);         \
+        case 6: return CALL(6);         \
+        case 7: return CALL(7);         \
+        case 8: return CALL(8);         \
+        case 9: return CALL(9);         \
+        case 10: return CALL(10);       \
+        case 11: return CALL(11);       \
+        case 12: return CALL(12);       \
+        case 13: return CALL(13);       \
+        case 14: return CALL(14);       \
+        case 15: return CALL(15);       \
+        case 16: return CALL(16);       \
+        default: return cudaErrorInvalidValue; \
+    }
+
+static cudaError_t dispatch_forward(const pl::CallArgs& a) {
+#define PL_FWD(N) pl::run_forward<N>(a)
+    PL_PD_SWITCH(a.lay.pd, PL_FWD)
+#undef PL_FWD
+}
+
+static cudaError_t dispatch_backward(const pl::CallArgs& a) {
+#define PL_BWD(N) pl::run_backward<N>(a)
+    PL_PD_SWITCH(a.lay.pd, PL_BWD)
+#undef PL_BWD
+}
+
+static cudaError_t dispatch_keys(const void* lat, const void* scr, const PlLayout& lay, int16_t* out,
+                                 int max_keys, cudaStream_t s) {
+#define PL_KEYS(N) pl::run_export_keys<N>(lat, scr, lay, out, max_keys, s)
+    PL_PD_SWITCH(lay.pd, PL_KEYS)
+#undef PL_KEYS
+}
+
+static int sm_count_current() {
+    static int cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    return n;
+}
+
+// dimension checks of permuto.cpp:37-40 plus the index range of this build
+// (32-bit vertex ids and slot indices)
+static int check_dims(int h, int w, int pd, int vd) {
+    if (pd < 1 || pd > PL_MAX_PD || vd < 1 || vd > PL_MAX_VD) return PLATTICE_ERR_INVALID;
+    if (h < 0 || w < 0) return PLATTICE_ERR_INVALID;
+    if (h == 0 || w == 0) return PLATTICE_OK;
+    PlLayout L;
+    pl_layout(&L, h, w, pd, vd);
+    if (L.slots > (1ll << 29)) return PLATTICE_ERR_INVALID;
+    return PLATTICE_OK;
+}
+
+static int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return PLATTICE_OK;
+    if (e == cudaErrorInvalidValue) return PLATTICE_ERR_INVALID;
+    return PLATTICE_ERR_CUDA;
+}
+
+extern "C" {
+
+int plattice_abi_version(void) { return PLATTICE_ABI_VERSION; }
+
+const char* plattice_error_string(int status) {
+    switch (status) {
+        case PLATTICE_OK: return "ok";
+        case PLATTICE_ERR_INVALID: return "invalid argument (pd must be in [1, 16], vd in [1, 8], image within size limits, pointers non-null)";
+        case PLATTICE_ERR_WORKSPACE: return "lattice or scratch buffer smaller than plattice_workspace_sizes requires";
+        case PLATTICE_ERR_CUDA: return "CUDA runtime error";
+        case PLATTICE_ERR_DEVICE: return "device-side failure reported in the lattice status word";
+        default: return "unknown status";
+    }
+}
+
+int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes, size_t* scratch_bytes) {
+    const int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    size_t lb = 256, sb = 256;
+    if (h > 0 && w > 0) {
+        PlLayout L;
+        pl_layout(&L, h, w, pd, vd);
+        lb = L.lattice_bytes;
+        sb = L.scratch_bytes;
+    }
+    if (lattice_bytes) *lattice_bytes = lb;
+    if (scratch_bytes) *scratch_bytes = sb;
+    return PLATTICE_OK;
+}
+
+int plattice_forward(float* weight_out, float* out, const float* values, const float* features,
+                     void* lattice, size_t lattice_bytes, void* scratch, size_t scratch_bytes, int pd,
+                     int vd, int w, int h, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (h == 0 || w == 0) return PLATTICE_OK;
+    if (!weight_out || !out || !values || !features || !lattice || !scratch) return PLATTICE_ERR_INVALID;
+    pl::CallArgs a = {};
+    pl_layout(&a.lay, h, w, pd, vd);
+    if (lattice_bytes < a.lay.lattice_bytes || scratch_bytes < a.lay.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
+    a.features = features; a.values = values; a.weight_in = nullptr;
+    a.out = out; a.wout = weight_out;
+    a.lattice = lattice; a.scratch = scratch;
+    a.stream = static_cast<cudaStream_t>(stream);
+    a.sm_count = sm_count_current();
+    a.lattice_state = 0;
+    a.cap_override_log2 = g_cap_override_log2;
+    return cuda_status(dispatch_forward(a));
+}
+
+int plattice_backward(float* grad_values_out, const float* grad, const float* weight_in, const float* features,
+                      void* lattice, size_t lattice_bytes, int lattice_state, void* scratch, size_t scratch_bytes,
+                      int pd, int vd, int w, int h, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (h == 0 || w == 0) return PLATTICE_OK;
+    if (lattice_state < 0 || lattice_state > 2) return PLATTICE_ERR_INVALID;
+    if (!grad_values_out || !grad || !weight_in || !features || !lattice) return PLATTICE_ERR_INVALID;
+    if (lattice_state == 0 && !scratch) return PLATTICE_ERR_INVALID;
+    pl::CallArgs a = {};
+    pl_layout(&a.lay, h, w, pd, vd);
+    if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
+    if (lattice_state == 0 && scratch_bytes < a.lay.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
+    a.features = features; a.values = grad; a.weight_in = weight_in;
+    a.out = grad_values_out; a.wout = nullptr;
+    a.lattice = lattice; a.scratch = scratch;
+    a.stream = static_cast<cudaStream_t>(stream);
+    a.sm_count = sm_count_current();
+    a.lattice_state = lattice_state;
+    a.cap_override_log2 = g_cap_override_log2;
+    return cuda_status(dispatch_backward(a));
+}
+
+int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total, int* cap_log2, void* stream) {
+    if (!lattice) return PLATTICE_ERR_INVALID;
+    LatticeHeader hh;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(&hh, lattice, sizeof(hh), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return PLATTICE_ERR_CUDA;
+    if (status) *status = hh.status;
+    if (m) *m = hh.m;
+    if (u_total) *u_total = hh.u_total;
+    if (cap_log2) *cap_log2 = hh.cap_log2;
+    return hh.status ? PLATTICE_ERR_DEVICE : PLATTICE_OK;
+}
+
+int plattice_vertex_keys(const void* lattice, const void* scratch, int pd, int vd, int w, int h,
+                         int16_t* keys_dev, int max_keys, int* m, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (!lattice || !scratch || (!keys_dev && max_keys > 0)) return PLATTICE_ERR_INVALID;
+    if (h == 0 || w == 0) { if (m) *m = 0; return PLATTICE_OK; }
+    PlLayout L;
+    pl_layout(&L, h, w, pd, vd);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (max_keys > 0) {
+        cudaError_t e = dispatch_keys(lattice, scratch, L, keys_dev, max_keys, s);
+        if (e != cudaSuccess) return cuda_status(e);
+    }
+    return plattice_lattice_info(lattice, nullptr, m, nullptr, nullptr, stream);
+}
+
+void plattice_profile_enable(int on) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_on = on != 0;
+}
+
+int plattice_profile_read(double* ms_total, int* launches, int n_stages) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    for (int i = 0; i < n_stages; ++i) {
+        if (ms_total) ms_total[i] = 0.0;
+        if (launches) launches[i] = 0;
+    }
+    int rc = PLATTICE_OK;
+    for (const ProfRec& r : g_prof_done) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(r.end) != cudaSuccess || cudaEventElapsedTime(&ms, r.begin, r.end) != cudaSuccess)
+            rc = PLATTICE_ERR_CUDA;
+        else if (r.stage < n_stages) {
+            if (ms_total) ms_total[r.stage] += ms;
+            if (launches) launches[r.stage] += 1;
+        }
+        g_prof_pool.push_back(r.begin);
+        g_prof_pool.push_back(r.end);
+    }
+    g_prof_done.clear();
+    return rc;
+}
+
+const char* plattice_profile_stage_name(int stage) {
+    static const char* names[pl::STAGE_COUNT] = {
+        "tile_build", "clear", "insert", "neighbors", "blur_fwd", "slice_fwd",
+        "zero", "splat_bwd", "blur_bwd", "slice_bwd"};
+    return (stage >= 0 && stage < pl::STAGE_COUNT) ? names[stage] : "";
+}
+
+void plattice_debug_set_table_cap_log2(int log2_cells) {
+    g_cap_override_log2 = (log2_cells > 0 && log2_cells < 31) ? log2_cells : 0;
+}
+
+}  // extern "C"
