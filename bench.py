@@ -55,6 +55,8 @@ def parse_args():
     ap.add_argument("--profile-steps", type=int, default=10)
     ap.add_argument("--soak-seconds", type=float, default=1.0,
                     help="untimed steps before warm-up so that clocks settle under load")
+    ap.add_argument("--mode", choices=["full", "device"], default="full",
+                    help="device: only the warm-up and the K device-timed steps (for profilers)")
     return ap.parse_args()
 
 
@@ -253,22 +255,25 @@ def hbm_peak():
 
 
 def kernel_bytes(stage, n, pd, vd, m, u, cap_log2):
-    """Compulsory HBM bytes of one launch of a stage of this implementation."""
+    """Compulsory HBM bytes per step of a stage of this implementation (reads
+    + writes of the data it must touch once; L2-resident gathers not
+    counted)."""
     K = pd + 1
     CW = (4 + 2 * pd + 15) // 16
     pad = (lambda c: c if c <= 2 else ((c + 3) // 4) * 4)
     CPF, CPB = pad(vd + 1), pad(vd)
     slot = 6 * K * n   # uint16 local id + float weight per slot
     return {
-        "tile_build": n * 4 * (pd + vd) + slot + u * (16 * CW + 4 * CPF),
-        "clear": (1 << cap_log2) * 16 * CW + u * 4 * (CPF + CPB),
-        "insert": u * (16 * CW + 4 * CPF + 4) + m * (2 * 16 * CW + 4 * CPF),
+        "tile_build": n * 4 * pd + slot + u * (16 * CW + 4 * (CPF + CPB)),
+        "clear": (1 << cap_log2) * 16 * CW,
+        "insert": u * (2 * 16 * CW + 8) + m * (2 * 16 * CW + 8),   # insert + compaction
+        "splat_fwd": slot + n * 4 * vd + m * 4 * CPF,
         "neighbors": m * (16 * CW + 8 * K),
-        "blur_fwd": m * (8 * CPF + 8),
+        "blur_fwd": K * m * (8 * CPF + 8),
         "slice_fwd": slot + m * 4 * CPF + n * 4 * (vd + 1),
         "zero": m * 4 * CPB,
         "splat_bwd": slot + n * 4 * (vd + 1) + m * 4 * CPB,
-        "blur_bwd": m * (8 * CPB + 8),
+        "blur_bwd": K * m * (8 * CPB + 8),
         "slice_bwd": slot + m * 4 * CPB + n * 4 * vd,
     }[stage]
 
@@ -389,6 +394,16 @@ def main():
         batch.append((f, v, g))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
+    if args.mode == "device":
+        for _ in range(args.warmup):
+            for (f, v, g) in batch:
+                step(fn, f, v, g)
+        t = timed_device(fn, batch, args.steps, flush)
+        if rank == 0:
+            print(json.dumps({"mode": "device", "impl": args.impl, "workload": args.workload,
+                              "ms_per_step": t / args.steps}))
+        return
+
     clocks = ClockSampler(dev)
     clocks.start()
     # soak: untimed steps until clocks settle under load
@@ -452,25 +467,26 @@ def main():
                 continue
             launches_per_step += cnt / args.profile_steps
             kb = kernel_bytes(st, n, pd, vd, m, u, cap)
-            avg_ms = ms / cnt
-            per_stage[st] = {"ms_per_step": ms / args.profile_steps, "launches_per_step": cnt / args.profile_steps,
-                             "avg_launch_us": avg_ms * 1e3, "bytes_per_launch": kb,
-                             "gbs": kb / (avg_ms * 1e-3) / 1e9}
+            step_ms = ms / args.profile_steps
+            per_stage[st] = {"ms_per_step": step_ms, "launches_per_step": cnt / args.profile_steps,
+                             "avg_launch_us": ms / cnt * 1e3, "bytes_per_step": kb,
+                             "gbs": kb / (step_ms * 1e-3) / 1e9}
         dom = max(per_stage, key=lambda k: per_stage[k]["ms_per_step"])
         d = per_stage[dom]
         ach = d["gbs"]
         res["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": ach, "peak": peak, "unit": "GB/s",
                            "frac": ach / peak, "peak_kind": peak_kind,
                            "traffic": traffic_from_profiles(dom),
-                           "bytes_per_launch": d["bytes_per_launch"]}
+                           "bytes_per_step": d["bytes_per_step"],
+                           "launches_per_step": d["launches_per_step"]}
         b_fwd, b_bwd = stage_bytes(n, pd, vd, m)
         stage_ms = sum(per_stage[s]["ms_per_step"] for s in per_stage
-                       if s in ("tile_build", "insert", "blur_fwd", "slice_fwd", "zero", "splat_bwd",
-                                "blur_bwd", "slice_bwd"))
+                       if s in ("splat_fwd", "blur_fwd", "slice_fwd", "zero", "splat_bwd", "blur_bwd", "slice_bwd"))
         all_ms = sum(per_stage[s]["ms_per_step"] for s in per_stage)
         res["roofline_stages"] = {
             "definition": "(B_fwd + B_bwd) of splat+blur+slice / summed device time of those kernels "
-                          "(tile_build, insert, blur, slice, splat_bwd); B per the lattice byte formula",
+                          "(splat_fwd, blur_fwd, slice_fwd, splat_bwd, blur_bwd, slice_bwd); "
+                          "B per the lattice byte formula",
             "bytes": b_fwd + b_bwd, "kernel_ms": stage_ms,
             "achieved": (b_fwd + b_bwd) / (stage_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
             "frac": (b_fwd + b_bwd) / (stage_ms * 1e-3) / 1e9 / peak,

@@ -53,6 +53,10 @@ int plattice_abi_version(void);
 /* Human-readable text of a status code. */
 const char* plattice_error_string(int status);
 
+/* The CUDA error name and text behind the last PLATTICE_ERR_CUDA returned on
+ * the calling thread ("" if none). */
+const char* plattice_last_error_detail(void);
+
 /* Bytes of the lattice and scratch buffers for an h x w image.  Replaces the
  * workspace sizing of permuto.cpp:51-69. */
 int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes,
@@ -104,9 +108,10 @@ void plattice_debug_set_table_cap_log2(int log2_cells);
  * bracketed by CUDA events recorded on its stream.  plattice_profile_read
  * waits for the recorded events, writes per stage the summed milliseconds and
  * the launch count (stage order as plattice_profile_stage_name), and clears
- * the record.  Stages: 0 tile_build, 1 clear, 2 insert, 3 neighbors,
- * 4 blur_fwd, 5 slice_fwd, 6 zero, 7 splat_bwd, 8 blur_bwd, 9 slice_bwd. */
-#define PLATTICE_PROFILE_STAGES 10
+ * the record.  Stages: 0 tile_build, 1 clear, 2 insert (and compaction),
+ * 3 neighbors, 4 blur_fwd, 5 slice_fwd, 6 zero, 7 splat_bwd, 8 blur_bwd,
+ * 9 slice_bwd, 10 splat_fwd. */
+#define PLATTICE_PROFILE_STAGES 11
 void plattice_profile_enable(int on);
 int plattice_profile_read(double* ms_total, int* launches, int n_stages);
 const char* plattice_profile_stage_name(int stage);

@@ -27,6 +27,11 @@ class PlatticeError(RuntimeError):
         msg = f"{call} failed: {error_string(status)} (status {status})"
         if detail:
             msg += f"; {detail}"
+        if status == ERR_CUDA:
+            try:
+                msg += f"; {lib().plattice_last_error_detail().decode()}"
+            except ImportError:
+                pass
         super().__init__(msg)
 
 
@@ -48,6 +53,8 @@ def lib():
         L.plattice_abi_version.argtypes = []
         L.plattice_error_string.restype = ctypes.c_char_p
         L.plattice_error_string.argtypes = [I]
+        L.plattice_last_error_detail.restype = ctypes.c_char_p
+        L.plattice_last_error_detail.argtypes = []
         L.plattice_workspace_sizes.restype = I
         L.plattice_workspace_sizes.argtypes = [I, I, I, I, ctypes.POINTER(S), ctypes.POINTER(S)]
         L.plattice_forward.restype = I
@@ -89,7 +96,7 @@ def workspace_sizes(h, w, pd, vd):
     return lb.value, sb.value
 
 
-PROFILE_STAGES = 10
+PROFILE_STAGES = 11
 
 
 def profile_enable(on=True):

@@ -133,8 +133,11 @@ static int check_dims(int h, int w, int pd, int vd) {
     return PLATTICE_OK;
 }
 
-static int cuda_status(cudaError_t e) {
+static thread_local char g_last_error[256] = "";
+
+static int cuda_status(cudaError_t e, const char* where = "") {
     if (e == cudaSuccess) return PLATTICE_OK;
+    snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
     if (e == cudaErrorInvalidValue) return PLATTICE_ERR_INVALID;
     return PLATTICE_ERR_CUDA;
 }
@@ -142,6 +145,8 @@ static int cuda_status(cudaError_t e) {
 extern "C" {
 
 int plattice_abi_version(void) { return PLATTICE_ABI_VERSION; }
+
+const char* plattice_last_error_detail(void) { return g_last_error; }
 
 const char* plattice_error_string(int status) {
     switch (status) {
@@ -186,7 +191,7 @@ int plattice_forward(float* weight_out, float* out, const float* values, const f
     a.sm_count = sm_count_current();
     a.lattice_state = 0;
     a.cap_override_log2 = g_cap_override_log2;
-    return cuda_status(dispatch_forward(a));
+    return cuda_status(dispatch_forward(a), "plattice_forward");
 }
 
 int plattice_backward(float* grad_values_out, const float* grad, const float* weight_in, const float* features,
@@ -209,7 +214,7 @@ int plattice_backward(float* grad_values_out, const float* grad, const float* we
     a.sm_count = sm_count_current();
     a.lattice_state = lattice_state;
     a.cap_override_log2 = g_cap_override_log2;
-    return cuda_status(dispatch_backward(a));
+    return cuda_status(dispatch_backward(a), "plattice_backward");
 }
 
 int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total, int* cap_log2, void* stream) {
@@ -218,7 +223,7 @@ int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaMemcpyAsync(&hh, lattice, sizeof(hh), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return PLATTICE_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_status(e, "plattice_lattice_info");
     if (status) *status = hh.status;
     if (m) *m = hh.m;
     if (u_total) *u_total = hh.u_total;
@@ -237,7 +242,7 @@ int plattice_vertex_keys(const void* lattice, const void* scratch, int pd, int v
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (max_keys > 0) {
         cudaError_t e = dispatch_keys(lattice, scratch, L, keys_dev, max_keys, s);
-        if (e != cudaSuccess) return cuda_status(e);
+        if (e != cudaSuccess) return cuda_status(e, "plattice_vertex_keys");
     }
     return plattice_lattice_info(lattice, nullptr, m, nullptr, nullptr, stream);
 }
@@ -272,7 +277,7 @@ int plattice_profile_read(double* ms_total, int* launches, int n_stages) {
 const char* plattice_profile_stage_name(int stage) {
     static const char* names[pl::STAGE_COUNT] = {
         "tile_build", "clear", "insert", "neighbors", "blur_fwd", "slice_fwd",
-        "zero", "splat_bwd", "blur_bwd", "slice_bwd"};
+        "zero", "splat_bwd", "blur_bwd", "slice_bwd", "splat_fwd"};
     return (stage >= 0 && stage < pl::STAGE_COUNT) ? names[stage] : "";
 }
 

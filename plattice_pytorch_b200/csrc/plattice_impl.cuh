@@ -32,6 +32,8 @@ inline LatView lat_view(void* base, const PlLayout& L) {
     v.tile_cnt = reinterpret_cast<int*>(b + L.off_tile_cnt);
     v.slot_lid = reinterpret_cast<uint16_t*>(b + L.off_slot_lid);
     v.slot_w = reinterpret_cast<float*>(b + L.off_slot_w);
+    v.slot_order = reinterpret_cast<uint16_t*>(b + L.off_slot_order);
+    v.seg_off = reinterpret_cast<uint16_t*>(b + L.off_seg_off);
     v.staged_vid = reinterpret_cast<int*>(b + L.off_staged_vid);
     v.nbr = reinterpret_cast<int2*>(b + L.off_nbr);
     v.vb0 = reinterpret_cast<float*>(b + L.off_vb0);
@@ -43,8 +45,9 @@ inline ScrView scr_view(void* base, const PlLayout& L) {
     char* b = static_cast<char*>(base);
     ScrView v;
     v.skeys = reinterpret_cast<uint4*>(b + L.off_skeys);
-    v.svals = reinterpret_cast<float*>(b + L.off_svals);
-    v.table = reinterpret_cast<uint4*>(b + L.off_table);
+    v.table = reinterpret_cast<uint32_t*>(b + L.off_table);
+    v.owner = reinterpret_cast<int*>(b + L.off_owner);
+    v.vid_of = reinterpret_cast<int*>(b + L.off_vid_of);
     v.vkeys = reinterpret_cast<uint4*>(b + L.off_vkeys);
     v.vf0 = reinterpret_cast<float*>(b + L.off_vf0);
     v.vf1 = reinterpret_cast<float*>(b + L.off_vf1);
@@ -72,7 +75,7 @@ inline Geo make_geo(const CallArgs& a) {
 }
 
 // opt in to more than 48 KB of dynamic shared memory, once per device
-template <int PD, int V>
+template <int PD>
 cudaError_t prepare_tile_build() {
     static bool done[64] = {};
     constexpr int smem = tile_build_smem_bytes<PD>();
@@ -80,50 +83,76 @@ cudaError_t prepare_tile_build() {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64 || !done[dev]) {
-        e = cudaFuncSetAttribute(k_tile_build<PD, V>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        e = cudaFuncSetAttribute(k_tile_build<PD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) done[dev] = true;
     }
     return cudaSuccess;
 }
 
-// Build the lattice: tile dedup (+ forward splat when values != nullptr),
-// table clear, global insert, blur neighbours.
-template <int PD, int V>
+// Build the lattice: tile dedup (which also zeroes the lattice value rows),
+// table clear, global insert.  Blur neighbours are resolved by the first
+// phase of k_blur_all.
+template <int PD>
 cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
-                          const float* values) {
+                          float* zero_f, int cpf, float* zero_b, int cpb) {
     using C = Cfg<PD>;
-    constexpr int CPF = pad_ch(V + 1), CPB = pad_ch(V);
     const cudaStream_t s = a.stream;
     const int grid = a.sm_count * 8;
-    cudaError_t e = prepare_tile_build<PD, V>();
+    cudaError_t e = prepare_tile_build<PD>();
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(Lv.hdr, 0, sizeof(LatticeHeader), s);
     if (e != cudaSuccess) return e;
     const EmbedConsts ec = embed_consts(PD);
-    PL_LAUNCH(STAGE_TILE_BUILD, s, k_tile_build<PD, V><<<a.lay.tiles, C::P, tile_build_smem_bytes<PD>(), s>>>(
-        a.features, values, geo, ec, Lv, Sv));
-    PL_LAUNCH(STAGE_CLEAR, s, k_clear<<<grid, 256, 0, s>>>(geo, Lv, Sv, C::CW, values ? CPF : 0, CPB));
-    PL_LAUNCH(STAGE_INSERT, s, k_insert<PD, CPF><<<grid, 256, 0, s>>>(Lv, Sv, values ? 1 : 0));
+    PL_LAUNCH(STAGE_TILE_BUILD, s, k_tile_build<PD><<<a.lay.tiles, C::P, tile_build_smem_bytes<PD>(), s>>>(
+        a.features, geo, ec, Lv, Sv, zero_f, cpf, zero_b, cpb));
+    PL_LAUNCH(STAGE_CLEAR, s, k_clear<<<grid, 256, 0, s>>>(geo, Lv, Sv));
+    PL_LAUNCH(STAGE_INSERT, s, k_insert<PD><<<grid * 2, 256, 0, s>>>(Lv, Sv));
+    PL_LAUNCH(STAGE_INSERT, s, k_compact<PD><<<grid, 256, 0, s>>>(Lv, Sv));
     PL_LAUNCH(STAGE_NEIGHBORS, s, k_neighbors<PD><<<grid, 256, 0, s>>>(Lv, Sv));
     return cudaGetLastError();
 }
 
+// Cooperative launch of the fused neighbour + blur kernel on as many CTAs as
+// are co-resident (at most kCoopPerSm per SM).
+constexpr int kCoopPerSm = 2;
+
+template <int PD, int CP>
+cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1, int reverse) {
+    static int per_sm[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int n = (dev >= 0 && dev < 64) ? per_sm[dev] : 0;
+    if (n == 0) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_blur_all<PD, CP>, 256, 0);
+        if (e != cudaSuccess) return e;
+        if (n < 1) return cudaErrorLaunchOutOfResources;
+        if (dev >= 0 && dev < 64) per_sm[dev] = n;
+    }
+    const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
+    void* args[] = {&Lv, &b0, &b1, &reverse};
+    PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
+              e = cudaLaunchCooperativeKernel((const void*)k_blur_all<PD, CP>, dim3(blocks), dim3(256), args, 0,
+                                              a.stream));
+    return e;
+}
+
 template <int PD, int V>
 cudaError_t forward_v(const CallArgs& a) {
-    constexpr int CPF = pad_ch(V + 1);
+    constexpr int CPF = pad_ch(V + 1), CPB = pad_ch(V);
     const Geo geo = make_geo(a);
     const LatView Lv = lat_view(a.lattice, a.lay);
     const ScrView Sv = scr_view(a.scratch, a.lay);
-    cudaError_t e = build_lattice<PD, V>(a, geo, Lv, Sv, a.values);
+    cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, Sv.vf0, CPF, Lv.vb0, CPB);
     if (e != cudaSuccess) return e;
-    const int grid = a.sm_count * 8;
-    float* x = Sv.vf0;
-    float* y = Sv.vf1;
-    for (int ax = 0; ax <= PD; ++ax) {   // axis order 0..pd (permutohedral.cu:585)
-        PL_LAUNCH(STAGE_BLUR_FWD, a.stream, k_blur<CPF><<<grid, 256, 0, a.stream>>>(x, y, Lv.nbr, Lv.hdr, ax, V + 1));
-        float* t = x; x = y; y = t;
-    }
+    PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
+              k_splat<PD, V, true><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.values, nullptr, geo, Lv, Sv, 1,
+                                                                             Sv.vf0));
+    // blur in axis order 0..pd (permutohedral.cu:585)
+    e = launch_blur_all<PD, CPF>(a, Lv, Sv.vf0, Sv.vf1, 0);
+    if (e != cudaSuccess) return e;
+    float* x = ((PD + 1) % 2 == 0) ? Sv.vf0 : Sv.vf1;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
               k_slice<PD, V, true><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.out, a.wout, geo, Lv, x));
     return cudaGetLastError();
@@ -136,21 +165,20 @@ cudaError_t backward_v(const CallArgs& a) {
     const LatView Lv = lat_view(a.lattice, a.lay);
     const ScrView Sv = scr_view(a.scratch, a.lay);
     const int grid = a.sm_count * 8;
-    cudaError_t e;
+    cudaError_t e = cudaSuccess;
     if (a.lattice_state == 0) {
-        e = build_lattice<PD, V>(a, geo, Lv, Sv, nullptr);
+        e = build_lattice<PD>(a, geo, Lv, Sv, nullptr, 0, Lv.vb0, CPB);
         if (e != cudaSuccess) return e;
     } else if (a.lattice_state == 2) {
         PL_LAUNCH(STAGE_ZERO, a.stream, k_zero_rows<<<grid, 256, 0, a.stream>>>(Lv.vb0, Lv.hdr, CPB));
     }
     PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
-              k_splat_bwd<PD, V><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.values, a.weight_in, geo, Lv, Lv.vb0));
-    float* x = Lv.vb0;
-    float* y = Lv.vb1;
-    for (int s = 0; s <= PD; ++s) {   // axis order pd..0 (permutohedral.cu:647)
-        PL_LAUNCH(STAGE_BLUR_BWD, a.stream, k_blur<CPB><<<grid, 256, 0, a.stream>>>(x, y, Lv.nbr, Lv.hdr, PD - s, V));
-        float* t = x; x = y; y = t;
-    }
+              k_splat<PD, V, false><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(
+                  a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, Lv.vb0));
+    // blur in axis order pd..0 (permutohedral.cu:647)
+    e = launch_blur_all<PD, CPB>(a, Lv, Lv.vb0, Lv.vb1, 1);
+    if (e != cudaSuccess) return e;
+    float* x = ((PD + 1) % 2 == 0) ? Lv.vb0 : Lv.vb1;
     PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
               k_slice<PD, V, false><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.out, nullptr, geo, Lv, x));
     return cudaGetLastError();

@@ -1,20 +1,21 @@
 // plattice_kernels.cuh -- sm_100a kernels of the permutohedral-lattice filter.
 //
 // Pipeline of one forward call (all on one stream, no host synchronisation):
-//   k_tile_build   per tile of P pixels: lattice embedding in registers, the
+//   k_tile_build   per tile of P pixels: lattice embedding in registers; the
 //                  tile's distinct vertex keys deduplicated in a shared-memory
-//                  hash table, [v*w, w] pre-summed per distinct vertex in
-//                  shared memory, unique keys + partial sums staged to HBM
-//   k_clear        zero the part of the hash table and of the lattice value
-//                  buffers that this call uses (sized from the staged count)
+//                  hash table (16-bit local ids); unique keys staged to HBM
+//   k_clear        zero the part of the global hash table this call uses
 //   k_insert       global open-addressed insert of the staged keys, compact
-//                  vertex ids allocated per CTA, partial sums reduced with
-//                  vector red.global.add into the lattice values
-//   k_neighbors    blur neighbours of every vertex resolved once per axis
-//   k_blur         K passes of the [1 2 1]/4 stencil over the compact vertices
+//                  vertex ids allocated per CTA
+//   k_splat        per tile: [v*w, w] summed over runs of equal vertex along
+//                  each warp (one row of 32 pixels), one vector red.global.add
+//                  per run into the lattice values
+//   k_blur_all     blur neighbours resolved once, then the pd+1 passes of the
+//                  [1 2 1]/4 stencil over the compact vertex list: one
+//                  cooperative launch with grid barriers between passes
 //   k_slice        barycentric gather back to the pixels and normalisation
-// Backward reuses the lattice: k_splat_bwd, k_blur in reverse axis order,
-// k_slice without normalisation.
+// Backward reuses the lattice: k_splat of grad * weight, k_blur_all in
+// reverse axis order, k_slice without normalisation.
 //
 // The float steps that decide the lattice keys (elevation, greedy rounding,
 // rank, barycentric weights) reproduce the reference's operation order,
@@ -32,9 +33,6 @@ namespace pl {
 
 // ---------------------------------------------------------------- constants
 
-constexpr uint32_t kBusy = 0xFFFFFFFFu;   // global cell being written
-constexpr int kSpinLimit = 1 << 20;       // bounded wait on a tile-local insert
-constexpr int kRoundLimit = 1 << 16;      // bounded insert rounds per CTA chunk
 
 template <int PD> struct Cfg {
     static constexpr int K = PD + 1;
@@ -65,6 +63,8 @@ struct LatView {
     int* tile_cnt;
     uint16_t* slot_lid;
     float* slot_w;
+    uint16_t* slot_order;
+    uint16_t* seg_off;
     int* staged_vid;
     int2* nbr;
     float* vb0;
@@ -73,8 +73,9 @@ struct LatView {
 
 struct ScrView {
     uint4* skeys;
-    float* svals;
-    uint4* table;
+    uint32_t* table;
+    int* owner;     // [U] staged index of the owner of each staged key
+    int* vid_of;    // [U] vertex id of each owner
     uint4* vkeys;
     float* vf0;
     float* vf1;
@@ -130,6 +131,23 @@ __device__ __forceinline__ void load_row(const float* __restrict__ p, float (&v)
     }
 }
 
+// load of CP consecutive floats through L2 only (data written in this launch)
+template <int CP>
+__device__ __forceinline__ void load_row_cg(const float* p, float (&v)[CP]) {
+    if constexpr (CP == 1) {
+        v[0] = __ldcg(p);
+    } else if constexpr (CP == 2) {
+        float2 a = __ldcg(reinterpret_cast<const float2*>(p));
+        v[0] = a.x; v[1] = a.y;
+    } else {
+#pragma unroll
+        for (int j = 0; j < CP; j += 4) {
+            float4 a = __ldcg(reinterpret_cast<const float4*>(p + j));
+            v[j] = a.x; v[j + 1] = a.y; v[j + 2] = a.z; v[j + 3] = a.w;
+        }
+    }
+}
+
 // store of CP consecutive floats with the widest aligned vector stores
 template <int CP>
 __device__ __forceinline__ void store_row(float* p, const float (&v)[CP]) {
@@ -153,12 +171,16 @@ __device__ __forceinline__ uint32_t fmix32(uint32_t h) {
     return h;
 }
 
-// hash of a key record's coordinate words (word 0 is the hash slot itself)
+// hash of a key record's coordinate words (word 0 is the hash slot itself):
+// multiply-xorshift per word, one final avalanche
 template <int NW>
 __device__ __forceinline__ uint32_t key_hash(const uint32_t (&kw)[NW]) {
     uint32_t h = 0x9E3779B9u;
 #pragma unroll
-    for (int k = 1; k < NW; ++k) h = fmix32(h ^ kw[k]) + 0x7F4A7C15u * (uint32_t)k;
+    for (int k = 1; k < NW; ++k) {
+        h = (h ^ kw[k]) * 0x85EBCA77u;
+        h ^= h >> 15;
+    }
     return fmix32(h);
 }
 
@@ -266,73 +288,92 @@ __device__ __forceinline__ void make_key(const int (&g)[PD + 1], const int (&ran
     kw[0] = key_hash<NW>(kw);
 }
 
-// ---------------------------------------------------------------- tile-local dedup
+// ---------------------------------------------------------------- warp helpers
 
-// Insert a key into the tile's shared-memory table; returns its local id.
-// Cells hold -1 (empty), -2 (being written) or a local id.  The owner of a
-// new key writes the record then publishes the id; other threads wait for
-// the publication with a bounded spin.
-template <int CW, int SC>
-__device__ __forceinline__ int tile_insert(int* stab, uint4* ukeys, const uint32_t (&kw)[4 * CW],
-                                           int* count, int* status) {
-    uint32_t pos = (kw[0] >> 7) & (SC - 1);
-    volatile int* vt = stab;
-    for (int probe = 0; probe < SC; ++probe) {
-        int cur = vt[pos];
-        if (cur == -1) {
-            cur = atomicCAS(&stab[pos], -1, -2);
-            if (cur == -1) {
-                const int lid = atomicAdd(count, 1);
+constexpr unsigned kFull = 0xffffffffu;
+
+// segmented inclusive sum along runs of lanes: lanes [start, lane] of the
+// caller's run; the last lane of a run ends with the run's total
+template <int NC>
+__device__ __forceinline__ void run_sum(float (&v)[NC], int start) {
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-                for (int w = 0; w < CW; ++w)
-                    ukeys[lid * CW + w] = make_uint4(kw[4 * w], kw[4 * w + 1], kw[4 * w + 2], kw[4 * w + 3]);
-                __threadfence_block();
-                atomicExch(&stab[pos], lid);
-                return lid;
-            }
-        }
-        int spins = 0;
-        while (cur == -2) {
-            if (++spins > kSpinLimit) { atomicOr(status, PL_ST_SPIN); return 0; }
-            cur = vt[pos];
-        }
-        __threadfence_block();
-        const volatile uint4* rec = ukeys + cur * CW;
-        bool eq = true;
+    for (int d = 1; d < 32; d <<= 1) {
 #pragma unroll
-        for (int w = 0; w < CW; ++w) {
-            const uint32_t a = rec[w].x, b = rec[w].y, c = rec[w].z, d = rec[w].w;
-            eq = eq && a == kw[4 * w] && b == kw[4 * w + 1] && c == kw[4 * w + 2] && d == kw[4 * w + 3];
+        for (int j = 0; j < NC; ++j) {
+            const float o = __shfl_up_sync(kFull, v[j], d);
+            if (lane - d >= start) v[j] = __fadd_rn(v[j], o);
         }
-        if (eq) return cur;
-        pos = (pos + 1) & (SC - 1);
     }
-    atomicOr(status, PL_ST_SMEM_PROBE);
-    return 0;
 }
 
-// ---------------------------------------------------------------- K1: tile build (+ forward splat)
+// ---------------------------------------------------------------- block scan
+
+// Exclusive prefix sum of a[0..n) in place by the P threads of the CTA, with
+// a[n] set to the total.  Contains barriers: every thread must call it.
+template <int P>
+__device__ __forceinline__ void block_scan_excl(int* a, int n, int* warp_tot) {
+    const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+    const int per = (n + P - 1) / P;
+    const int b = t * per, e = min(n, b + per);
+    int sum = 0;
+    for (int i = b; i < e; ++i) sum += a[i];
+    int x = sum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int y = __shfl_up_sync(kFull, x, d);
+        if (lane >= d) x += y;
+    }
+    if (lane == 31) warp_tot[wid] = x;
+    __syncthreads();
+    int run = x - sum;
+    for (int k = 0; k < wid; ++k) run += warp_tot[k];
+    for (int i = b; i < e; ++i) {
+        const int v = a[i];
+        a[i] = run;
+        run += v;
+    }
+    if (t == P - 1) {
+        int tot = 0;
+        for (int k = 0; k < P / 32; ++k) tot += warp_tot[k];
+        a[n] = tot;
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------- K1: tile build
 
 template <int PD>
 __host__ __device__ constexpr int tile_build_smem_bytes() {
-    return Cfg<PD>::SLOTS * Cfg<PD>::CW * 16 + Cfg<PD>::SC * 4;
+    return Cfg<PD>::SLOTS * Cfg<PD>::CW * 16 + Cfg<PD>::SC * 4 + Cfg<PD>::SLOTS * 2;
 }
 
-template <int PD, int V>
+// Per tile of P pixels (one thread per pixel):
+//  1. lattice embedding in registers;
+//  2. every slot (pixel, corner) writes its key record to shared memory; one
+//     lane per distinct key of the warp (equal hash, then checked word by word
+//     against the group leader) inserts the record's index into the tile hash
+//     table with a CAS -- the first index to land in a cell owns the key, later
+//     equal keys read the owner's record and take its index, so no cell is ever
+//     half-written and nobody waits;
+//  3. owners get compact local ids; the tile's unique keys are staged to HBM,
+//     the per-slot (local id, weight) records written, and the tile's rows
+//     [base, base + U) of the lattice value buffers zeroed (the union of all
+//     tiles' rows covers every vertex id, since ids are < the staged count).
+template <int PD>
 __global__ void __launch_bounds__(Cfg<PD>::P)
-k_tile_build(const float* __restrict__ feat, const float* __restrict__ vals, Geo geo, EmbedConsts ec,
-             LatView L, ScrView S) {
+k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L, ScrView S,
+             float* zero_f, int cpf, float* zero_b, int cpb) {
     using C = Cfg<PD>;
     constexpr int K = C::K, P = C::P, CW = C::CW, NW = C::NW, SLOTS = C::SLOTS, SC = C::SC;
-    constexpr int CPF = pad_ch(V + 1);
-    constexpr int REGION_FLOATS = tile_build_smem_bytes<PD>() / 4;
+    constexpr bool KEEP_KEYS = K * NW <= 32;   // keep key words in registers when small
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint4* ukeys = reinterpret_cast<uint4*>(smem_raw);
-    int* stab = reinterpret_cast<int*>(ukeys + SLOTS * CW);
-    float* part = reinterpret_cast<float*>(smem_raw);   // reused once the keys are staged
-    __shared__ int s_count, s_base;
+    uint4* ukeys = reinterpret_cast<uint4*>(smem_raw);                  // [SLOTS][CW]
+    int* stab = reinterpret_cast<int*>(ukeys + SLOTS * CW);             // [SC]
+    int16_t* cand_lid = reinterpret_cast<int16_t*>(stab + SC);          // [SLOTS]
+    __shared__ int s_count, s_base, s_wtot[P / 32];
 
-    const int t = threadIdx.x;
+    const int t = threadIdx.x, lane = t & 31;
     const int tile = blockIdx.x;
     const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
     const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
@@ -348,20 +389,80 @@ k_tile_build(const float* __restrict__ feat, const float* __restrict__ vals, Geo
     int g[K], rank[K];
     float bary[K];
     embed<PD>(f, ec, g, rank, bary);
-    __syncthreads();
 
-    int lid[K];
+    // 2a. candidate key records (visible to other lanes' CAS winners after the fence)
+    uint32_t keys[KEEP_KEYS ? K : 1][NW];
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        lid[c] = 0;
+        uint32_t kw[NW];
+        make_key<PD>(g, rank, c, kw);
         if (active) {
-            uint32_t kw[NW];
-            make_key<PD>(g, rank, c, kw);
-            lid[c] = tile_insert<CW, SC>(stab, ukeys, kw, &s_count, &L.hdr->status);
+#pragma unroll
+            for (int w = 0; w < CW; ++w)
+                ukeys[(t * K + c) * CW + w] = make_uint4(kw[4 * w], kw[4 * w + 1], kw[4 * w + 2], kw[4 * w + 3]);
+        }
+        if constexpr (KEEP_KEYS) {
+#pragma unroll
+            for (int k = 0; k < NW; ++k) keys[c][k] = kw[k];
         }
     }
+    __syncthreads();   // table initialised, records written
+
+    // 2b. one CAS per distinct key of the warp; the cell stores the owning candidate
+    const unsigned amask = __ballot_sync(kFull, active);
+    int mine[K];
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        const int cand = t * K + c;
+        uint32_t kw[NW];
+        if constexpr (KEEP_KEYS) {
+#pragma unroll
+            for (int k = 0; k < NW; ++k) kw[k] = keys[c][k];
+        } else {
+            make_key<PD>(g, rank, c, kw);
+        }
+        const unsigned grp = __match_any_sync(kFull, kw[0]) & amask;
+        const int leader = active ? __ffs(grp) - 1 : lane;
+        bool same = true;
+#pragma unroll
+        for (int k = 1; k < NW; ++k) same = (__shfl_sync(kFull, kw[k], leader) == kw[k]) && same;
+        int res = cand;
+        if (active && (lane == leader || !same)) {
+            uint32_t pos = (kw[0] >> 7) & (SC - 1);
+            int probe = 0;
+            for (; probe < SC; ++probe) {
+                const int cur = atomicCAS(&stab[pos], -1, cand);
+                if (cur == -1) break;
+                const uint4* rec = ukeys + cur * CW;
+                bool eq = true;
+#pragma unroll
+                for (int w = 0; w < CW; ++w) {
+                    const uint4 r = rec[w];
+                    eq = eq && r.x == kw[4 * w] && r.y == kw[4 * w + 1] && r.z == kw[4 * w + 2] && r.w == kw[4 * w + 3];
+                }
+                if (eq) {
+                    res = cur;
+                    break;
+                }
+                pos = (pos + 1) & (SC - 1);
+            }
+            if (probe == SC) atomicOr(&L.hdr->status, PL_ST_SMEM_PROBE);   // unreachable: table is 2x the slots
+        }
+        const int lres = __shfl_sync(kFull, res, leader);
+        mine[c] = (active && same) ? lres : res;
+    }
+    __syncthreads();
+
+    // 3. compact local ids for owners, staging, slot records, value rows
+#pragma unroll
+    for (int c = 0; c < K; ++c)
+        if (active && mine[c] == t * K + c) cand_lid[t * K + c] = (int16_t)atomicAdd(&s_count, 1);
     __syncthreads();
     const int U = s_count;
+    // the tile hash table is dead from here on: reuse it for the counting sort
+    int* cnt = stab;                                                     // [U + 1]
+    uint16_t* ord = reinterpret_cast<uint16_t*>(stab + SLOTS + 1);      // [SLOTS]
+    for (int i = t; i <= U; i += P) cnt[i] = 0;
     if (t == 0) {
         const int b = atomicAdd(&L.hdr->u_total, U);
         s_base = b;
@@ -370,57 +471,55 @@ k_tile_build(const float* __restrict__ feat, const float* __restrict__ vals, Geo
     }
     __syncthreads();
     const int base = s_base;
-    for (int i = t; i < U * CW; i += P) S.skeys[(size_t)base * CW + i] = ukeys[i];
-
     const size_t so = (size_t)tile * K * P + t;
+    int lid[K];
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        L.slot_lid[so + (size_t)c * P] = (uint16_t)lid[c];
+        const int l = active ? cand_lid[mine[c]] : 0;
+        lid[c] = l;
+        if (active && mine[c] == t * K + c) {
+#pragma unroll
+            for (int w = 0; w < CW; ++w)
+                S.skeys[(size_t)(base + l) * CW + w] = ukeys[(t * K + c) * CW + w];
+        }
+        L.slot_lid[so + (size_t)c * P] = (uint16_t)l;
         L.slot_w[so + (size_t)c * P] = active ? bary[c] : 0.0f;
     }
-    if (vals == nullptr) return;   // lattice rebuild only (block-uniform)
 
-    float v[V];
+    // 4. counting sort of the tile's slots by local id (integer shared
+    // atomics, one per distinct id of the warp), for the splat kernels
+    int rk[K];
 #pragma unroll
-    for (int j = 0; j < V; ++j) v[j] = active ? __ldg(vals + p * V + j) : 0.0f;
-    __syncthreads();   // staged keys read out of shared memory before it is reused
-    if (U * CPF <= REGION_FLOATS) {
-        for (int i = t; i < U * CPF; i += P) part[i] = 0.0f;
-        __syncthreads();
-        if (active) {
-#pragma unroll
-            for (int c = 0; c < K; ++c) {
-                float* pp = part + lid[c] * CPF;
-#pragma unroll
-                for (int j = 0; j < V; ++j) atomicAdd(pp + j, __fmul_rn(v[j], bary[c]));
-                atomicAdd(pp + V, bary[c]);
-            }
-        }
-        __syncthreads();
-        float* out = S.svals + (size_t)base * CPF;
-        for (int i = t; i < U * CPF; i += P) out[i] = part[i];
-    } else {
-        float* gp = S.svals + (size_t)base * CPF;
-        for (int i = t; i < U * CPF; i += P) gp[i] = 0.0f;
-        __syncthreads();
-        if (active) {
-#pragma unroll
-            for (int c = 0; c < K; ++c) {
-                float* pp = gp + lid[c] * CPF;
-#pragma unroll
-                for (int j = 0; j < V; ++j) atomicAdd(pp + j, __fmul_rn(v[j], bary[c]));
-                atomicAdd(pp + V, bary[c]);
-            }
-        }
+    for (int c = 0; c < K; ++c) {
+        const unsigned grp = __match_any_sync(kFull, active ? lid[c] : (1 << 20) + lane);
+        const int leader = __ffs(grp) - 1;
+        int b = 0;
+        if (active && lane == leader) b = atomicAdd(&cnt[lid[c]], __popc(grp));
+        b = __shfl_sync(kFull, b, leader);
+        rk[c] = b + __popc(grp & ((1u << lane) - 1u));
     }
+    __syncthreads();
+    block_scan_excl<P>(cnt, U, s_wtot);   // cnt[u] = first sorted position of id u, cnt[U] = total
+    if (active) {
+#pragma unroll
+        for (int c = 0; c < K; ++c) ord[cnt[lid[c]] + rk[c]] = (uint16_t)((t << 5) | c);
+    }
+    __syncthreads();
+    const int total = cnt[U];
+    uint16_t* gord = L.slot_order + (size_t)tile * SLOTS;
+    for (int i = t; i < total; i += P) gord[i] = ord[i];
+    for (int u = t; u < U; u += P) L.seg_off[base + u] = (uint16_t)cnt[u];
+    if (zero_f)
+        for (int i = t; i < U * cpf; i += P) zero_f[(size_t)base * cpf + i] = 0.0f;
+    for (int i = t; i < U * cpb; i += P) zero_b[(size_t)base * cpb + i] = 0.0f;
 }
 
 // ---------------------------------------------------------------- K_clear
 
-// Chooses the table capacity from the staged count (load <= 1/2), zeroes the
-// cells in use and the first u_total rows of the lattice value buffers that
-// are accumulated into (forward vf0 when cpf > 0, backward vb0).
-static __global__ void k_clear(Geo geo, LatView L, ScrView S, int cw, int cpf, int cpb) {
+// Chooses the table capacity from the staged count (load <= 1/2) and zeroes
+// the cells in use.  A cell is 0 (empty) or 1 + the staged index of the key
+// that owns it.
+static __global__ void k_clear(Geo geo, LatView L, ScrView S) {
     const int U = L.hdr->u_total;
     int lg = 6;
     while ((1ll << lg) < 2ll * U) ++lg;
@@ -429,22 +528,10 @@ static __global__ void k_clear(Geo geo, LatView L, ScrView S, int cw, int cpf, i
         lg = geo.cap_override_log2 < geo.cap_max_log2 ? geo.cap_override_log2 : geo.cap_max_log2;
     if (blockIdx.x == 0 && threadIdx.x == 0) L.hdr->cap_log2 = lg;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
-    const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const size_t cells = ((size_t)1 << lg) * cw;
+    const size_t n4 = ((size_t)1 << lg) / 4;
+    uint4* t4 = reinterpret_cast<uint4*>(S.table);
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-    for (size_t i = tid; i < cells; i += stride) S.table[i] = z;
-    if (cpf > 0) {
-        float4* a = reinterpret_cast<float4*>(S.vf0);
-        const size_t nf = (size_t)U * cpf;
-        for (size_t i = tid; i < nf / 4; i += stride) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (size_t i = (nf / 4) * 4 + tid; i < nf; i += stride) S.vf0[i] = 0.0f;
-    }
-    {
-        float4* a = reinterpret_cast<float4*>(L.vb0);
-        const size_t nb = (size_t)U * cpb;
-        for (size_t i = tid; i < nb / 4; i += stride) a[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (size_t i = (nb / 4) * 4 + tid; i < nb; i += stride) L.vb0[i] = 0.0f;
-    }
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) t4[i] = z;
 }
 
 // zero the first m rows of a lattice value buffer (a repeated backward)
@@ -454,35 +541,40 @@ static __global__ void k_zero_rows(float* buf, const LatticeHeader* hdr, int cp)
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) buf[i] = 0.0f;
 }
 
-// ---------------------------------------------------------------- global table lookups
+// ---------------------------------------------------------------- global table
 
 template <int CW>
-__device__ __forceinline__ bool cell_key_equal(const uint4* cell, const uint32_t (&kw)[4 * CW], uint4 c0) {
-    bool eq = c0.y == kw[1] && c0.z == kw[2] && c0.w == kw[3];
+__device__ __forceinline__ void load_key(const uint4* rec, uint32_t (&kw)[4 * CW]) {
 #pragma unroll
-    for (int w = 1; w < CW; ++w) {
-        const uint4 c = __ldcg(cell + w);
-        eq = eq && c.x == kw[4 * w] && c.y == kw[4 * w + 1] && c.z == kw[4 * w + 2] && c.w == kw[4 * w + 3];
+    for (int w = 0; w < CW; ++w) {
+        const uint4 r = __ldg(rec + w);
+        kw[4 * w] = r.x; kw[4 * w + 1] = r.y; kw[4 * w + 2] = r.z; kw[4 * w + 3] = r.w;
+    }
+}
+
+// 16-byte key compares against a staged record (word 0 is the hash: compared too)
+template <int CW>
+__device__ __forceinline__ bool key_equal(const uint4* rec, const uint32_t (&kw)[4 * CW]) {
+    bool eq = true;
+#pragma unroll
+    for (int w = 0; w < CW; ++w) {
+        const uint4 r = __ldg(rec + w);
+        eq = eq && r.x == kw[4 * w] && r.y == kw[4 * w + 1] && r.z == kw[4 * w + 2] && r.w == kw[4 * w + 3];
     }
     return eq;
 }
 
-// read-only probe after the table is complete; returns the vertex id or -1
+// Read-only lookup after the table is complete: the staged index of the
+// owner of kw, or -1 when kw is not a lattice vertex.
 template <int CW>
-__device__ __forceinline__ int table_find(const uint4* __restrict__ table, uint32_t mask,
-                                          const uint32_t (&kw)[4 * CW], int* status) {
+__device__ __forceinline__ int table_find(const uint32_t* __restrict__ table, uint32_t mask,
+                                          const uint4* __restrict__ skeys, const uint32_t (&kw)[4 * CW],
+                                          int* status) {
     uint32_t pos = kw[0] & mask;
     for (uint32_t probe = 0; probe <= mask; ++probe) {
-        const uint4* cell = table + (size_t)pos * CW;
-        const uint4 c0 = __ldg(cell);
-        if (c0.x == 0u) return -1;
-        bool eq = c0.y == kw[1] && c0.z == kw[2] && c0.w == kw[3];
-#pragma unroll
-        for (int w = 1; w < CW; ++w) {
-            const uint4 c = __ldg(cell + w);
-            eq = eq && c.x == kw[4 * w] && c.y == kw[4 * w + 1] && c.z == kw[4 * w + 2] && c.w == kw[4 * w + 3];
-        }
-        if (eq && c0.x != kBusy) return (int)c0.x - 1;
+        const uint32_t c = __ldg(table + pos);
+        if (c == 0u) return -1;
+        if (key_equal<CW>(skeys + (size_t)(c - 1) * CW, kw)) return (int)c - 1;
         pos = (pos + 1) & mask;
     }
     atomicOr(status, PL_ST_TABLE_FULL);
@@ -491,134 +583,113 @@ __device__ __forceinline__ int table_find(const uint4* __restrict__ table, uint3
 
 // ---------------------------------------------------------------- K2: global insert
 
-// One thread per staged key.  Each CTA works in rounds: every unresolved
-// thread probes without waiting (a cell being written by another thread ends
-// its probe for this round), winners of an empty cell get compact vertex ids
-// from one atomicAdd per CTA, write the vertex record and publish the cell.
-// Nobody spins, so every round ends and a published cell is seen next round.
-template <int PD, int CPF>
-__global__ void __launch_bounds__(256) k_insert(LatView L, ScrView S, int with_values) {
+// One thread per staged key.  The staged key records are complete before this
+// kernel starts, so a cell can name its owner the moment the owner's CAS lands:
+// a CAS of (1 + my staged index) into an empty cell makes me the owner; a
+// full cell names an owner whose record is compared word by word.  No cell is
+// ever half-written and nobody waits.
+template <int PD>
+__global__ void __launch_bounds__(256) k_insert(LatView L, ScrView S) {
     constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
-    __shared__ int s_nwin, s_vbase;
     const int U = L.hdr->u_total;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
-    if (threadIdx.x == 0) s_nwin = 0;
-    __syncthreads();
-    for (int base = blockIdx.x * blockDim.x; base < U; base += gridDim.x * blockDim.x) {
-        const int i = base + threadIdx.x;
-        bool pending = i < U, won = false;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < U; i += gridDim.x * blockDim.x) {
         uint32_t kw[NW];
-#pragma unroll
-        for (int k = 0; k < NW; ++k) kw[k] = 0u;
-        if (pending) {
-#pragma unroll
-            for (int w = 0; w < CW; ++w) {
-                const uint4 r = S.skeys[(size_t)i * CW + w];
-                kw[4 * w] = r.x; kw[4 * w + 1] = r.y; kw[4 * w + 2] = r.z; kw[4 * w + 3] = r.w;
-            }
+        load_key<CW>(S.skeys + (size_t)i * CW, kw);
+        uint32_t pos = kw[0] & mask;
+        int owner = -1;
+        for (uint32_t probe = 0; probe <= mask; ++probe) {
+            const uint32_t c = atomicCAS(S.table + pos, 0u, (uint32_t)i + 1u);
+            if (c == 0u) { owner = i; break; }
+            if (key_equal<CW>(S.skeys + (size_t)(c - 1) * CW, kw)) { owner = (int)c - 1; break; }
+            pos = (pos + 1) & mask;
         }
-        uint32_t pos = kw[0] & mask, probes = 0;
-        int vid = -1;
-        for (int round = 0;; ++round) {
-            if (pending && !won) {
-                for (;;) {
-                    uint4* cell = S.table + (size_t)pos * CW;
-                    uint32_t* state = reinterpret_cast<uint32_t*>(cell);
-                    uint32_t st = ld_acquire(state);
-                    if (st == 0u) {
-                        if (atomicCAS(state, 0u, kBusy) == 0u) {
-                            uint32_t* cw32 = reinterpret_cast<uint32_t*>(cell);
-#pragma unroll
-                            for (int k = 1; k < NW; ++k) cw32[k] = kw[k];
-                            won = true;
-                            break;
-                        }
-                        st = ld_acquire(state);   // lost the race: see who won, with acquire
-                        if (st == 0u) {           // cells never return to empty; stay bounded anyway
-                            if (++probes > mask) {
-                                atomicOr(&L.hdr->status, PL_ST_TABLE_FULL);
-                                pending = false;
-                                break;
-                            }
-                            continue;
-                        }
-                    }
-                    if (st == kBusy) break;   // written right now: look again next round
-                    const uint4 c0 = __ldcg(cell);
-                    if (cell_key_equal<CW>(cell, kw, c0)) {
-                        vid = (int)st - 1;
-                        pending = false;
-                        break;
-                    }
-                    pos = (pos + 1) & mask;
-                    if (++probes > mask) {
-                        atomicOr(&L.hdr->status, PL_ST_TABLE_FULL);
-                        pending = false;
-                        break;
-                    }
-                }
-            }
-            int local = 0;
-            if (won) local = atomicAdd(&s_nwin, 1);
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                const int nw = s_nwin;
-                s_vbase = nw ? atomicAdd(&L.hdr->m, nw) : 0;
-                s_nwin = 0;
-            }
-            __syncthreads();
-            if (won) {
-                vid = s_vbase + local;
-#pragma unroll
-                for (int w = 0; w < CW; ++w)
-                    S.vkeys[(size_t)vid * CW + w] = make_uint4(kw[4 * w], kw[4 * w + 1], kw[4 * w + 2], kw[4 * w + 3]);
-                __threadfence();
-                st_release(reinterpret_cast<uint32_t*>(S.table + (size_t)pos * CW), (uint32_t)vid + 1u);
-                won = false;
-                pending = false;
-            }
-            if (!__syncthreads_or(pending)) break;
-            if (round >= kRoundLimit) {
-                if (threadIdx.x == 0) atomicOr(&L.hdr->status, PL_ST_ROUNDS);
-                break;
-            }
-        }
-        if (i < U) {
-            L.staged_vid[i] = vid;
-            if (with_values && vid >= 0) {
-                float r[CPF];
-                const float* src = S.svals + (size_t)i * CPF;
-#pragma unroll
-                for (int j = 0; j < CPF; ++j) r[j] = __ldcg(src + j);
-                red_add_row<CPF>(S.vf0 + (size_t)vid * CPF, r);
-            }
-        }
+        if (owner < 0) atomicOr(&L.hdr->status, PL_ST_TABLE_FULL);
+        S.owner[i] = owner;
     }
 }
 
-// ---------------------------------------------------------------- K3: blur neighbours
+// Compact vertex ids for the owners (one atomicAdd per CTA and chunk); their
+// keys are copied to the vertex key array and their table cell is rewritten
+// to hold the vertex id (flag kVidCell set), so that later lookups read the
+// vertex id straight from the cell and compare against the vertex key.
+constexpr uint32_t kVidCell = 0x80000000u;
 
-// neighbour of key along axis c: every coordinate +1 (or -1), coordinate c
-// (when c < PD) additionally -K (or +K); permutohedral.cu:368-375.
+template <int PD>
+__global__ void __launch_bounds__(256) k_compact(LatView L, ScrView S) {
+    constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
+    __shared__ int s_wcnt[8], s_base;
+    const int U = L.hdr->u_total;
+    const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int i0 = blockIdx.x * blockDim.x; i0 < U; i0 += gridDim.x * blockDim.x) {   // block-uniform
+        const int i = i0 + threadIdx.x;
+        const bool own = i < U && S.owner[i] == i;
+        const unsigned m = __ballot_sync(kFull, own);
+        if (lane == 0) s_wcnt[wid] = __popc(m);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int tot = 0;
+            for (int k = 0; k < 8; ++k) { const int c = s_wcnt[k]; s_wcnt[k] = tot; tot += c; }
+            s_base = tot ? atomicAdd(&L.hdr->m, tot) : 0;
+        }
+        __syncthreads();
+        if (own) {
+            const int vid = s_base + s_wcnt[wid] + __popc(m & ((1u << lane) - 1u));
+            S.vid_of[i] = vid;
+            uint32_t kw[NW];
+            load_key<CW>(S.skeys + (size_t)i * CW, kw);
+#pragma unroll
+            for (int w = 0; w < CW; ++w)
+                S.vkeys[(size_t)vid * CW + w] = make_uint4(kw[4 * w], kw[4 * w + 1], kw[4 * w + 2], kw[4 * w + 3]);
+            // find my cell (it holds 1 + i) and store the vertex id there
+            uint32_t pos = kw[0] & mask;
+            for (uint32_t probe = 0; probe <= mask; ++probe) {
+                if (S.table[pos] == (uint32_t)i + 1u) {
+                    S.table[pos] = kVidCell | (uint32_t)vid;
+                    break;
+                }
+                pos = (pos + 1) & mask;
+            }
+        }
+        __syncthreads();   // s_wcnt / s_base reused by the next chunk
+    }
+}
+
+// Blur neighbours of every vertex: for axis c < PD the step is every
+// coordinate +1 (or -1) and coordinate c -K (or +K), for c == PD every
+// coordinate +1 (or -1) (permutohedral.cu:368-375).  One lookup pair per
+// (vertex, axis); the table cells hold vertex ids after k_compact.
+template <int CW>
+__device__ __forceinline__ int table_find_vid(const uint32_t* __restrict__ table, uint32_t mask,
+                                              const uint4* __restrict__ vkeys, const uint32_t (&kw)[4 * CW],
+                                              int* status) {
+    uint32_t pos = kw[0] & mask;
+    for (uint32_t probe = 0; probe <= mask; ++probe) {
+        const uint32_t c = __ldg(table + pos);
+        if (c == 0u) return -1;
+        const int vid = (int)(c & ~kVidCell);
+        if ((c & kVidCell) && key_equal<CW>(vkeys + (size_t)vid * CW, kw)) return vid;
+        pos = (pos + 1) & mask;
+    }
+    atomicOr(status, PL_ST_TABLE_FULL);
+    return -1;
+}
+
 template <int PD>
 __global__ void __launch_bounds__(256) k_neighbors(LatView L, ScrView S) {
     constexpr int K = PD + 1, CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
     const int M = L.hdr->m;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
     const size_t total = (size_t)M * K;
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (size_t)gridDim.x * blockDim.x) {
         const int c = (int)(idx / M);
         const int v = (int)(idx - (size_t)c * M);
         uint32_t kp[NW], km[NW];
-#pragma unroll
-        for (int w = 0; w < CW; ++w) {
-            const uint4 r = __ldg(S.vkeys + (size_t)v * CW + w);
-            kp[4 * w] = r.x; kp[4 * w + 1] = r.y; kp[4 * w + 2] = r.z; kp[4 * w + 3] = r.w;
-        }
+        load_key<CW>(S.vkeys + (size_t)v * CW, kp);
 #pragma unroll
         for (int k = 1; k < NW; ++k) {
-            // +1 on the halfwords that hold coordinates, 0 on padding
             const int lo = 2 * (k - 1), hi = lo + 1;
             const uint32_t ones = (lo < PD ? 0x0001u : 0u) | (hi < PD ? 0x00010000u : 0u);
             uint32_t step = 0u;
@@ -629,38 +700,234 @@ __global__ void __launch_bounds__(256) k_neighbors(LatView L, ScrView S) {
         }
         kp[0] = key_hash<NW>(kp);
         km[0] = key_hash<NW>(km);
-        const int a = table_find<CW>(S.table, mask, kp, &L.hdr->status);
-        const int b = table_find<CW>(S.table, mask, km, &L.hdr->status);
+        const int a = table_find_vid<CW>(S.table, mask, S.vkeys, kp, &L.hdr->status);
+        const int b = table_find_vid<CW>(S.table, mask, S.vkeys, km, &L.hdr->status);
         L.nbr[(size_t)c * M + v] = make_int2(a, b);
     }
 }
 
-// ---------------------------------------------------------------- blur
+// ---------------------------------------------------------------- splat
 
-// out[v] = (2 in[v] + in[n+] + in[n-]) / 4 along one axis; a missing neighbour
-// adds nothing (permutohedral.cu:341-347).
-template <int CP>
-__global__ void __launch_bounds__(256) k_blur(const float* __restrict__ in, float* __restrict__ out,
-                                              const int2* __restrict__ nbr, const LatticeHeader* hdr,
-                                              int axis, int nch) {
-    const int M = hdr->m;
-    const int2* nb = nbr + (size_t)axis * M;
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t v = (size_t)blockIdx.x * blockDim.x + threadIdx.x; v < (size_t)M; v += stride) {
-        const int2 n = __ldg(nb + v);
-        float me[CP], a[CP], b[CP];
-        load_row<CP>(in + v * CP, me);
-        if (n.x >= 0) load_row<CP>(in + (size_t)n.x * CP, a);
-        if (n.y >= 0) load_row<CP>(in + (size_t)n.y * CP, b);
-        float r[CP];
+// FWD: [v*w, w] per slot (permutohedral.cu:286-293); otherwise
+// (grad * weight_in) * w (permutohedral.cu:437-445).
+//
+// The tile's slots were counting-sorted by local vertex when the lattice was
+// built, so every local vertex owns a contiguous segment of the sorted order.
+// Thread t sums the K sorted positions [t*K, t*K + K): segments that start and
+// end inside them are added to the lattice at once; the segment the thread
+// ends in is carried across lanes by a segmented warp scan and added by the
+// lane where it ends; the segment it starts in picks up the previous lanes'
+// carry.  About one vector red.global.add per tile vertex, no shared-memory
+// float atomics; the float reduction of a vertex across tiles happens in L2.
+template <int CP, int NC>
+__device__ __forceinline__ void red_run(float* lat, int vid, const float (&s)[NC]) {
+    float r[CP];
 #pragma unroll
-        for (int j = 0; j < CP; ++j) {
-            float acc = __fmul_rn(2.0f, me[j]);
-            if (n.x >= 0) acc = __fadd_rn(acc, a[j]);
-            if (n.y >= 0) acc = __fadd_rn(acc, b[j]);
-            r[j] = __fmul_rn(0.25f, acc);
+    for (int j = 0; j < CP; ++j) r[j] = j < NC ? s[j] : 0.0f;
+    red_add_row<CP>(lat + (size_t)vid * CP, r);
+}
+
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(Cfg<PD>::P)
+k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, ScrView S,
+        int resolve, float* lat) {
+    using C = Cfg<PD>;
+    constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
+    constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
+    constexpr int NC = FWD ? V + 1 : V;
+    __shared__ __align__(16) uint16_t ord[SLOTS];
+    __shared__ __align__(16) float ws[SLOTS];   // [K][P] slot weights, pixel-major
+    __shared__ int seg[SLOTS + 1];
+    __shared__ int svid[SLOTS];
+    __shared__ float pv[P * NC];                 // per-pixel values
+    const int t = threadIdx.x, lane = t & 31, tile = blockIdx.x;
+    if (tile == 0 && t == 0) L.hdr->bar_count = 0u;   // grid barrier of the blur that follows
+    const int x0 = (tile % geo.tiles_x) * C::TW, y0 = (tile / geo.tiles_x) * C::TH;
+    const int nx = min(C::TW, geo.w - x0), ny = min(C::TH, geo.h - y0);
+    const int total = nx * ny * K;
+    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
+    {   // this pixel's values
+        const int x = x0 + (t % C::TW), y = y0 + (t / C::TW);
+        const bool active = x < geo.w && y < geo.h;
+        const size_t p = (size_t)y * geo.w + x;
+        float wp = 1.0f;
+        if constexpr (!FWD) wp = active ? __ldg(wt + p) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const float v = active ? __ldg(vals + p * V + j) : 0.0f;
+            pv[t * NC + j] = FWD ? v : __fmul_rn(v, wp);
         }
-        store_row<CP>(out + v * CP, r);
+        if constexpr (FWD) pv[t * NC + V] = 1.0f;
+    }
+    {   // the tile's sorted order and pixel-major weights (16-byte loads)
+        const uint4* go = reinterpret_cast<const uint4*>(L.slot_order + (size_t)tile * SLOTS);
+        const float4* gw = reinterpret_cast<const float4*>(L.slot_w + (size_t)tile * SLOTS);
+#pragma unroll
+        for (int i = t; i < SLOTS / 8; i += P) reinterpret_cast<uint4*>(ord)[i] = __ldg(go + i);
+#pragma unroll
+        for (int i = t; i < SLOTS / 4; i += P) reinterpret_cast<float4*>(ws)[i] = __ldg(gw + i);
+    }
+    // vertex ids of the tile's keys; the call right after a build resolves
+    // them through the owners and stores them for the kernels that follow
+    for (int u = t; u < cnt; u += P) {
+        seg[u] = L.seg_off[off + u];
+        int vid;
+        if (resolve) {
+            const int o = S.owner[off + u];
+            vid = o >= 0 ? S.vid_of[o] : -1;
+            L.staged_vid[off + u] = vid;
+        } else {
+            vid = L.staged_vid[off + u];
+        }
+        svid[u] = vid;
+    }
+    if (t == 0) seg[cnt] = total;
+    __syncthreads();
+
+    // my sorted positions [q0, q1); l = local id of position q0
+    const int q0 = t * K, q1 = min(total, q0 + K);
+    int l = -1;
+    if (q0 < total) {
+        int lo = 0, hi = cnt - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (seg[mid] <= q0) lo = mid; else hi = mid - 1;
+        }
+        l = lo;
+    }
+    const int F = l;
+    int next = (l >= 0) ? seg[l + 1] : 0x7fffffff;
+    float cur[NC], first[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) cur[j] = first[j] = 0.0f;
+    bool multi = false;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int q = q0 + k;
+        if (q < q1) {
+            if (q == next) {   // a new segment starts at q
+                if (!multi) {
+#pragma unroll
+                    for (int j = 0; j < NC; ++j) first[j] = cur[j];
+                    multi = true;
+                } else if (svid[l] >= 0) {
+                    red_run<CP, NC>(lat, svid[l], cur);   // segment inside my positions: complete
+                }
+                ++l;
+                next = seg[l + 1];
+#pragma unroll
+                for (int j = 0; j < NC; ++j) cur[j] = 0.0f;
+            }
+            const int s = ord[q];
+            const int px = s >> 5, c = s & 31;
+            const float w = ws[c * P + px];
+#pragma unroll
+            for (int j = 0; j < NC; ++j)
+                cur[j] = __fadd_rn(cur[j], (FWD && j == V) ? w : __fmul_rn(pv[px * NC + j], w));
+        }
+    }
+    // carry the last segment across lanes
+    const unsigned below = 0xffffffffu >> (31 - lane);
+    const int prevLast = __shfl_up_sync(kFull, l, 1);
+    const bool cont = lane > 0 && F >= 0 && F == prevLast;   // my first segment continues the previous lane's
+    const unsigned heads = __ballot_sync(kFull, multi || !cont);
+    const int start = 31 - __clz(heads & below);
+    run_sum<NC>(cur, start);
+    float prevY[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) prevY[j] = __shfl_up_sync(kFull, cur[j], 1);
+    const bool nextCont = __shfl_down_sync(kFull, cont ? 1 : 0, 1) != 0;
+    if (multi && F >= 0 && svid[F] >= 0) {
+        if (cont) {
+#pragma unroll
+            for (int j = 0; j < NC; ++j) first[j] = __fadd_rn(first[j], prevY[j]);
+        }
+        red_run<CP, NC>(lat, svid[F], first);
+    }
+    if ((lane == 31 || !nextCont) && l >= 0 && svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
+}
+
+// ---------------------------------------------------------------- fused neighbours + blur
+
+// Grid barrier over the CTAs of a cooperative launch (all co-resident): one
+// release-add per CTA on a counter that only grows during the launch (it is
+// zeroed by the kernel before), then acquire polls until all CTAs of this
+// phase have arrived.  The wait is bounded: a CTA that polls kBarrierSpin
+// times records PL_ST_SPIN and continues, so a failure shows in the status
+// word instead of a hang.
+constexpr int kBarrierSpin = 1 << 22;
+
+__device__ __forceinline__ unsigned atom_add_release(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase) {
+    __syncthreads();
+    ++phase;
+    if (threadIdx.x == 0) {
+        const unsigned target = phase * gridDim.x;
+        atom_add_release(&hdr->bar_count, 1u);
+        int spins = 0;
+        while (ld_acquire(&hdr->bar_count) < target) {
+            if (++spins > kBarrierSpin) {
+                atomicOr(&hdr->status, PL_ST_SPIN);
+                break;
+            }
+            if (spins > 4096) __nanosleep(32);
+        }
+    }
+    __syncthreads();
+}
+
+// The K blur passes, axis order 0..PD or PD..0, ping-ponging buf0 <-> buf1;
+// the result ends in buf0 when K is even, else in buf1.  One cooperative
+// launch: grid barriers separate the passes; every read of data written
+// inside this launch goes to L2 (ld.global.cg), never to a stale L1 line.
+// Each thread fetches its neighbour pairs of the next pass before the
+// barrier (they do not depend on the values).
+template <int PD, int CP>
+__global__ void __launch_bounds__(256) k_blur_all(LatView L, float* buf0, float* buf1, int reverse) {
+    constexpr int K = PD + 1;
+    constexpr int VPT = 4;   // vertices per thread and pass held in flight
+    const int M = L.hdr->m;
+    const int stride = gridDim.x * blockDim.x;
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+    unsigned phase = 0;
+    float* x = buf0;
+    float* y = buf1;
+    for (int s = 0; s < K; ++s) {
+        const int axis = reverse ? K - 1 - s : s;
+        const int2* nb = L.nbr + (size_t)axis * M;
+        for (int v0 = tid; v0 < M; v0 += stride * VPT) {
+            int2 n[VPT];
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int v = v0 + k * stride;
+                n[k] = v < M ? __ldg(nb + v) : make_int2(-1, -1);
+            }
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int v = v0 + k * stride;
+                if (v >= M) continue;
+                float me[CP], a[CP], b[CP];
+                load_row_cg<CP>(x + (size_t)v * CP, me);
+                if (n[k].x >= 0) load_row_cg<CP>(x + (size_t)n[k].x * CP, a);
+                if (n[k].y >= 0) load_row_cg<CP>(x + (size_t)n[k].y * CP, b);
+                float r[CP];
+#pragma unroll
+                for (int j = 0; j < CP; ++j) {
+                    float acc = __fmul_rn(2.0f, me[j]);
+                    if (n[k].x >= 0) acc = __fadd_rn(acc, a[j]);
+                    if (n[k].y >= 0) acc = __fadd_rn(acc, b[j]);
+                    r[j] = __fmul_rn(0.25f, acc);
+                }
+                store_row<CP>(y + (size_t)v * CP, r);
+            }
+        }
+        if (s + 1 < K) grid_barrier(L.hdr, phase);
+        float* t = x; x = y; y = t;
     }
 }
 
@@ -678,27 +945,34 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
     constexpr int NC = FWD ? V + 1 : V;
     __shared__ int svid[SLOTS];
     const int t = threadIdx.x, tile = blockIdx.x;
+    const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
+    const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
+    const bool active = x < geo.w && y < geo.h;
+    const size_t so = (size_t)tile * K * P + t;
+    // slot records first, so that their loads overlap the vertex-list load
+    int lid[K];
+    float w[K];
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        lid[c] = active ? (int)L.slot_lid[so + (size_t)c * P] : 0;
+        w[c] = active ? L.slot_w[so + (size_t)c * P] : 0.0f;
+    }
     const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
     for (int u = t; u < cnt; u += P) svid[u] = L.staged_vid[off + u];
     __syncthreads();
-    const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
-    const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
-    if (x >= geo.w || y >= geo.h) return;
+    if (!active) return;
     const size_t p = (size_t)y * geo.w + x;
-    const size_t so = (size_t)tile * K * P + t;
     float acc[NC];
 #pragma unroll
     for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        const int lid = L.slot_lid[so + (size_t)c * P];
-        const float w = L.slot_w[so + (size_t)c * P];
-        const int vid = svid[lid];
+        const int vid = svid[lid[c]];
         if (vid < 0) continue;   // failed insert (reported in the status word)
         float r[CP];
         load_row<CP>(lat + (size_t)vid * CP, r);
 #pragma unroll
-        for (int j = 0; j < NC; ++j) acc[j] = __fmaf_rn(w, r[j], acc[j]);
+        for (int j = 0; j < NC; ++j) acc[j] = __fmaf_rn(w[c], r[j], acc[j]);
     }
     if constexpr (FWD) {
         const float inv = 1.0f / acc[V];
@@ -708,66 +982,6 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
     } else {
 #pragma unroll
         for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
-    }
-}
-
-// ---------------------------------------------------------------- backward splat
-
-// value (grad * weight_in) * w per slot (permutohedral.cu:437-445), summed per
-// tile-unique vertex in shared memory, then one vector red per vertex.
-template <int PD, int V>
-__host__ __device__ constexpr int bsplat_part_floats() {
-    return Cfg<PD>::SLOTS * pad_ch(V) <= 8192 ? Cfg<PD>::SLOTS * pad_ch(V) : 8192;
-}
-
-template <int PD, int V>
-__global__ void __launch_bounds__(Cfg<PD>::P)
-k_splat_bwd(const float* __restrict__ grad, const float* __restrict__ wt, Geo geo, LatView L, float* vb) {
-    using C = Cfg<PD>;
-    constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
-    constexpr int CP = pad_ch(V);
-    constexpr int PF = bsplat_part_floats<PD, V>();
-    __shared__ int svid[SLOTS];
-    __shared__ __align__(16) float part[PF];
-    const int t = threadIdx.x, tile = blockIdx.x;
-    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
-    const bool in_smem = cnt * CP <= PF;
-    for (int u = t; u < cnt; u += P) svid[u] = L.staged_vid[off + u];
-    if (in_smem)
-        for (int i = t; i < cnt * CP; i += P) part[i] = 0.0f;
-    __syncthreads();
-    const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
-    const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
-    if (x < geo.w && y < geo.h) {
-        const size_t p = (size_t)y * geo.w + x;
-        const float wp = __ldg(wt + p);
-        float gw[V];
-#pragma unroll
-        for (int j = 0; j < V; ++j) gw[j] = __fmul_rn(__ldg(grad + p * V + j), wp);
-        const size_t so = (size_t)tile * K * P + t;
-#pragma unroll
-        for (int c = 0; c < K; ++c) {
-            const int lid = L.slot_lid[so + (size_t)c * P];
-            const float w = L.slot_w[so + (size_t)c * P];
-            if (in_smem) {
-                float* pp = part + lid * CP;
-#pragma unroll
-                for (int j = 0; j < V; ++j) atomicAdd(pp + j, __fmul_rn(gw[j], w));
-            } else if (svid[lid] >= 0) {
-                float* gp = vb + (size_t)svid[lid] * CP;
-#pragma unroll
-                for (int j = 0; j < V; ++j) red_add_f32(gp + j, __fmul_rn(gw[j], w));
-            }
-        }
-    }
-    if (!in_smem) return;
-    __syncthreads();
-    for (int u = t; u < cnt; u += P) {
-        if (svid[u] < 0) continue;
-        float r[CP];
-#pragma unroll
-        for (int j = 0; j < CP; ++j) r[j] = part[u * CP + j];
-        red_add_row<CP>(vb + (size_t)svid[u] * CP, r);
     }
 }
 

@@ -11,13 +11,18 @@
 //   tile_off/cnt   per tile: offset and length of its unique-vertex list
 //   slot_lid       [tile][K][P] uint16   local id of each (pixel, simplex corner)
 //   slot_w         [tile][K][P] float    barycentric weight of the same slot
+//   slot_order     [tile][K*P]  uint16   the tile's slots sorted by local id,
+//                                        (pixel << 5) | corner
+//   seg_off        [U]          uint16   first sorted position of each local id
 //   staged_vid     [U]          int32    global vertex id of each staged key
 //   nbr            [K][m]       int2     blur neighbours (+, -) per axis, -1 absent
 //   vb0, vb1       [m][CPb]     float    backward lattice values (ping-pong)
 // Scratch blob (forward build only):
 //   staged_keys    [U][CW]      uint4    each tile's unique keys (word 0: hash)
-//   staged_vals    [U][CPf]     float    each tile's partial splat sums
-//   table          [cap][CW]    uint4    open-addressed hash table, word 0 = state
+//   table          [cap]        uint32   open-addressed hash table: 0 empty, else
+//                                        1 + staged index of the owning key
+//   owner          [U]          int32    staged index of the owner of each staged key
+//   vid_of         [U]          int32    vertex id of each owner
 //   vkeys          [m][CW]      uint4    key of every vertex
 //   vf0, vf1       [m][CPf]     float    forward lattice values (ping-pong)
 // U, m <= slots = tiles*K*P: buffers are sized for that bound, but every kernel
@@ -32,7 +37,7 @@
 // status bits (LatticeHeader::status)
 #define PL_ST_SMEM_PROBE 1   /* tile-local table exhausted (cannot happen: sized 2x) */
 #define PL_ST_TABLE_FULL 2   /* global hash table probe limit reached */
-#define PL_ST_SPIN 4         /* a bounded wait on a tile-local insert gave up */
+#define PL_ST_SPIN 4         /* a bounded wait (tile-local insert, grid barrier) gave up */
 #define PL_ST_ROUNDS 8       /* global insert did not settle within the round limit */
 
 typedef struct {
@@ -41,7 +46,8 @@ typedef struct {
     int u_total;     /* staged (tile-unique) keys */
     int cap_log2;    /* hash table capacity in use (log2 of cells) */
     int n, pd, vd, tiles;
-    int pad[56];     /* header is 256 bytes */
+    unsigned bar_count, bar_gen;   /* grid barrier of the cooperative blur kernel */
+    int pad[54];     /* header is 256 bytes */
 } LatticeHeader;
 
 static inline int pl_tile_pixels(int pd) { return pd <= 6 ? 256 : (pd <= 10 ? 128 : 64); }
@@ -54,9 +60,9 @@ typedef struct {
     int CW, CPf, CPb;
     long long slots;      /* tiles*K*P: bound on staged keys and on vertices */
     int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
-    size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_staged_vid, off_nbr,
-        off_vb0, off_vb1, lattice_bytes;
-    size_t off_skeys, off_svals, off_table, off_vkeys, off_vf0, off_vf1, scratch_bytes;
+    size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_seg_off,
+        off_staged_vid, off_nbr, off_vb0, off_vb1, lattice_bytes;
+    size_t off_skeys, off_table, off_owner, off_vid_of, off_vkeys, off_vf0, off_vf1, scratch_bytes;
 } PlLayout;
 
 static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
@@ -79,6 +85,8 @@ static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
     L->off_tile_cnt = o;   o = pl_align(o + T * 4);
     L->off_slot_lid = o;   o = pl_align(o + S * 2);
     L->off_slot_w = o;     o = pl_align(o + S * 4);
+    L->off_slot_order = o; o = pl_align(o + S * 2);
+    L->off_seg_off = o;    o = pl_align(o + S * 2);
     L->off_staged_vid = o; o = pl_align(o + S * 4);
     L->off_nbr = o;        o = pl_align(o + S * L->K * 8);
     L->off_vb0 = o;        o = pl_align(o + S * L->CPb * 4);
@@ -86,8 +94,9 @@ static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
     L->lattice_bytes = o;
     o = 0;
     L->off_skeys = o;      o = pl_align(o + S * L->CW * 16);
-    L->off_svals = o;      o = pl_align(o + S * L->CPf * 4);
-    L->off_table = o;      o = pl_align(o + ((size_t)1 << lg) * L->CW * 16);
+    L->off_table = o;      o = pl_align(o + ((size_t)1 << lg) * 4);
+    L->off_owner = o;      o = pl_align(o + S * 4);
+    L->off_vid_of = o;     o = pl_align(o + S * 4);
     L->off_vkeys = o;      o = pl_align(o + S * L->CW * 16);
     L->off_vf0 = o;        o = pl_align(o + S * L->CPf * 4);
     L->off_vf1 = o;        o = pl_align(o + S * L->CPf * 4);

@@ -7,16 +7,17 @@
 namespace pl {
 
 enum Stage {
-    STAGE_TILE_BUILD = 0,  // fwd: lattice embedding + tile dedup + splat partial sums
-    STAGE_CLEAR,           // fwd: hash table / value buffer clear
-    STAGE_INSERT,          // fwd: global insert + splat reduction
-    STAGE_NEIGHBORS,       // fwd: blur neighbour resolution
-    STAGE_BLUR_FWD,        // fwd: one blur pass
+    STAGE_TILE_BUILD = 0,  // build: lattice embedding + tile dedup + staging
+    STAGE_CLEAR,           // build: hash table clear
+    STAGE_INSERT,          // build: global insert + vertex id compaction
+    STAGE_NEIGHBORS,       // build: blur neighbour resolution
+    STAGE_BLUR_FWD,        // fwd: the blur passes
     STAGE_SLICE_FWD,       // fwd: normalised slice
     STAGE_ZERO,            // bwd: re-zero of the value buffer (repeated backward)
     STAGE_SPLAT_BWD,       // bwd: splat of grad * weight
-    STAGE_BLUR_BWD,        // bwd: one blur pass
+    STAGE_BLUR_BWD,        // bwd: the blur passes
     STAGE_SLICE_BWD,       // bwd: slice
+    STAGE_SPLAT_FWD,       // fwd: splat of [v*w, w]
     STAGE_COUNT
 };
 
