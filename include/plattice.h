@@ -104,6 +104,22 @@ int plattice_vertex_keys(const void* lattice, const void* scratch, int pd, int v
  * build report PLATTICE_DEV_TABLE_FULL instead of looping. */
 void plattice_debug_set_table_cap_log2(int log2_cells);
 
+/* Forward filter for callers that cannot allocate device memory (no
+ * counterpart in the reference, whose host layer allocates a new workspace on
+ * every call).  Same computation and outputs as plattice_forward, but the
+ * lattice and scratch buffers live in one fixed 64 MiB array inside the
+ * library (plattice_noalloc_capacity() bytes), held on every GPU that loads
+ * the library until the process exits; the call allocates nothing.  An image
+ * whose workspace exceeds the array returns PLATTICE_ERR_WORKSPACE
+ * (plattice_noalloc_error_detail() says how much it needs).  The first call
+ * on each device looks up the array's device address: make it before any
+ * stream capture.  All calls on a device share the array, so calls that
+ * overlap on the GPU race: issue them one after the other. */
+int plattice_forward_noalloc(float* weight_out, float* out, const float* values, const float* features,
+                             int pd, int vd, int w, int h, void* stream);
+size_t plattice_noalloc_capacity(void);
+const char* plattice_noalloc_error_detail(void);
+
 /* Profiling (no reference counterpart): when enabled, every kernel launch is
  * bracketed by CUDA events recorded on its stream.  plattice_profile_read
  * waits for the recorded events, writes per stage the summed milliseconds and
