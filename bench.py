@@ -78,18 +78,13 @@ def dist_init(world, local):
 
 
 def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
+    from plattice_pytorch_b200.sharding import barrier as _barrier
+    _barrier(world)
 
 
 def max_over_ranks(x, world):
-    if world <= 1:
-        return x
-    import torch.distributed as dist
-    t = torch.tensor([float(x)], device="cuda", dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return t.item()
+    from plattice_pytorch_b200.sharding import max_over_ranks as _max
+    return _max(x, world, device="cuda")
 
 
 # ---------------------------------------------------------------- clocks

@@ -1,0 +1,114 @@
+"""Host-side checks that need no GPU: the C ABI library loads and exports every
+function include/plattice.h declares, its argument checks, the Python layer's
+input checks (the reference's messages), and the multi-rank plumbing over gloo."""
+import ctypes
+import os
+import re
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "plattice.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(plattice_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from plattice_pytorch_b200 import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        pytest.skip("libplattice_b200.so not built (python -m plattice_pytorch_b200.build)")
+    return _lib.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = _declared_functions()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_abi_version_and_error_strings(lib):
+    from plattice_pytorch_b200 import _lib
+    assert lib.plattice_abi_version() == _lib.ABI_VERSION
+    for code in range(5):
+        assert _lib.error_string(code)
+
+
+def test_workspace_sizes_and_argument_checks(lib):
+    from plattice_pytorch_b200 import _lib
+    lb, sb = _lib.workspace_sizes(1024, 1024, 5, 3)
+    assert lb > 1024 * 1024 * 6 * 6 and sb > 0
+    lb0, sb0 = _lib.workspace_sizes(0, 7, 5, 3)
+    assert lb0 == 256 and sb0 == 256
+    for pd, vd in [(0, 3), (17, 3), (5, 0), (5, 9)]:
+        with pytest.raises(_lib.PlatticeError):
+            _lib.workspace_sizes(8, 8, pd, vd)
+    # invalid dimensions are refused before anything touches a device
+    S = ctypes.c_size_t
+    lib.plattice_forward.argtypes = [ctypes.c_void_p] * 5 + [S, ctypes.c_void_p, S] + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    assert lib.plattice_forward(None, None, None, None, None, 0, None, 0, 0, 3, 8, 8, None) == _lib.ERR_INVALID
+    assert lib.plattice_forward(None, None, None, None, None, 0, None, 0, 5, 3, 8, 8, None) == _lib.ERR_INVALID
+
+
+def test_python_checks_raise_reference_messages():
+    from plattice_pytorch_b200 import PLOO
+    f = torch.zeros(4, 4, 5)
+    v = torch.zeros(4, 4, 3)
+    with pytest.raises(RuntimeError, match="features must be CUDA"):
+        PLOO.forward(f, v)
+    with pytest.raises(RuntimeError, match="features must be CUDA"):
+        PLOO.backward(f, v, torch.zeros(4, 4, 1))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, q):
+    import torch.distributed as dist
+    from plattice_pytorch_b200.sharding import barrier, max_over_ranks, shard_range
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        start, stop = shard_range(64, world, rank)
+        barrier(world)
+        mx = max_over_ranks(10.0 + rank, world)
+        q.put((rank, start, stop, mx))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_image_sharding_over_two_gloo_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [(r[1], r[2]) for r in res] == [(0, 32), (32, 64)]
+    assert all(r[3] == 11.0 for r in res)
+
+
+def test_shard_range_partitions_any_batch():
+    from plattice_pytorch_b200.sharding import shard_range
+    for n in (0, 1, 7, 64, 65):
+        for world in (1, 2, 3, 8):
+            parts = [shard_range(n, world, r) for r in range(world)]
+            assert parts[0][0] == 0 and parts[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+            assert max(p[1] - p[0] for p in parts) - min(p[1] - p[0] for p in parts) <= 1
