@@ -33,6 +33,7 @@ inline LatView lat_view(void* base, const PlLayout& L) {
     v.slot_lid = reinterpret_cast<uint16_t*>(b + L.off_slot_lid);
     v.slot_w = reinterpret_cast<float*>(b + L.off_slot_w);
     v.slot_order = reinterpret_cast<uint16_t*>(b + L.off_slot_order);
+    v.slot_wsort = reinterpret_cast<float*>(b + L.off_slot_wsort);
     v.seg_off = reinterpret_cast<uint16_t*>(b + L.off_seg_off);
     v.staged_vid = reinterpret_cast<int*>(b + L.off_staged_vid);
     v.nbr = reinterpret_cast<int2*>(b + L.off_nbr);
@@ -115,7 +116,7 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
 
 // Cooperative launch of the fused neighbour + blur kernel on as many CTAs as
 // are co-resident (at most kCoopPerSm per SM).
-constexpr int kCoopPerSm = 2;
+constexpr int kCoopPerSm = 1;
 
 template <int PD, int CP>
 cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1, int reverse) {
@@ -125,7 +126,7 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     if (e != cudaSuccess) return e;
     int n = (dev >= 0 && dev < 64) ? per_sm[dev] : 0;
     if (n == 0) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_blur_all<PD, CP>, 256, 0);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_blur_all<PD, CP>, kBlurThreads, 0);
         if (e != cudaSuccess) return e;
         if (n < 1) return cudaErrorLaunchOutOfResources;
         if (dev >= 0 && dev < 64) per_sm[dev] = n;
@@ -133,7 +134,7 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
     void* args[] = {&Lv, &b0, &b1, &reverse};
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
-              e = cudaLaunchCooperativeKernel((const void*)k_blur_all<PD, CP>, dim3(blocks), dim3(256), args, 0,
+              e = cudaLaunchCooperativeKernel((const void*)k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), args, 0,
                                               a.stream));
     return e;
 }
@@ -154,7 +155,7 @@ cudaError_t forward_v(const CallArgs& a) {
     if (e != cudaSuccess) return e;
     float* x = ((PD + 1) % 2 == 0) ? Sv.vf0 : Sv.vf1;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
-              k_slice<PD, V, true><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.out, a.wout, geo, Lv, x));
+              k_slice<PD, V, true><<<a.lay.tiles, Cfg<PD>::P / kSlicePix, 0, a.stream>>>(a.out, a.wout, geo, Lv, x));
     return cudaGetLastError();
 }
 
@@ -180,7 +181,7 @@ cudaError_t backward_v(const CallArgs& a) {
     if (e != cudaSuccess) return e;
     float* x = ((PD + 1) % 2 == 0) ? Lv.vb0 : Lv.vb1;
     PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
-              k_slice<PD, V, false><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.out, nullptr, geo, Lv, x));
+              k_slice<PD, V, false><<<a.lay.tiles, Cfg<PD>::P / kSlicePix, 0, a.stream>>>(a.out, nullptr, geo, Lv, x));
     return cudaGetLastError();
 }
 

@@ -64,6 +64,7 @@ struct LatView {
     uint16_t* slot_lid;
     float* slot_w;
     uint16_t* slot_order;
+    float* slot_wsort;
     uint16_t* seg_off;
     int* staged_vid;
     int2* nbr;
@@ -500,14 +501,23 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     }
     __syncthreads();
     block_scan_excl<P>(cnt, U, s_wtot);   // cnt[u] = first sorted position of id u, cnt[U] = total
+    float* wsort = reinterpret_cast<float*>(ukeys);   // key records are staged: reuse their space
     if (active) {
 #pragma unroll
-        for (int c = 0; c < K; ++c) ord[cnt[lid[c]] + rk[c]] = (uint16_t)((t << 5) | c);
+        for (int c = 0; c < K; ++c) {
+            const int pos = cnt[lid[c]] + rk[c];
+            ord[pos] = (uint16_t)((t << 5) | c);
+            wsort[pos] = bary[c];
+        }
     }
     __syncthreads();
     const int total = cnt[U];
     uint16_t* gord = L.slot_order + (size_t)tile * SLOTS;
-    for (int i = t; i < total; i += P) gord[i] = ord[i];
+    float* gws = L.slot_wsort + (size_t)tile * SLOTS;
+    for (int i = t; i < total; i += P) {
+        gord[i] = ord[i];
+        gws[i] = wsort[i];
+    }
     for (int u = t; u < U; u += P) L.seg_off[base + u] = (uint16_t)cnt[u];
     if (zero_f)
         for (int i = t; i < U * cpf; i += P) zero_f[(size_t)base * cpf + i] = 0.0f;
@@ -735,38 +745,60 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
     constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
-    __shared__ __align__(16) uint16_t ord[SLOTS];
-    __shared__ __align__(16) float ws[SLOTS];   // [K][P] slot weights, pixel-major
+    constexpr int NV4 = (NC + 3) / 4;            // float4 per pixel value row
     __shared__ int seg[SLOTS + 1];
     __shared__ int svid[SLOTS];
-    __shared__ float pv[P * NC];                 // per-pixel values
+    __shared__ float4 pv[P * NV4];               // per-pixel values, padded to float4
     const int t = threadIdx.x, lane = t & 31, tile = blockIdx.x;
     if (tile == 0 && t == 0) L.hdr->bar_count = 0u;   // grid barrier of the blur that follows
     const int x0 = (tile % geo.tiles_x) * C::TW, y0 = (tile / geo.tiles_x) * C::TH;
     const int nx = min(C::TW, geo.w - x0), ny = min(C::TH, geo.h - y0);
     const int total = nx * ny * K;
-    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
+    // my K sorted positions: slot codes and weights straight into registers
+    const int q0 = t * K;
+    int code[K];
+    float wq[K];
+    {
+        const uint16_t* go = L.slot_order + (size_t)tile * SLOTS + q0;
+        const float* gw = L.slot_wsort + (size_t)tile * SLOTS + q0;
+        if constexpr (K % 2 == 0) {
+            // K even: the K codes are K/2 aligned 32-bit words, the weights K/2 float2
+#pragma unroll
+            for (int k = 0; k < K; k += 2) {
+                const uint32_t two = __ldg(reinterpret_cast<const uint32_t*>(go + k));
+                const float2 ww = __ldg(reinterpret_cast<const float2*>(gw + k));
+                code[k] = (int)(two & 0xffffu);
+                code[k + 1] = (int)(two >> 16);
+                wq[k] = ww.x;
+                wq[k + 1] = ww.y;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                code[k] = (int)__ldg(go + k);
+                wq[k] = __ldg(gw + k);
+            }
+        }
+    }
     {   // this pixel's values
         const int x = x0 + (t % C::TW), y = y0 + (t / C::TW);
         const bool active = x < geo.w && y < geo.h;
         const size_t p = (size_t)y * geo.w + x;
         float wp = 1.0f;
         if constexpr (!FWD) wp = active ? __ldg(wt + p) : 0.0f;
+        float r[4 * NV4];
+#pragma unroll
+        for (int j = 0; j < 4 * NV4; ++j) r[j] = 0.0f;
 #pragma unroll
         for (int j = 0; j < V; ++j) {
             const float v = active ? __ldg(vals + p * V + j) : 0.0f;
-            pv[t * NC + j] = FWD ? v : __fmul_rn(v, wp);
+            r[j] = FWD ? v : __fmul_rn(v, wp);
         }
-        if constexpr (FWD) pv[t * NC + V] = 1.0f;
-    }
-    {   // the tile's sorted order and pixel-major weights (16-byte loads)
-        const uint4* go = reinterpret_cast<const uint4*>(L.slot_order + (size_t)tile * SLOTS);
-        const float4* gw = reinterpret_cast<const float4*>(L.slot_w + (size_t)tile * SLOTS);
+        if constexpr (FWD) r[V] = 1.0f;
 #pragma unroll
-        for (int i = t; i < SLOTS / 8; i += P) reinterpret_cast<uint4*>(ord)[i] = __ldg(go + i);
-#pragma unroll
-        for (int i = t; i < SLOTS / 4; i += P) reinterpret_cast<float4*>(ws)[i] = __ldg(gw + i);
+        for (int k = 0; k < NV4; ++k) pv[t * NV4 + k] = make_float4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
     }
+    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
     // vertex ids of the tile's keys; the call right after a build resolves
     // them through the owners and stores them for the kernels that follow
     for (int u = t; u < cnt; u += P) {
@@ -784,8 +816,8 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
     if (t == 0) seg[cnt] = total;
     __syncthreads();
 
-    // my sorted positions [q0, q1); l = local id of position q0
-    const int q0 = t * K, q1 = min(total, q0 + K);
+    // local id of position q0
+    const int q1 = min(total, q0 + K);
     int l = -1;
     if (q0 < total) {
         int lo = 0, hi = cnt - 1;
@@ -818,12 +850,16 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
 #pragma unroll
                 for (int j = 0; j < NC; ++j) cur[j] = 0.0f;
             }
-            const int s = ord[q];
-            const int px = s >> 5, c = s & 31;
-            const float w = ws[c * P + px];
+            const int px = code[k] >> 5;
+            const float w = wq[k];
+            float r[4 * NV4];
 #pragma unroll
-            for (int j = 0; j < NC; ++j)
-                cur[j] = __fadd_rn(cur[j], (FWD && j == V) ? w : __fmul_rn(pv[px * NC + j], w));
+            for (int m = 0; m < NV4; ++m) {
+                const float4 a = pv[px * NV4 + m];
+                r[4 * m] = a.x; r[4 * m + 1] = a.y; r[4 * m + 2] = a.z; r[4 * m + 3] = a.w;
+            }
+#pragma unroll
+            for (int j = 0; j < NC; ++j) cur[j] = __fadd_rn(cur[j], (FWD && j == V) ? w : __fmul_rn(r[j], w));
         }
     }
     // carry the last segment across lanes
@@ -887,10 +923,12 @@ __device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase
 // inside this launch goes to L2 (ld.global.cg), never to a stale L1 line.
 // Each thread fetches its neighbour pairs of the next pass before the
 // barrier (they do not depend on the values).
+constexpr int kBlurThreads = 1024;
+
 template <int PD, int CP>
-__global__ void __launch_bounds__(256) k_blur_all(LatView L, float* buf0, float* buf1, int reverse) {
+__global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse) {
     constexpr int K = PD + 1;
-    constexpr int VPT = 4;   // vertices per thread and pass held in flight
+    constexpr int VPT = 2;   // vertices per thread and pass held in flight
     const int M = L.hdr->m;
     const int stride = gridDim.x * blockDim.x;
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
@@ -936,52 +974,67 @@ __global__ void __launch_bounds__(256) k_blur_all(LatView L, float* buf0, float*
 // FWD: out = sum_i w_i val_i[0:V] / sum_i w_i val_i[V], weight_out = 1/sum;
 // otherwise the unnormalised gather of V channels (permutohedral.cu:401-413,
 // 487-496).
+constexpr int kSlicePix = 1;   // pixels per thread in k_slice
+
 template <int PD, int V, bool FWD>
-__global__ void __launch_bounds__(Cfg<PD>::P)
+__global__ void __launch_bounds__(Cfg<PD>::P / kSlicePix)
 k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat) {
     using C = Cfg<PD>;
-    constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
+    constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS, R = kSlicePix, T = P / R;
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
     __shared__ int svid[SLOTS];
     const int t = threadIdx.x, tile = blockIdx.x;
-    const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
-    const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
-    const bool active = x < geo.w && y < geo.h;
-    const size_t so = (size_t)tile * K * P + t;
-    // slot records first, so that their loads overlap the vertex-list load
-    int lid[K];
-    float w[K];
+    const int x0 = (tile % geo.tiles_x) * C::TW, y0 = (tile / geo.tiles_x) * C::TH;
+    // pixels t and t + T of the tile; all slot loads issued before any use
+    bool act[R];
+    int lid[R][K];
+    float w[R][K];
 #pragma unroll
-    for (int c = 0; c < K; ++c) {
-        lid[c] = active ? (int)L.slot_lid[so + (size_t)c * P] : 0;
-        w[c] = active ? L.slot_w[so + (size_t)c * P] : 0.0f;
+    for (int r = 0; r < R; ++r) {
+        const int pi = t + r * T;
+        act[r] = x0 + (pi % C::TW) < geo.w && y0 + (pi / C::TW) < geo.h;
+        const size_t so = (size_t)tile * K * P + pi;
+#pragma unroll
+        for (int c = 0; c < K; ++c) {
+            lid[r][c] = act[r] ? (int)L.slot_lid[so + (size_t)c * P] : 0;
+            w[r][c] = act[r] ? L.slot_w[so + (size_t)c * P] : 0.0f;
+        }
     }
     const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
-    for (int u = t; u < cnt; u += P) svid[u] = L.staged_vid[off + u];
+    for (int u = t; u < cnt; u += T) svid[u] = L.staged_vid[off + u];
     __syncthreads();
-    if (!active) return;
-    const size_t p = (size_t)y * geo.w + x;
-    float acc[NC];
+    float acc[R][NC];
 #pragma unroll
-    for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int j = 0; j < NC; ++j) acc[r][j] = 0.0f;
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        const int vid = svid[lid[c]];
-        if (vid < 0) continue;   // failed insert (reported in the status word)
-        float r[CP];
-        load_row<CP>(lat + (size_t)vid * CP, r);
 #pragma unroll
-        for (int j = 0; j < NC; ++j) acc[j] = __fmaf_rn(w[c], r[j], acc[j]);
+        for (int r = 0; r < R; ++r) {
+            const int vid = act[r] ? svid[lid[r][c]] : -1;
+            if (vid < 0) continue;   // inactive pixel, or failed insert (reported in the status word)
+            float rw[CP];
+            load_row<CP>(lat + (size_t)vid * CP, rw);
+#pragma unroll
+            for (int j = 0; j < NC; ++j) acc[r][j] = __fmaf_rn(w[r][c], rw[j], acc[r][j]);
+        }
     }
-    if constexpr (FWD) {
-        const float inv = 1.0f / acc[V];
 #pragma unroll
-        for (int j = 0; j < V; ++j) out[p * V + j] = acc[j] * inv;
-        wout[p] = inv;
-    } else {
+    for (int r = 0; r < R; ++r) {
+        if (!act[r]) continue;
+        const int pi = t + r * T;
+        const size_t p = (size_t)(y0 + pi / C::TW) * geo.w + x0 + (pi % C::TW);
+        if constexpr (FWD) {
+            const float inv = 1.0f / acc[r][V];
 #pragma unroll
-        for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
+            for (int j = 0; j < V; ++j) out[p * V + j] = acc[r][j] * inv;
+            wout[p] = inv;
+        } else {
+#pragma unroll
+            for (int j = 0; j < V; ++j) out[p * V + j] = acc[r][j];
+        }
     }
 }
 
