@@ -24,6 +24,48 @@ PL_DECLARE_PD(13) PL_DECLARE_PD(14) PL_DECLARE_PD(15) PL_DECLARE_PD(16)
 
 static int g_cap_override_log2 = 0;
 
+// ---------------------------------------------------------------- side stream
+
+namespace {
+struct DeviceSide {
+    std::mutex mu;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+DeviceSide g_side[64];
+}  // namespace
+
+namespace pl {
+cudaError_t side_fork(cudaStream_t main, SideFork* f) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    DeviceSide& d = g_side[dev];
+    d.mu.lock();
+    if (!d.stream) {
+        e = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d.join, cudaEventDisableTiming);
+        if (e != cudaSuccess) { d.mu.unlock(); return e; }
+    }
+    e = cudaEventRecord(d.fork, main);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(d.stream, d.fork, 0);
+    if (e != cudaSuccess) { d.mu.unlock(); return e; }
+    f->side = d.stream;
+    f->token = &d;
+    return cudaSuccess;
+}
+
+cudaError_t side_join(cudaStream_t main, SideFork* f) {
+    DeviceSide& d = *static_cast<DeviceSide*>(f->token);
+    cudaError_t e = cudaEventRecord(d.join, d.stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, d.join, 0);
+    d.mu.unlock();
+    return e;
+}
+}  // namespace pl
+
 // ---------------------------------------------------------------- profiling
 
 namespace {

@@ -92,8 +92,8 @@ cudaError_t prepare_tile_build() {
 }
 
 // Build the lattice: tile dedup (which also zeroes the lattice value rows),
-// table clear, global insert.  Blur neighbours are resolved by the first
-// phase of k_blur_all.
+// table clear, global insert, vertex ids.  Blur neighbours follow, alongside
+// the first splat (neighbors_alongside).
 template <int PD>
 cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
                           float* zero_f, int cpf, float* zero_b, int cpb) {
@@ -110,8 +110,30 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     PL_LAUNCH(STAGE_CLEAR, s, k_clear<<<grid, 256, 0, s>>>(geo, Lv, Sv));
     PL_LAUNCH(STAGE_INSERT, s, k_insert<PD><<<grid * 2, 256, 0, s>>>(Lv, Sv));
     PL_LAUNCH(STAGE_INSERT, s, k_compact<PD><<<grid, 256, 0, s>>>(Lv, Sv));
-    PL_LAUNCH(STAGE_NEIGHBORS, s, k_neighbors<PD><<<grid, 256, 0, s>>>(Lv, Sv));
     return cudaGetLastError();
+}
+
+// Side stream of the current device, forked from and joined back into the
+// caller's stream with events, so that independent kernels overlap (defined
+// in plattice_capi.cu; the fork is held by one host thread at a time).
+struct SideFork {
+    cudaStream_t side;
+    void* token;
+};
+cudaError_t side_fork(cudaStream_t main, SideFork* f);
+cudaError_t side_join(cudaStream_t main, SideFork* f);
+
+// Blur neighbours on the side stream while `main_work` runs on the caller's stream.
+template <int PD, typename MainWork>
+cudaError_t neighbors_alongside(const CallArgs& a, const LatView& Lv, const ScrView& Sv, MainWork main_work) {
+    SideFork f;
+    cudaError_t e = side_fork(a.stream, &f);
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_NEIGHBORS, f.side, k_neighbors<PD><<<a.sm_count * 8, 256, 0, f.side>>>(Lv, Sv));
+    main_work();
+    const cudaError_t e1 = cudaGetLastError();
+    e = side_join(a.stream, &f);
+    return e1 != cudaSuccess ? e1 : e;
 }
 
 // Cooperative launch of the fused neighbour + blur kernel on as many CTAs as
@@ -147,9 +169,13 @@ cudaError_t forward_v(const CallArgs& a) {
     const ScrView Sv = scr_view(a.scratch, a.lay);
     cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, Sv.vf0, CPF, Lv.vb0, CPB);
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
-              k_splat<PD, V, true><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.values, nullptr, geo, Lv, Sv, 1,
-                                                                             Sv.vf0));
+    // neighbour lookups (L2-latency-bound) overlap the splat (HBM-bound)
+    e = neighbors_alongside<PD>(a, Lv, Sv, [&] {
+        PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
+                  k_splat<PD, V, true><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.values, nullptr, geo, Lv, Sv, 1,
+                                                                                 Sv.vf0));
+    });
+    if (e != cudaSuccess) return e;
     // blur in axis order 0..pd (permutohedral.cu:585)
     e = launch_blur_all<PD, CPF>(a, Lv, Sv.vf0, Sv.vf1, 0);
     if (e != cudaSuccess) return e;
@@ -167,15 +193,21 @@ cudaError_t backward_v(const CallArgs& a) {
     const ScrView Sv = scr_view(a.scratch, a.lay);
     const int grid = a.sm_count * 8;
     cudaError_t e = cudaSuccess;
+    auto splat = [&] {
+        PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
+                  k_splat<PD, V, false><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(
+                      a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, Lv.vb0));
+    };
     if (a.lattice_state == 0) {
         e = build_lattice<PD>(a, geo, Lv, Sv, nullptr, 0, Lv.vb0, CPB);
         if (e != cudaSuccess) return e;
-    } else if (a.lattice_state == 2) {
-        PL_LAUNCH(STAGE_ZERO, a.stream, k_zero_rows<<<grid, 256, 0, a.stream>>>(Lv.vb0, Lv.hdr, CPB));
+        e = neighbors_alongside<PD>(a, Lv, Sv, splat);
+        if (e != cudaSuccess) return e;
+    } else {
+        if (a.lattice_state == 2)
+            PL_LAUNCH(STAGE_ZERO, a.stream, k_zero_rows<<<grid, 256, 0, a.stream>>>(Lv.vb0, Lv.hdr, CPB));
+        splat();
     }
-    PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
-              k_splat<PD, V, false><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(
-                  a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, Lv.vb0));
     // blur in axis order pd..0 (permutohedral.cu:647)
     e = launch_blur_all<PD, CPB>(a, Lv, Lv.vb0, Lv.vb1, 1);
     if (e != cudaSuccess) return e;

@@ -1,18 +1,20 @@
 // plattice_kernels.cuh -- sm_100a kernels of the permutohedral-lattice filter.
 //
-// Pipeline of one forward call (all on one stream, no host synchronisation):
+// Pipeline of one forward call (no host synchronisation):
 //   k_tile_build   per tile of P pixels: lattice embedding in registers; the
 //                  tile's distinct vertex keys deduplicated in a shared-memory
-//                  hash table (16-bit local ids); unique keys staged to HBM
+//                  hash table (16-bit local ids); unique keys staged to HBM;
+//                  the tile's slots counting-sorted by local id
 //   k_clear        zero the part of the global hash table this call uses
-//   k_insert       global open-addressed insert of the staged keys, compact
-//                  vertex ids allocated per CTA
-//   k_splat        per tile: [v*w, w] summed over runs of equal vertex along
-//                  each warp (one row of 32 pixels), one vector red.global.add
-//                  per run into the lattice values
-//   k_blur_all     blur neighbours resolved once, then the pd+1 passes of the
-//                  [1 2 1]/4 stencil over the compact vertex list: one
-//                  cooperative launch with grid barriers between passes
+//   k_insert       global open-addressed insert of the staged keys
+//   k_compact      compact vertex ids for the owners (one atomic per CTA chunk)
+//   k_neighbors    blur neighbours of every vertex by table lookup; runs on a
+//                  side stream, overlapped with the splat
+//   k_splat        per tile: [v*w, w] summed over the sorted segments of equal
+//                  vertex, one vector red.global.add per segment
+//   k_blur_all     the pd+1 passes of the [1 2 1]/4 stencil over the compact
+//                  vertex list: one cooperative launch with grid barriers
+//                  between passes
 //   k_slice        barycentric gather back to the pixels and normalisation
 // Backward reuses the lattice: k_splat of grad * weight, k_blur_all in
 // reverse axis order, k_slice without normalisation.
@@ -699,7 +701,9 @@ __global__ void __launch_bounds__(256) k_neighbors(LatView L, ScrView S) {
         uint32_t kp[NW], km[NW];
         load_key<CW>(S.vkeys + (size_t)v * CW, kp);
 #pragma unroll
-        for (int k = 1; k < NW; ++k) {
+        for (int k = 0; k < NW; ++k) km[k] = kp[k];   // padding words are copied as they are (0)
+#pragma unroll
+        for (int k = 1; k <= 1 + (PD - 1) / 2; ++k) {   // the words that hold coordinates
             const int lo = 2 * (k - 1), hi = lo + 1;
             const uint32_t ones = (lo < PD ? 0x0001u : 0u) | (hi < PD ? 0x00010000u : 0u);
             uint32_t step = 0u;

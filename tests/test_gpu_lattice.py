@@ -1,0 +1,178 @@
+"""Invariants of the lattice the sm_100a build leaves in its buffers.
+
+The parity tests compare what the filter returns; these read the lattice and
+scratch buffers of one forward call back to the host and check the structure
+every later kernel relies on, for every feature dimension:
+  * every vertex key record has its padding halfwords zero and word 0 equal to
+    the hash of words 1.. (lookups compare whole records, so a record that
+    decodes to the right coordinates but differs anywhere else is not found);
+  * every (pixel, simplex corner) slot resolves to the vertex whose key the
+    oracle's embedding gives (permutohedral.cu:238-244), with the same weight;
+  * each tile's slots, counting-sorted by local vertex id, cover the tile's
+    active slots exactly once, segment by segment;
+  * the blur neighbour table holds, per axis and direction, the vertex whose
+    key is the step of permutohedral.cu:368-375 away, or -1 where there is none.
+The buffer layout is restated here and checked against the library's own
+workspace sizes, so that a change of layout fails loudly instead of being
+misread.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import GOLDEN, golden_files
+
+pytestmark = pytest.mark.gpu
+
+
+def _align(x):
+    return (x + 255) & ~255
+
+
+def _pad_ch(c):
+    return c if c <= 2 else ((c + 3) // 4) * 4
+
+
+def _layout(h, w, pd, vd):
+    K = pd + 1
+    P = 256 if pd <= 6 else (128 if pd <= 10 else 64)
+    TH = P // 32
+    tx = (w + 31) // 32
+    T = tx * ((h + TH - 1) // TH)
+    CW = (4 + 2 * pd + 15) // 16
+    CPf, CPb = _pad_ch(vd + 1), _pad_ch(vd)
+    S = T * K * P
+    lg = 6
+    while (1 << lg) < 2 * S:
+        lg += 1
+    lat, o = {}, _align(256)
+    for name, sz in [("tile_off", T * 4), ("tile_cnt", T * 4), ("slot_lid", S * 2), ("slot_w", S * 4),
+                     ("slot_order", S * 2), ("slot_wsort", S * 4), ("seg_off", S * 2), ("staged_vid", S * 4),
+                     ("nbr", S * K * 8), ("vb0", S * CPb * 4), ("vb1", S * CPb * 4)]:
+        lat[name] = o
+        o = _align(o + sz)
+    lat_bytes, scr, o = o, {}, 0
+    for name, sz in [("skeys", S * CW * 16), ("table", (1 << lg) * 4), ("owner", S * 4), ("vid_of", S * 4),
+                     ("vkeys", S * CW * 16), ("vf0", S * CPf * 4), ("vf1", S * CPf * 4)]:
+        scr[name] = o
+        o = _align(o + sz)
+    return lat, scr, dict(K=K, P=P, TH=TH, tx=tx, T=T, CW=CW, S=S, lat_bytes=lat_bytes, scr_bytes=o)
+
+
+def _view(buf, off, n, dt):
+    return buf[off:off + n * np.dtype(dt).itemsize].view(dt)
+
+
+def _key_hash(words):
+    """Hash of key records [n][NW] (word 0 excluded), as the device computes it."""
+    m32 = np.uint64(0xFFFFFFFF)
+    h = np.full(words.shape[0], 0x9E3779B9, np.uint64)
+    for k in range(1, words.shape[1]):
+        h = ((h ^ words[:, k].astype(np.uint64)) * np.uint64(0x85EBCA77)) & m32
+        h ^= h >> np.uint64(15)
+    h ^= h >> np.uint64(16)
+    h = (h * np.uint64(0x85EBCA6B)) & m32
+    h ^= h >> np.uint64(13)
+    h = (h * np.uint64(0xC2B2AE35)) & m32
+    h ^= h >> np.uint64(16)
+    return h.astype(np.uint32)
+
+
+def _decode(words, pd):
+    """int16 coordinates [n][pd] and the OR of the padding halfwords [n]."""
+    half = np.stack([(words[:, 1:] >> np.uint32(16 * s)) & np.uint32(0xFFFF) for s in (0, 1)], axis=2)
+    half = half.reshape(words.shape[0], -1)
+    return half[:, :pd].astype(np.uint16).view(np.int16), np.bitwise_or.reduce(half[:, pd:], axis=1)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    from plattice_pytorch_b200 import _lib
+    _lib.lib()
+    return torch.device("cuda:0")
+
+
+CASES = [f for f in golden_files() if f.startswith("ref_randn24x20_")] + ["ref_ragged13x29_pd5_vd3.npz"]
+
+
+@pytest.mark.parametrize("fn", CASES)
+def test_lattice_invariants(fn, dev):
+    from plattice_pytorch_b200 import PLOO, _lib
+    d = np.load(os.path.join(GOLDEN, fn))
+    f, v = d["features"], d["values"]
+    h, w, pd = f.shape
+    vd = v.shape[2]
+    lat_off, scr_off, g = _layout(h, w, pd, vd)
+    assert (g["lat_bytes"], g["scr_bytes"]) == tuple(_lib.workspace_sizes(h, w, pd, vd))
+    K, P, TH, tx, T, CW, S = (g[k] for k in ("K", "P", "TH", "tx", "T", "CW", "S"))
+
+    _, _, lat = PLOO.lattice_forward(torch.from_numpy(f).to(dev), torch.from_numpy(v).to(dev), keep_scratch=True)
+    torch.cuda.synchronize()
+    lb, sb = lat.buf.cpu().numpy(), lat.scratch.cpu().numpy()
+    hdr = lb[:256].view(np.int32)
+    assert hdr[0] == 0
+    M, U = int(hdr[1]), int(hdr[2])
+
+    # key records: padding zero, hash consistent, all distinct
+    for name, n in (("vkeys", M), ("skeys", U)):
+        words = _view(sb, scr_off[name], n * CW * 4, np.uint32).reshape(n, CW * 4)
+        coords, padding = _decode(words, pd)
+        assert not padding.any(), (name, int(np.count_nonzero(padding)))
+        assert np.array_equal(words[:, 0], _key_hash(words)), name
+    vk, _ =_decode(_view(sb, scr_off["vkeys"], M * CW * 4, np.uint32).reshape(M, CW * 4), pd)
+    assert len({r.tobytes() for r in vk}) == M
+    vid_of_key = {r.tobytes(): i for i, r in enumerate(vk)}
+
+    # slots against the oracle's embedding
+    tile_off = _view(lb, lat_off["tile_off"], T, np.int32)
+    tile_cnt = _view(lb, lat_off["tile_cnt"], T, np.int32)
+    slot_lid = _view(lb, lat_off["slot_lid"], S, np.uint16).reshape(T, K, P)
+    slot_w = _view(lb, lat_off["slot_w"], S, np.float32).reshape(T, K, P)
+    order = _view(lb, lat_off["slot_order"], S, np.uint16).reshape(T, K * P)
+    wsort = _view(lb, lat_off["slot_wsort"], S, np.float32).reshape(T, K * P)
+    seg_off = _view(lb, lat_off["seg_off"], S, np.uint16)
+    staged_vid = _view(lb, lat_off["staged_vid"], S, np.int32)
+    okeys, ow = oracle.embed(f)
+    okeys = okeys.reshape(h * w, K, pd)
+    ow = ow.reshape(h * w, K)
+    assert int(tile_cnt.sum()) == U
+    for tile in range(T):
+        ts = np.arange(P)
+        xs = (tile % tx) * 32 + ts % 32
+        ys = (tile // tx) * TH + ts // 32
+        act = ts[(xs < w) & (ys < h)]
+        base, cnt = int(tile_off[tile]), int(tile_cnt[tile])
+        for t in act:
+            p = int(ys[t]) * w + int(xs[t])
+            for c in range(K):
+                lid = int(slot_lid[tile, c, t])
+                assert lid < cnt
+                assert staged_vid[base + lid] == vid_of_key[okeys[p, c].tobytes()], (tile, t, c)
+                assert slot_w[tile, c, t].view(np.uint32) == ow[p, c].view(np.uint32), (tile, t, c)
+        total = len(act) * K
+        segs = np.append(seg_off[base:base + cnt].astype(np.int64), total)
+        assert np.all(np.diff(segs) > 0)
+        seen = set()
+        for u in range(cnt):
+            for pos in range(segs[u], segs[u + 1]):
+                t, c = int(order[tile, pos]) >> 5, int(order[tile, pos]) & 31
+                assert slot_lid[tile, c, t] == u and (t, c) not in seen
+                assert wsort[tile, pos].view(np.uint32) == slot_w[tile, c, t].view(np.uint32)
+                seen.add((t, c))
+        assert len(seen) == total
+
+    # blur neighbours
+    nbr = _view(lb, lat_off["nbr"], M * K * 2, np.int32).reshape(K, M, 2)
+    for c in range(K):
+        step = np.ones(pd, np.int32)
+        if c < pd:
+            step[c] -= K
+        for col, sgn in ((0, 1), (1, -1)):
+            nk = (vk.astype(np.int32) + sgn * step).astype(np.int16)
+            expect = np.array([vid_of_key.get(r.tobytes(), -1) for r in nk], np.int32)
+            assert np.array_equal(nbr[c, :, col], expect), (c, sgn, int(np.count_nonzero(nbr[c, :, col] != expect)))
