@@ -72,6 +72,8 @@ inline Geo make_geo(const CallArgs& a) {
     g.h = a.lay.h; g.w = a.lay.w; g.tiles_x = a.lay.tiles_x; g.tiles = a.lay.tiles;
     g.cap_max_log2 = a.lay.cap_max_log2;
     g.cap_override_log2 = a.cap_override_log2;
+    g.idx_bits = 1;
+    while (g.idx_bits < 32 && (1ll << g.idx_bits) <= a.lay.slots) ++g.idx_bits;   // 1 + index <= slots
     return g;
 }
 
@@ -108,8 +110,7 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     PL_LAUNCH(STAGE_TILE_BUILD, s, k_tile_build<PD><<<a.lay.tiles, C::P, tile_build_smem_bytes<PD>(), s>>>(
         a.features, geo, ec, Lv, Sv, zero_f, cpf, zero_b, cpb));
     PL_LAUNCH(STAGE_CLEAR, s, k_clear<<<grid, 256, 0, s>>>(geo, Lv, Sv));
-    PL_LAUNCH(STAGE_INSERT, s, k_insert<PD><<<grid * 2, 256, 0, s>>>(Lv, Sv));
-    PL_LAUNCH(STAGE_INSERT, s, k_compact<PD><<<grid, 256, 0, s>>>(Lv, Sv));
+    PL_LAUNCH(STAGE_INSERT, s, k_insert<PD><<<grid * 2, 256, 0, s>>>(geo, Lv, Sv));
     return cudaGetLastError();
 }
 
@@ -125,11 +126,12 @@ cudaError_t side_join(cudaStream_t main, SideFork* f);
 
 // Blur neighbours on the side stream while `main_work` runs on the caller's stream.
 template <int PD, typename MainWork>
-cudaError_t neighbors_alongside(const CallArgs& a, const LatView& Lv, const ScrView& Sv, MainWork main_work) {
+cudaError_t neighbors_alongside(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
+                                MainWork main_work) {
     SideFork f;
     cudaError_t e = side_fork(a.stream, &f);
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_NEIGHBORS, f.side, k_neighbors<PD><<<a.sm_count * 8, 256, 0, f.side>>>(Lv, Sv));
+    PL_LAUNCH(STAGE_NEIGHBORS, f.side, k_neighbors<PD><<<a.sm_count * 8, 256, 0, f.side>>>(geo, Lv, Sv));
     main_work();
     const cudaError_t e1 = cudaGetLastError();
     e = side_join(a.stream, &f);
@@ -170,7 +172,7 @@ cudaError_t forward_v(const CallArgs& a) {
     cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, Sv.vf0, CPF, Lv.vb0, CPB);
     if (e != cudaSuccess) return e;
     // neighbour lookups (L2-latency-bound) overlap the splat (HBM-bound)
-    e = neighbors_alongside<PD>(a, Lv, Sv, [&] {
+    e = neighbors_alongside<PD>(a, geo, Lv, Sv, [&] {
         PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
                   k_splat<PD, V, true><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.values, nullptr, geo, Lv, Sv, 1,
                                                                                  Sv.vf0));
@@ -201,7 +203,7 @@ cudaError_t backward_v(const CallArgs& a) {
     if (a.lattice_state == 0) {
         e = build_lattice<PD>(a, geo, Lv, Sv, nullptr, 0, Lv.vb0, CPB);
         if (e != cudaSuccess) return e;
-        e = neighbors_alongside<PD>(a, Lv, Sv, splat);
+        e = neighbors_alongside<PD>(a, geo, Lv, Sv, splat);
         if (e != cudaSuccess) return e;
     } else {
         if (a.lattice_state == 2)

@@ -6,8 +6,9 @@
 //                  hash table (16-bit local ids); unique keys staged to HBM;
 //                  the tile's slots counting-sorted by local id
 //   k_clear        zero the part of the global hash table this call uses
-//   k_insert       global open-addressed insert of the staged keys
-//   k_compact      compact vertex ids for the owners (one atomic per CTA chunk)
+//   k_insert       global open-addressed insert of the staged keys (tagged
+//                  cells); compact vertex ids for the owners, one atomic per
+//                  CTA chunk
 //   k_neighbors    blur neighbours of every vertex by table lookup; runs on a
 //                  side stream, overlapped with the splat
 //   k_splat        per tile: [v*w, w] summed over the sorted segments of equal
@@ -57,6 +58,7 @@ struct EmbedConsts {
 struct Geo {
     int h, w, tiles_x, tiles;
     int cap_max_log2, cap_override_log2;
+    int idx_bits;   // bits that hold 1 + any staged index of the call (global table cells)
 };
 
 struct LatView {
@@ -163,6 +165,19 @@ __device__ __forceinline__ void store_row(float* p, const float (&v)[CP]) {
         for (int j = 0; j < CP; j += 4)
             *reinterpret_cast<float4*>(p + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     }
+}
+
+// ---------------------------------------------------------------- packed int16 keys
+
+// Two int16 key coordinates per 32-bit word.  Per-halfword wrap-around add in
+// plain integer arithmetic: the low halfwords' carry is kept out of the high
+// halfword by adding 15-bit parts and restoring the top bit with an XOR.
+__device__ __forceinline__ uint32_t hw_add(uint32_t a, uint32_t b) {
+    return ((a & 0x7FFF7FFFu) + (b & 0x7FFF7FFFu)) ^ ((a ^ b) & 0x80008000u);
+}
+
+__device__ __forceinline__ uint32_t pack_hw(int lo, int hi) {
+    return (uint32_t)(uint16_t)lo | ((uint32_t)(uint16_t)hi << 16);
 }
 
 // ---------------------------------------------------------------- hashing
@@ -529,8 +544,7 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
 // ---------------------------------------------------------------- K_clear
 
 // Chooses the table capacity from the staged count (load <= 1/2) and zeroes
-// the cells in use.  A cell is 0 (empty) or 1 + the staged index of the key
-// that owns it.
+// the cells in use (cell format: TableFmt).
 static __global__ void k_clear(Geo geo, LatView L, ScrView S) {
     const int U = L.hdr->u_total;
     int lg = 6;
@@ -576,18 +590,41 @@ __device__ __forceinline__ bool key_equal(const uint4* rec, const uint32_t (&kw)
     return eq;
 }
 
-// Read-only lookup after the table is complete: the staged index of the
-// owner of kw, or -1 when kw is not a lattice vertex.
+// Cell format of the global table.  A cell is 0 (empty) or holds, in its low
+// idx_bits, 1 + the staged index of the key that owns it, and above them the
+// same bits of that key's hash (a tag): a probe passes over the cells of
+// other keys on a tag mismatch without reading their records, so a lookup of
+// an absent key usually costs the cells it walks and nothing else.  idx_bits
+// is the width of the call's largest staged index + 1; the tag is what is left
+// of the 32 bits (possibly nothing, which only costs key compares).
+struct TableFmt {
+    uint32_t idx_mask;
+};
+
+__device__ __forceinline__ TableFmt table_fmt(const Geo& g) {
+    TableFmt f;
+    f.idx_mask = g.idx_bits >= 32 ? 0xFFFFFFFFu : ((1u << g.idx_bits) - 1u);
+    return f;
+}
+
+__device__ __forceinline__ uint32_t cell_tag(uint32_t hash, TableFmt f) { return hash & ~f.idx_mask; }
+
+// Continue a probe for kw (word 0 = hash) whose cell at pos has been read as
+// c: the staged index of the owner of kw, or -1 when kw is not in the table.
+// Read-only use, after the table is complete.
 template <int CW>
-__device__ __forceinline__ int table_find(const uint32_t* __restrict__ table, uint32_t mask,
-                                          const uint4* __restrict__ skeys, const uint32_t (&kw)[4 * CW],
-                                          int* status) {
-    uint32_t pos = kw[0] & mask;
+__device__ __forceinline__ int table_probe(const uint32_t* __restrict__ table, uint32_t mask, TableFmt f,
+                                           const uint4* __restrict__ skeys, const uint32_t (&kw)[4 * CW],
+                                           uint32_t pos, uint32_t c, int* status) {
+    const uint32_t tag = cell_tag(kw[0], f);
     for (uint32_t probe = 0; probe <= mask; ++probe) {
-        const uint32_t c = __ldg(table + pos);
         if (c == 0u) return -1;
-        if (key_equal<CW>(skeys + (size_t)(c - 1) * CW, kw)) return (int)c - 1;
+        if ((c & ~f.idx_mask) == tag) {
+            const int o = (int)(c & f.idx_mask) - 1;
+            if (key_equal<CW>(skeys + (size_t)o * CW, kw)) return o;
+        }
         pos = (pos + 1) & mask;
+        c = __ldg(table + pos);
     }
     atomicOr(status, PL_ST_TABLE_FULL);
     return -1;
@@ -597,72 +634,66 @@ __device__ __forceinline__ int table_find(const uint32_t* __restrict__ table, ui
 
 // One thread per staged key.  The staged key records are complete before this
 // kernel starts, so a cell can name its owner the moment the owner's CAS lands:
-// a CAS of (1 + my staged index) into an empty cell makes me the owner; a
-// full cell names an owner whose record is compared word by word.  No cell is
-// ever half-written and nobody waits.
+// a CAS of (tag | 1 + my staged index) into an empty cell makes me the owner;
+// a full cell with my tag names an owner whose record is compared word by
+// word.  No cell is ever half-written and nobody waits.  The owners of each
+// CTA's chunk then take consecutive vertex ids (one atomic per CTA and chunk)
+// and write their key to the vertex key array; cells keep the staged index,
+// and lookups map it to the vertex id through vid_of.
 template <int PD>
-__global__ void __launch_bounds__(256) k_insert(LatView L, ScrView S) {
-    constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
-    const int U = L.hdr->u_total;
-    const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < U; i += gridDim.x * blockDim.x) {
-        uint32_t kw[NW];
-        load_key<CW>(S.skeys + (size_t)i * CW, kw);
-        uint32_t pos = kw[0] & mask;
-        int owner = -1;
-        for (uint32_t probe = 0; probe <= mask; ++probe) {
-            const uint32_t c = atomicCAS(S.table + pos, 0u, (uint32_t)i + 1u);
-            if (c == 0u) { owner = i; break; }
-            if (key_equal<CW>(S.skeys + (size_t)(c - 1) * CW, kw)) { owner = (int)c - 1; break; }
-            pos = (pos + 1) & mask;
-        }
-        if (owner < 0) atomicOr(&L.hdr->status, PL_ST_TABLE_FULL);
-        S.owner[i] = owner;
-    }
-}
-
-// Compact vertex ids for the owners (one atomicAdd per CTA and chunk); their
-// keys are copied to the vertex key array and their table cell is rewritten
-// to hold the vertex id (flag kVidCell set), so that later lookups read the
-// vertex id straight from the cell and compare against the vertex key.
-constexpr uint32_t kVidCell = 0x80000000u;
-
-template <int PD>
-__global__ void __launch_bounds__(256) k_compact(LatView L, ScrView S) {
+__global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
     constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
     __shared__ int s_wcnt[8], s_base;
     const int U = L.hdr->u_total;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
+    const TableFmt f = table_fmt(geo);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     for (int i0 = blockIdx.x * blockDim.x; i0 < U; i0 += gridDim.x * blockDim.x) {   // block-uniform
         const int i = i0 + threadIdx.x;
-        const bool own = i < U && S.owner[i] == i;
+        uint32_t kw[NW];
+        int owner = -1;
+        if (i < U) {
+            load_key<CW>(S.skeys + (size_t)i * CW, kw);
+            const uint32_t tag = cell_tag(kw[0], f);
+            uint32_t pos = kw[0] & mask;
+            for (uint32_t probe = 0; probe <= mask; ++probe) {
+                const uint32_t c = atomicCAS(S.table + pos, 0u, tag | (uint32_t)(i + 1));
+                if (c == 0u) {
+                    owner = i;
+                    break;
+                }
+                if ((c & ~f.idx_mask) == tag) {
+                    const int o = (int)(c & f.idx_mask) - 1;
+                    if (key_equal<CW>(S.skeys + (size_t)o * CW, kw)) {
+                        owner = o;
+                        break;
+                    }
+                }
+                pos = (pos + 1) & mask;
+            }
+            if (owner < 0) atomicOr(&L.hdr->status, PL_ST_TABLE_FULL);
+            S.owner[i] = owner;
+        }
+        const bool own = i < U && owner == i;
         const unsigned m = __ballot_sync(kFull, own);
         if (lane == 0) s_wcnt[wid] = __popc(m);
         __syncthreads();
         if (threadIdx.x == 0) {
             int tot = 0;
-            for (int k = 0; k < 8; ++k) { const int c = s_wcnt[k]; s_wcnt[k] = tot; tot += c; }
+            for (int k = 0; k < 8; ++k) {
+                const int c = s_wcnt[k];
+                s_wcnt[k] = tot;
+                tot += c;
+            }
             s_base = tot ? atomicAdd(&L.hdr->m, tot) : 0;
         }
         __syncthreads();
         if (own) {
             const int vid = s_base + s_wcnt[wid] + __popc(m & ((1u << lane) - 1u));
             S.vid_of[i] = vid;
-            uint32_t kw[NW];
-            load_key<CW>(S.skeys + (size_t)i * CW, kw);
 #pragma unroll
             for (int w = 0; w < CW; ++w)
                 S.vkeys[(size_t)vid * CW + w] = make_uint4(kw[4 * w], kw[4 * w + 1], kw[4 * w + 2], kw[4 * w + 3]);
-            // find my cell (it holds 1 + i) and store the vertex id there
-            uint32_t pos = kw[0] & mask;
-            for (uint32_t probe = 0; probe <= mask; ++probe) {
-                if (S.table[pos] == (uint32_t)i + 1u) {
-                    S.table[pos] = kVidCell | (uint32_t)vid;
-                    break;
-                }
-                pos = (pos + 1) & mask;
-            }
         }
         __syncthreads();   // s_wcnt / s_base reused by the next chunk
     }
@@ -670,53 +701,48 @@ __global__ void __launch_bounds__(256) k_compact(LatView L, ScrView S) {
 
 // Blur neighbours of every vertex: for axis c < PD the step is every
 // coordinate +1 (or -1) and coordinate c -K (or +K), for c == PD every
-// coordinate +1 (or -1) (permutohedral.cu:368-375).  One lookup pair per
-// (vertex, axis); the table cells hold vertex ids after k_compact.
-template <int CW>
-__device__ __forceinline__ int table_find_vid(const uint32_t* __restrict__ table, uint32_t mask,
-                                              const uint4* __restrict__ vkeys, const uint32_t (&kw)[4 * CW],
-                                              int* status) {
-    uint32_t pos = kw[0] & mask;
-    for (uint32_t probe = 0; probe <= mask; ++probe) {
-        const uint32_t c = __ldg(table + pos);
-        if (c == 0u) return -1;
-        const int vid = (int)(c & ~kVidCell);
-        if ((c & kVidCell) && key_equal<CW>(vkeys + (size_t)vid * CW, kw)) return vid;
-        pos = (pos + 1) & mask;
-    }
-    atomicOr(status, PL_ST_TABLE_FULL);
-    return -1;
-}
-
+// coordinate +1 (or -1) (permutohedral.cu:368-375).  A thread takes one
+// vertex and a group of axes (all of them when there are enough vertices to
+// occupy the grid), loads the vertex key once and issues the two lookups of
+// an axis together.
 template <int PD>
-__global__ void __launch_bounds__(256) k_neighbors(LatView L, ScrView S) {
+__global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S) {
     constexpr int K = PD + 1, CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
     const int M = L.hdr->m;
+    if (M <= 0) return;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
-    const size_t total = (size_t)M * K;
-    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (size_t)gridDim.x * blockDim.x) {
-        const int c = (int)(idx / M);
-        const int v = (int)(idx - (size_t)c * M);
-        uint32_t kp[NW], km[NW];
-        load_key<CW>(S.vkeys + (size_t)v * CW, kp);
+    const TableFmt f = table_fmt(geo);
+    const int nthreads = gridDim.x * blockDim.x;
+    int G = (nthreads + M - 1) / M;   // axis groups
+    G = G < 1 ? 1 : (G > K ? K : G);
+    const size_t total = (size_t)M * G;
+    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += nthreads) {
+        const int g = (int)(idx / M);
+        const int v = (int)(idx - (size_t)g * M);
+        uint32_t key[NW];
+        load_key<CW>(S.vkeys + (size_t)v * CW, key);
+        for (int c = g; c < K; c += G) {
+            uint32_t kp[NW], km[NW];
 #pragma unroll
-        for (int k = 0; k < NW; ++k) km[k] = kp[k];   // padding words are copied as they are (0)
+            for (int k = 0; k < NW; ++k) kp[k] = km[k] = key[k];   // padding words stay as they are (0)
 #pragma unroll
-        for (int k = 1; k <= 1 + (PD - 1) / 2; ++k) {   // the words that hold coordinates
-            const int lo = 2 * (k - 1), hi = lo + 1;
-            const uint32_t ones = (lo < PD ? 0x0001u : 0u) | (hi < PD ? 0x00010000u : 0u);
-            uint32_t step = 0u;
-            if (c < PD && (c >> 1) == k - 1) step = (uint32_t)K << (16 * (c & 1));
-            const uint32_t w0 = kp[k];
-            kp[k] = __vsub2(__vadd2(w0, ones), step);
-            km[k] = __vadd2(__vsub2(w0, ones), step);
+            for (int k = 1; k <= 1 + (PD - 1) / 2; ++k) {          // the words that hold coordinates
+                const int lo = 2 * (k - 1), hi = lo + 1;
+                const int dlo = lo < PD ? 1 - (c == lo ? K : 0) : 0;
+                const int dhi = hi < PD ? 1 - (c == hi ? K : 0) : 0;
+                kp[k] = hw_add(key[k], pack_hw(dlo, dhi));
+                km[k] = hw_add(key[k], pack_hw(-dlo, -dhi));
+            }
+            kp[0] = key_hash<NW>(kp);
+            km[0] = key_hash<NW>(km);
+            const uint32_t pa = kp[0] & mask, pb = km[0] & mask;
+            const uint32_t ca = __ldg(S.table + pa), cb = __ldg(S.table + pb);
+            const int oa = table_probe<CW>(S.table, mask, f, S.skeys, kp, pa, ca, &L.hdr->status);
+            const int ob = table_probe<CW>(S.table, mask, f, S.skeys, km, pb, cb, &L.hdr->status);
+            const int a = oa >= 0 ? __ldg(S.vid_of + oa) : -1;
+            const int b = ob >= 0 ? __ldg(S.vid_of + ob) : -1;
+            L.nbr[(size_t)c * M + v] = make_int2(a, b);
         }
-        kp[0] = key_hash<NW>(kp);
-        km[0] = key_hash<NW>(km);
-        const int a = table_find_vid<CW>(S.table, mask, S.vkeys, kp, &L.hdr->status);
-        const int b = table_find_vid<CW>(S.table, mask, S.vkeys, km, &L.hdr->status);
-        L.nbr[(size_t)c * M + v] = make_int2(a, b);
     }
 }
 

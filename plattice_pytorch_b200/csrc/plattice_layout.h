@@ -21,7 +21,8 @@
 // Scratch blob (forward build only):
 //   staged_keys    [U][CW]      uint4    each tile's unique keys (word 0: hash)
 //   table          [cap]        uint32   open-addressed hash table: 0 empty, else
-//                                        1 + staged index of the owning key
+//                                        1 + staged index of the owning key in the
+//                                        low bits, hash bits above (a tag)
 //   owner          [U]          int32    staged index of the owner of each staged key
 //   vid_of         [U]          int32    vertex id of each owner
 //   vkeys          [m][CW]      uint4    key of every vertex
