@@ -4,6 +4,8 @@
 #pragma once
 #include <math.h>
 
+#include <utility>
+
 #include "plattice_kernels.cuh"
 #include "plattice_profile.h"
 
@@ -77,6 +79,24 @@ inline Geo make_geo(const CallArgs& a) {
     return g;
 }
 
+// Launch through cudaLaunchKernelEx (optionally cooperative), returning the
+// launch error.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool coop,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = coop ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // opt in to more than 48 KB of dynamic shared memory, once per device
 template <int PD>
 cudaError_t prepare_tile_build() {
@@ -107,11 +127,14 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     e = cudaMemsetAsync(Lv.hdr, 0, sizeof(LatticeHeader), s);
     if (e != cudaSuccess) return e;
     const EmbedConsts ec = embed_consts(PD);
-    PL_LAUNCH(STAGE_TILE_BUILD, s, k_tile_build<PD><<<a.lay.tiles, C::P, tile_build_smem_bytes<PD>(), s>>>(
-        a.features, geo, ec, Lv, Sv, zero_f, cpf, zero_b, cpb));
-    PL_LAUNCH(STAGE_CLEAR, s, k_clear<<<grid, 256, 0, s>>>(geo, Lv, Sv));
-    PL_LAUNCH(STAGE_INSERT, s, k_insert<PD><<<grid * 2, 256, 0, s>>>(geo, Lv, Sv));
-    return cudaGetLastError();
+    PL_LAUNCH(STAGE_TILE_BUILD, s,
+              e = launch_k(k_tile_build<PD>, dim3(a.lay.tiles), dim3(C::P), tile_build_smem_bytes<PD>(), s, false,
+                             a.features, geo, ec, Lv, Sv, zero_f, cpf, zero_b, cpb));
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_CLEAR, s, e = launch_k(k_clear, dim3(grid), dim3(256), 0, s, false, geo, Lv, Sv));
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_INSERT, s, e = launch_k(k_insert<PD>, dim3(grid * 2), dim3(256), 0, s, false, geo, Lv, Sv));
+    return e;
 }
 
 // Side stream of the current device, forked from and joined back into the
@@ -131,15 +154,15 @@ cudaError_t neighbors_alongside(const CallArgs& a, const Geo& geo, const LatView
     SideFork f;
     cudaError_t e = side_fork(a.stream, &f);
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_NEIGHBORS, f.side, k_neighbors<PD><<<a.sm_count * 8, 256, 0, f.side>>>(geo, Lv, Sv));
-    main_work();
-    const cudaError_t e1 = cudaGetLastError();
+    PL_LAUNCH(STAGE_NEIGHBORS, f.side,
+              e = launch_k(k_neighbors<PD>, dim3(a.sm_count * 8), dim3(256), 0, f.side, false, geo, Lv, Sv));
+    const cudaError_t e1 = e == cudaSuccess ? main_work() : e;
     e = side_join(a.stream, &f);
     return e1 != cudaSuccess ? e1 : e;
 }
 
-// Cooperative launch of the fused neighbour + blur kernel on as many CTAs as
-// are co-resident (at most kCoopPerSm per SM).
+// Cooperative launch of the blur kernel on as many CTAs as are co-resident
+// (at most kCoopPerSm per SM).
 constexpr int kCoopPerSm = 1;
 
 template <int PD, int CP>
@@ -156,10 +179,9 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
         if (dev >= 0 && dev < 64) per_sm[dev] = n;
     }
     const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
-    void* args[] = {&Lv, &b0, &b1, &reverse};
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
-              e = cudaLaunchCooperativeKernel((const void*)k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), args, 0,
-                                              a.stream));
+              e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), 0, a.stream, true, Lv, b0, b1,
+                             reverse));
     return e;
 }
 
@@ -173,18 +195,20 @@ cudaError_t forward_v(const CallArgs& a) {
     if (e != cudaSuccess) return e;
     // neighbour lookups (L2-latency-bound) overlap the splat (HBM-bound)
     e = neighbors_alongside<PD>(a, geo, Lv, Sv, [&] {
+        cudaError_t es;
         PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
-                  k_splat<PD, V, true><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(a.values, nullptr, geo, Lv, Sv, 1,
-                                                                                 Sv.vf0));
+                  es = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                                  a.values, (const float*)nullptr, geo, Lv, Sv, 1, Sv.vf0));
+        return es;
     });
     if (e != cudaSuccess) return e;
     // blur in axis order 0..pd (permutohedral.cu:585)
     e = launch_blur_all<PD, CPF>(a, Lv, Sv.vf0, Sv.vf1, 0);
     if (e != cudaSuccess) return e;
-    float* x = ((PD + 1) % 2 == 0) ? Sv.vf0 : Sv.vf1;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
-              k_slice<PD, V, true><<<a.lay.tiles, Cfg<PD>::P / kSlicePix, 0, a.stream>>>(a.out, a.wout, geo, Lv, x));
-    return cudaGetLastError();
+              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P / kSlicePix), 0, a.stream,
+                           false, a.out, a.wout, geo, Lv, (const float*)Sv.vf0, (const float*)Sv.vf1));
+    return e;
 }
 
 template <int PD, int V>
@@ -196,27 +220,33 @@ cudaError_t backward_v(const CallArgs& a) {
     const int grid = a.sm_count * 8;
     cudaError_t e = cudaSuccess;
     auto splat = [&] {
+        cudaError_t es;
         PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
-                  k_splat<PD, V, false><<<a.lay.tiles, Cfg<PD>::P, 0, a.stream>>>(
-                      a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, Lv.vb0));
+                  es = launch_k(k_splat<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                                  a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, Lv.vb0));
+        return es;
     };
     if (a.lattice_state == 0) {
         e = build_lattice<PD>(a, geo, Lv, Sv, nullptr, 0, Lv.vb0, CPB);
         if (e != cudaSuccess) return e;
         e = neighbors_alongside<PD>(a, geo, Lv, Sv, splat);
-        if (e != cudaSuccess) return e;
     } else {
-        if (a.lattice_state == 2)
-            PL_LAUNCH(STAGE_ZERO, a.stream, k_zero_rows<<<grid, 256, 0, a.stream>>>(Lv.vb0, Lv.hdr, CPB));
-        splat();
+        if (a.lattice_state == 2) {
+            PL_LAUNCH(STAGE_ZERO, a.stream,
+                      e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, Lv.vb0,
+                                     (const LatticeHeader*)Lv.hdr, CPB));
+            if (e != cudaSuccess) return e;
+        }
+        e = splat();
     }
+    if (e != cudaSuccess) return e;
     // blur in axis order pd..0 (permutohedral.cu:647)
     e = launch_blur_all<PD, CPB>(a, Lv, Lv.vb0, Lv.vb1, 1);
     if (e != cudaSuccess) return e;
-    float* x = ((PD + 1) % 2 == 0) ? Lv.vb0 : Lv.vb1;
     PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
-              k_slice<PD, V, false><<<a.lay.tiles, Cfg<PD>::P / kSlicePix, 0, a.stream>>>(a.out, nullptr, geo, Lv, x));
-    return cudaGetLastError();
+              e = launch_k(k_slice<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P / kSlicePix), 0, a.stream,
+                           false, a.out, (float*)nullptr, geo, Lv, (const float*)Lv.vb0, (const float*)Lv.vb1));
+    return e;
 }
 
 #define PL_DISPATCH_V(FN, PDV, ARGS)                      \

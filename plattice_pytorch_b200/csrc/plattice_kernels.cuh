@@ -913,7 +913,7 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
     if ((lane == 31 || !nextCont) && l >= 0 && svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
 }
 
-// ---------------------------------------------------------------- fused neighbours + blur
+// ---------------------------------------------------------------- blur
 
 // Grid barrier over the CTAs of a cooperative launch (all co-resident): one
 // release-add per CTA on a counter that only grows during the launch (it is
@@ -947,27 +947,129 @@ __device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase
     __syncthreads();
 }
 
-// The K blur passes, axis order 0..PD or PD..0, ping-ponging buf0 <-> buf1;
-// the result ends in buf0 when K is even, else in buf1.  One cooperative
-// launch: grid barriers separate the passes; every read of data written
-// inside this launch goes to L2 (ld.global.cg), never to a stale L1 line.
-// Each thread fetches its neighbour pairs of the next pass before the
-// barrier (they do not depend on the values).
+// One [1 2 1]/4 stencil step of a row along one axis; a missing neighbour
+// (index -1) contributes nothing (permutohedral.cu:341-347).
+template <int CP>
+__device__ __forceinline__ void blur_row(const float (&me)[CP], const float (&a)[CP], const float (&b)[CP], int2 n,
+                                         float (&r)[CP]) {
+#pragma unroll
+    for (int j = 0; j < CP; ++j) {
+        float acc = __fmul_rn(2.0f, me[j]);
+        if (n.x >= 0) acc = __fadd_rn(acc, a[j]);
+        if (n.y >= 0) acc = __fadd_rn(acc, b[j]);
+        r[j] = __fmul_rn(0.25f, acc);
+    }
+}
+
+// The K blur passes, axis order 0..PD or PD..0 (reverse), from buf0 over the
+// pair buf0/buf1; hdr->blur_final names the buffer that holds the result.
+// One cooperative launch: grid barriers separate the steps; every read of
+// data written inside this launch goes to L2 (ld.global.cg), never to a
+// stale L1 line.
+//
+// Rows of at most 4 channels and at most R vertices per thread: a thread keeps the same
+// vertices throughout, their rows in registers, and runs the passes in pairs.
+// For passes s, s+1 it evaluates pass s at its vertex v and at v's two
+// neighbours along the axis of pass s+1 (each from the rows pass s reads
+// there, with the float operations the owner of that neighbour uses, so the
+// values are bit-identical), then pass s+1 at v: one barrier per pair.  The
+// neighbour indices of a step, those two hops away included, are requested
+// before the preceding barrier.  Larger lattices stream every row through one
+// pass per step.
 constexpr int kBlurThreads = 1024;
+
+struct BlurIdx {
+    int2 s;        // neighbours along the step's first axis
+    int2 t;        // neighbours along its second axis (pairs only)
+    int2 ta, tb;   // first-axis neighbours of t.x and of t.y
+};
+
+__device__ __forceinline__ int2 nbr_at(const int2* nbr, int M, int axis, int v) {
+    return v >= 0 ? __ldg(nbr + (size_t)axis * M + v) : make_int2(-1, -1);
+}
+
+__device__ __forceinline__ BlurIdx blur_idx(const int2* nbr, int M, int v, int ax_s, int ax_t) {
+    BlurIdx I;
+    I.s = nbr_at(nbr, M, ax_s, v);
+    I.t = ax_t >= 0 ? nbr_at(nbr, M, ax_t, v) : make_int2(-1, -1);
+    I.ta = nbr_at(nbr, M, ax_s, I.t.x);
+    I.tb = nbr_at(nbr, M, ax_s, I.t.y);
+    return I;
+}
+
+// pass s evaluated at vertex u (u >= 0) whose first-axis neighbours are n
+template <int CP>
+__device__ __forceinline__ void blur_at(const float* x, int u, int2 n, float (&r)[CP]) {
+    float me[CP], a[CP], b[CP];
+    load_row_cg<CP>(x + (size_t)u * CP, me);
+    if (n.x >= 0) load_row_cg<CP>(x + (size_t)n.x * CP, a);
+    if (n.y >= 0) load_row_cg<CP>(x + (size_t)n.y * CP, b);
+    blur_row<CP>(me, a, b, n, r);
+}
 
 template <int PD, int CP>
 __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse) {
     constexpr int K = PD + 1;
-    constexpr int VPT = 2;   // vertices per thread and pass held in flight
+    constexpr int R = 2;   // vertices per thread kept in registers (rows of up to 4 channels)
     const int M = L.hdr->m;
     const int stride = gridDim.x * blockDim.x;
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned phase = 0;
     float* x = buf0;
     float* y = buf1;
+    if (CP <= 4 && M <= stride * R) {
+        auto axis = [&](int k) { return k >= K ? -1 : (reverse ? K - 1 - k : k); };
+        float me[R][CP];
+        BlurIdx idx[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int v = tid + r * stride;
+            if (v < M) load_row_cg<CP>(x + (size_t)v * CP, me[r]);
+            idx[r] = blur_idx(L.nbr, M, v < M ? v : -1, axis(0), axis(1));
+        }
+#pragma unroll 1
+        for (int k = 0; k < K; k += 2) {
+            const bool pair = k + 1 < K;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int v = tid + r * stride;
+                if (v >= M) continue;
+                const BlurIdx& I = idx[r];
+                float a[CP], b[CP], o[CP];
+                if (I.s.x >= 0) load_row_cg<CP>(x + (size_t)I.s.x * CP, a);
+                if (I.s.y >= 0) load_row_cg<CP>(x + (size_t)I.s.y * CP, b);
+                blur_row<CP>(me[r], a, b, I.s, o);
+                if (pair) {
+                    float pa[CP], pb[CP];
+                    if (I.t.x >= 0) blur_at<CP>(x, I.t.x, I.ta, pa);
+                    if (I.t.y >= 0) blur_at<CP>(x, I.t.y, I.tb, pb);
+                    float q[CP];
+                    blur_row<CP>(o, pa, pb, I.t, q);
+#pragma unroll
+                    for (int j = 0; j < CP; ++j) o[j] = q[j];
+                }
+                store_row<CP>(y + (size_t)v * CP, o);
+#pragma unroll
+                for (int j = 0; j < CP; ++j) me[r][j] = o[j];
+            }
+            float* t = x; x = y; y = t;
+            if (k + 2 < K) {
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int v = tid + r * stride;
+                    idx[r] = blur_idx(L.nbr, M, v < M ? v : -1, axis(k + 2), axis(k + 3));
+                }
+                grid_barrier(L.hdr, phase);
+            }
+        }
+        if (tid == 0) L.hdr->blur_final = (x == buf1) ? 1 : 0;
+        return;
+    }
+    constexpr int VPT = 2;   // vertices per thread and pass held in flight
+#pragma unroll 1
     for (int s = 0; s < K; ++s) {
-        const int axis = reverse ? K - 1 - s : s;
-        const int2* nb = L.nbr + (size_t)axis * M;
+        const int ax = reverse ? K - 1 - s : s;
+        const int2* nb = L.nbr + (size_t)ax * M;
         for (int v0 = tid; v0 < M; v0 += stride * VPT) {
             int2 n[VPT];
 #pragma unroll
@@ -979,24 +1081,15 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
             for (int k = 0; k < VPT; ++k) {
                 const int v = v0 + k * stride;
                 if (v >= M) continue;
-                float me[CP], a[CP], b[CP];
-                load_row_cg<CP>(x + (size_t)v * CP, me);
-                if (n[k].x >= 0) load_row_cg<CP>(x + (size_t)n[k].x * CP, a);
-                if (n[k].y >= 0) load_row_cg<CP>(x + (size_t)n[k].y * CP, b);
                 float r[CP];
-#pragma unroll
-                for (int j = 0; j < CP; ++j) {
-                    float acc = __fmul_rn(2.0f, me[j]);
-                    if (n[k].x >= 0) acc = __fadd_rn(acc, a[j]);
-                    if (n[k].y >= 0) acc = __fadd_rn(acc, b[j]);
-                    r[j] = __fmul_rn(0.25f, acc);
-                }
+                blur_at<CP>(x, v, n[k], r);
                 store_row<CP>(y + (size_t)v * CP, r);
             }
         }
         if (s + 1 < K) grid_barrier(L.hdr, phase);
         float* t = x; x = y; y = t;
     }
+    if (tid == 0) L.hdr->blur_final = (x == buf1) ? 1 : 0;
 }
 
 // ---------------------------------------------------------------- slice
@@ -1008,8 +1101,10 @@ constexpr int kSlicePix = 1;   // pixels per thread in k_slice
 
 template <int PD, int V, bool FWD>
 __global__ void __launch_bounds__(Cfg<PD>::P / kSlicePix)
-k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat) {
+k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
+        const float* __restrict__ lat1) {
     using C = Cfg<PD>;
+    const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
     constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS, R = kSlicePix, T = P / R;
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;

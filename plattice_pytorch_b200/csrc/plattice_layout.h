@@ -49,8 +49,11 @@ typedef struct {
     int cap_log2;    /* hash table capacity in use (log2 of cells) */
     int n, pd, vd, tiles;
     unsigned bar_count, bar_gen;   /* grid barrier of the cooperative blur kernel */
-    int pad[54];     /* header is 256 bytes */
+    int blur_final;  /* which value buffer (0/1) holds the last blur's result */
+    int pad[53];     /* header is 256 bytes */
 } LatticeHeader;
+
+typedef char pl_header_is_256_bytes[(sizeof(LatticeHeader) == 256) ? 1 : -1];
 
 static inline int pl_tile_pixels(int pd) { return pd <= 6 ? 256 : (pd <= 10 ? 128 : 64); }
 static inline int pl_key_words(int pd) { return (4 + 2 * pd + 15) / 16; }   /* 16-byte words */
