@@ -36,7 +36,7 @@ inline LatView lat_view(void* base, const PlLayout& L) {
     v.slot_w = reinterpret_cast<float*>(b + L.off_slot_w);
     v.slot_order = reinterpret_cast<uint16_t*>(b + L.off_slot_order);
     v.slot_wsort = reinterpret_cast<float*>(b + L.off_slot_wsort);
-    v.seg_off = reinterpret_cast<uint16_t*>(b + L.off_seg_off);
+    v.first_lid = reinterpret_cast<uint16_t*>(b + L.off_first_lid);
     v.staged_vid = reinterpret_cast<int*>(b + L.off_staged_vid);
     v.nbr = reinterpret_cast<int2*>(b + L.off_nbr);
     v.vb0 = reinterpret_cast<float*>(b + L.off_vb0);
@@ -206,7 +206,7 @@ cudaError_t forward_v(const CallArgs& a) {
     e = launch_blur_all<PD, CPF>(a, Lv, Sv.vf0, Sv.vf1, 0);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
-              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P / kSlicePix), 0, a.stream,
+              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
                            false, a.out, a.wout, geo, Lv, (const float*)Sv.vf0, (const float*)Sv.vf1));
     return e;
 }
@@ -244,7 +244,7 @@ cudaError_t backward_v(const CallArgs& a) {
     e = launch_blur_all<PD, CPB>(a, Lv, Lv.vb0, Lv.vb1, 1);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
-              e = launch_k(k_slice<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P / kSlicePix), 0, a.stream,
+              e = launch_k(k_slice<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
                            false, a.out, (float*)nullptr, geo, Lv, (const float*)Lv.vb0, (const float*)Lv.vb1));
     return e;
 }

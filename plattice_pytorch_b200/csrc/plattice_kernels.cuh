@@ -69,7 +69,7 @@ struct LatView {
     float* slot_w;
     uint16_t* slot_order;
     float* slot_wsort;
-    uint16_t* seg_off;
+    uint16_t* first_lid;
     int* staged_vid;
     int2* nbr;
     float* vb0;
@@ -310,21 +310,6 @@ __device__ __forceinline__ void make_key(const int (&g)[PD + 1], const int (&ran
 
 constexpr unsigned kFull = 0xffffffffu;
 
-// segmented inclusive sum along runs of lanes: lanes [start, lane] of the
-// caller's run; the last lane of a run ends with the run's total
-template <int NC>
-__device__ __forceinline__ void run_sum(float (&v)[NC], int start) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-#pragma unroll
-        for (int j = 0; j < NC; ++j) {
-            const float o = __shfl_up_sync(kFull, v[j], d);
-            if (lane - d >= start) v[j] = __fadd_rn(v[j], o);
-        }
-    }
-}
-
 // ---------------------------------------------------------------- block scan
 
 // Exclusive prefix sum of a[0..n) in place by the P threads of the CTA, with
@@ -523,8 +508,9 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
 #pragma unroll
         for (int c = 0; c < K; ++c) {
             const int pos = cnt[lid[c]] + rk[c];
-            ord[pos] = (uint16_t)((t << 5) | c);
+            ord[pos] = (uint16_t)((t << 1) | (rk[c] == 0 ? 1 : 0));   // pixel, run start
             wsort[pos] = bary[c];
+            if (pos % K == 0) L.first_lid[(size_t)tile * P + pos / K] = (uint16_t)lid[c];
         }
     }
     __syncthreads();
@@ -535,7 +521,6 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
         gord[i] = ord[i];
         gws[i] = wsort[i];
     }
-    for (int u = t; u < U; u += P) L.seg_off[base + u] = (uint16_t)cnt[u];
     if (zero_f)
         for (int i = t; i < U * cpf; i += P) zero_f[(size_t)base * cpf + i] = 0.0f;
     for (int i = t; i < U * cpb; i += P) zero_b[(size_t)base * cpb + i] = 0.0f;
@@ -752,13 +737,14 @@ __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S
 // (grad * weight_in) * w (permutohedral.cu:437-445).
 //
 // The tile's slots were counting-sorted by local vertex when the lattice was
-// built, so every local vertex owns a contiguous segment of the sorted order.
-// Thread t sums the K sorted positions [t*K, t*K + K): segments that start and
-// end inside them are added to the lattice at once; the segment the thread
-// ends in is carried across lanes by a segmented warp scan and added by the
-// lane where it ends; the segment it starts in picks up the previous lanes'
-// carry.  About one vector red.global.add per tile vertex, no shared-memory
-// float atomics; the float reduction of a vertex across tiles happens in L2.
+// built: every local vertex owns a contiguous run of the sorted order, runs
+// are in local-id order, and each sorted entry carries its pixel and a
+// run-start flag.  Thread t sums the K sorted positions [t*K, t*K + K),
+// starting from the local id recorded for position t*K and stepping to the
+// next id at every run start, and adds each piece of a run that falls in its
+// positions to the lattice with one vector red.global.add (a run that spans
+// several threads is summed in L2).  Balanced work per thread, no search and
+// no cross-lane scan; no shared-memory float atomics.
 template <int CP, int NC>
 __device__ __forceinline__ void red_run(float* lat, int vid, const float (&s)[NC]) {
     float r[CP];
@@ -776,27 +762,31 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
     constexpr int NV4 = (NC + 3) / 4;            // float4 per pixel value row
-    __shared__ int seg[SLOTS + 1];
     __shared__ int svid[SLOTS];
     __shared__ float4 pv[P * NV4];               // per-pixel values, padded to float4
-    const int t = threadIdx.x, lane = t & 31, tile = blockIdx.x;
+    const int t = threadIdx.x, tile = blockIdx.x;
     if (tile == 0 && t == 0) L.hdr->bar_count = 0u;   // grid barrier of the blur that follows
     const int x0 = (tile % geo.tiles_x) * C::TW, y0 = (tile / geo.tiles_x) * C::TH;
     const int nx = min(C::TW, geo.w - x0), ny = min(C::TH, geo.h - y0);
     const int total = nx * ny * K;
-    // my K sorted positions: slot codes and weights straight into registers
+    // my K sorted positions: entries and weights straight into registers
     const int q0 = t * K;
+    const int nq = max(0, min(K, total - q0));
     int code[K];
     float wq[K];
     {
         const uint16_t* go = L.slot_order + (size_t)tile * SLOTS + q0;
         const float* gw = L.slot_wsort + (size_t)tile * SLOTS + q0;
         if constexpr (K % 2 == 0) {
-            // K even: the K codes are K/2 aligned 32-bit words, the weights K/2 float2
+            // K even: the K entries are K/2 aligned 32-bit words, the weights K/2 float2
 #pragma unroll
             for (int k = 0; k < K; k += 2) {
-                const uint32_t two = __ldg(reinterpret_cast<const uint32_t*>(go + k));
-                const float2 ww = __ldg(reinterpret_cast<const float2*>(gw + k));
+                uint32_t two = 0u;
+                float2 ww = make_float2(0.0f, 0.0f);
+                if (k < nq) {
+                    two = __ldg(reinterpret_cast<const uint32_t*>(go + k));
+                    ww = __ldg(reinterpret_cast<const float2*>(gw + k));
+                }
                 code[k] = (int)(two & 0xffffu);
                 code[k + 1] = (int)(two >> 16);
                 wq[k] = ww.x;
@@ -805,11 +795,12 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
         } else {
 #pragma unroll
             for (int k = 0; k < K; ++k) {
-                code[k] = (int)__ldg(go + k);
-                wq[k] = __ldg(gw + k);
+                code[k] = k < nq ? (int)__ldg(go + k) : 0;
+                wq[k] = k < nq ? __ldg(gw + k) : 0.0f;
             }
         }
     }
+    const int first = nq > 0 ? (int)L.first_lid[(size_t)tile * P + t] : 0;
     {   // this pixel's values
         const int x = x0 + (t % C::TW), y = y0 + (t / C::TW);
         const bool active = x < geo.w && y < geo.h;
@@ -828,11 +819,11 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
 #pragma unroll
         for (int k = 0; k < NV4; ++k) pv[t * NV4 + k] = make_float4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
     }
+    // vertex ids of the tile's local vertices; the call right after a build
+    // resolves them through the owners and stores them for the kernels that
+    // follow
     const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
-    // vertex ids of the tile's keys; the call right after a build resolves
-    // them through the owners and stores them for the kernels that follow
     for (int u = t; u < cnt; u += P) {
-        seg[u] = L.seg_off[off + u];
         int vid;
         if (resolve) {
             const int o = S.owner[off + u];
@@ -843,44 +834,22 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
         }
         svid[u] = vid;
     }
-    if (t == 0) seg[cnt] = total;
     __syncthreads();
-
-    // local id of position q0
-    const int q1 = min(total, q0 + K);
-    int l = -1;
-    if (q0 < total) {
-        int lo = 0, hi = cnt - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (seg[mid] <= q0) lo = mid; else hi = mid - 1;
-        }
-        l = lo;
-    }
-    const int F = l;
-    int next = (l >= 0) ? seg[l + 1] : 0x7fffffff;
-    float cur[NC], first[NC];
+    if (nq == 0) return;
+    int l = first;
+    float cur[NC];
 #pragma unroll
-    for (int j = 0; j < NC; ++j) cur[j] = first[j] = 0.0f;
-    bool multi = false;
+    for (int j = 0; j < NC; ++j) cur[j] = 0.0f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-        const int q = q0 + k;
-        if (q < q1) {
-            if (q == next) {   // a new segment starts at q
-                if (!multi) {
-#pragma unroll
-                    for (int j = 0; j < NC; ++j) first[j] = cur[j];
-                    multi = true;
-                } else if (svid[l] >= 0) {
-                    red_run<CP, NC>(lat, svid[l], cur);   // segment inside my positions: complete
-                }
+        if (k < nq) {
+            if (k > 0 && (code[k] & 1)) {   // a new run starts: the previous piece is complete
+                if (svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
                 ++l;
-                next = seg[l + 1];
 #pragma unroll
                 for (int j = 0; j < NC; ++j) cur[j] = 0.0f;
             }
-            const int px = code[k] >> 5;
+            const int px = code[k] >> 1;
             const float w = wq[k];
             float r[4 * NV4];
 #pragma unroll
@@ -892,25 +861,7 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
             for (int j = 0; j < NC; ++j) cur[j] = __fadd_rn(cur[j], (FWD && j == V) ? w : __fmul_rn(r[j], w));
         }
     }
-    // carry the last segment across lanes
-    const unsigned below = 0xffffffffu >> (31 - lane);
-    const int prevLast = __shfl_up_sync(kFull, l, 1);
-    const bool cont = lane > 0 && F >= 0 && F == prevLast;   // my first segment continues the previous lane's
-    const unsigned heads = __ballot_sync(kFull, multi || !cont);
-    const int start = 31 - __clz(heads & below);
-    run_sum<NC>(cur, start);
-    float prevY[NC];
-#pragma unroll
-    for (int j = 0; j < NC; ++j) prevY[j] = __shfl_up_sync(kFull, cur[j], 1);
-    const bool nextCont = __shfl_down_sync(kFull, cont ? 1 : 0, 1) != 0;
-    if (multi && F >= 0 && svid[F] >= 0) {
-        if (cont) {
-#pragma unroll
-            for (int j = 0; j < NC; ++j) first[j] = __fadd_rn(first[j], prevY[j]);
-        }
-        red_run<CP, NC>(lat, svid[F], first);
-    }
-    if ((lane == 31 || !nextCont) && l >= 0 && svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
+    if (svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
 }
 
 // ---------------------------------------------------------------- blur

@@ -11,10 +11,12 @@
 //   tile_off/cnt   per tile: offset and length of its unique-vertex list
 //   slot_lid       [tile][K][P] uint16   local id of each (pixel, simplex corner)
 //   slot_w         [tile][K][P] float    barycentric weight of the same slot
-//   slot_order     [tile][K*P]  uint16   the tile's slots sorted by local id,
-//                                        (pixel << 5) | corner
+//   slot_order     [tile][K*P]  uint16   the tile's slots sorted by local id:
+//                                        (pixel << 1) | 1 where a local id's
+//                                        run of slots starts
 //   slot_wsort     [tile][K*P]  float    the weights in that sorted order
-//   seg_off        [U]          uint16   first sorted position of each local id
+//   first_lid      [tile][P]    uint16   local id at sorted position t*K (the
+//                                        first position of splat thread t)
 //   staged_vid     [U]          int32    global vertex id of each staged key
 //   nbr            [K][m]       int2     blur neighbours (+, -) per axis, -1 absent
 //   vb0, vb1       [m][CPb]     float    backward lattice values (ping-pong)
@@ -65,7 +67,7 @@ typedef struct {
     int CW, CPf, CPb;
     long long slots;      /* tiles*K*P: bound on staged keys and on vertices */
     int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
-    size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_slot_wsort, off_seg_off,
+    size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_slot_wsort, off_first_lid,
         off_staged_vid, off_nbr, off_vb0, off_vb1, lattice_bytes;
     size_t off_skeys, off_table, off_owner, off_vid_of, off_vkeys, off_vf0, off_vf1, scratch_bytes;
 } PlLayout;
@@ -92,7 +94,7 @@ static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
     L->off_slot_w = o;     o = pl_align(o + S * 4);
     L->off_slot_order = o; o = pl_align(o + S * 2);
     L->off_slot_wsort = o; o = pl_align(o + S * 4);
-    L->off_seg_off = o;    o = pl_align(o + S * 2);
+    L->off_first_lid = o;  o = pl_align(o + T * (size_t)L->P * 2);
     L->off_staged_vid = o; o = pl_align(o + S * 4);
     L->off_nbr = o;        o = pl_align(o + S * L->K * 8);
     L->off_vb0 = o;        o = pl_align(o + S * L->CPb * 4);

@@ -9,7 +9,8 @@ every later kernel relies on, for every feature dimension:
   * every (pixel, simplex corner) slot resolves to the vertex whose key the
     oracle's embedding gives (permutohedral.cu:238-244), with the same weight;
   * each tile's slots, counting-sorted by local vertex id, cover the tile's
-    active slots exactly once, segment by segment;
+    active slots exactly once, in runs of one id each with the run starts
+    flagged, and the first id of every K positions is recorded;
   * the blur neighbour table holds, per axis and direction, the vertex whose
     key is the step of permutohedral.cu:368-375 away, or -1 where there is none.
 The buffer layout is restated here and checked against the library's own
@@ -50,7 +51,7 @@ def _layout(h, w, pd, vd):
         lg += 1
     lat, o = {}, _align(256)
     for name, sz in [("tile_off", T * 4), ("tile_cnt", T * 4), ("slot_lid", S * 2), ("slot_w", S * 4),
-                     ("slot_order", S * 2), ("slot_wsort", S * 4), ("seg_off", S * 2), ("staged_vid", S * 4),
+                     ("slot_order", S * 2), ("slot_wsort", S * 4), ("first_lid", T * P * 2), ("staged_vid", S * 4),
                      ("nbr", S * K * 8), ("vb0", S * CPb * 4), ("vb1", S * CPb * 4)]:
         lat[name] = o
         o = _align(o + sz)
@@ -124,7 +125,7 @@ def test_lattice_invariants(fn, dev):
         coords, padding = _decode(words, pd)
         assert not padding.any(), (name, int(np.count_nonzero(padding)))
         assert np.array_equal(words[:, 0], _key_hash(words)), name
-    vk, _ =_decode(_view(sb, scr_off["vkeys"], M * CW * 4, np.uint32).reshape(M, CW * 4), pd)
+    vk, _ = _decode(_view(sb, scr_off["vkeys"], M * CW * 4, np.uint32).reshape(M, CW * 4), pd)
     assert len({r.tobytes() for r in vk}) == M
     vid_of_key = {r.tobytes(): i for i, r in enumerate(vk)}
 
@@ -135,7 +136,7 @@ def test_lattice_invariants(fn, dev):
     slot_w = _view(lb, lat_off["slot_w"], S, np.float32).reshape(T, K, P)
     order = _view(lb, lat_off["slot_order"], S, np.uint16).reshape(T, K * P)
     wsort = _view(lb, lat_off["slot_wsort"], S, np.float32).reshape(T, K * P)
-    seg_off = _view(lb, lat_off["seg_off"], S, np.uint16)
+    first_lid = _view(lb, lat_off["first_lid"], T * P, np.uint16).reshape(T, P)
     staged_vid = _view(lb, lat_off["staged_vid"], S, np.int32)
     okeys, ow = oracle.embed(f)
     okeys = okeys.reshape(h * w, K, pd)
@@ -154,17 +155,22 @@ def test_lattice_invariants(fn, dev):
                 assert lid < cnt
                 assert staged_vid[base + lid] == vid_of_key[okeys[p, c].tobytes()], (tile, t, c)
                 assert slot_w[tile, c, t].view(np.uint32) == ow[p, c].view(np.uint32), (tile, t, c)
+        # sorted order: runs of equal local id in id order, each entry (pixel, run start)
         total = len(act) * K
-        segs = np.append(seg_off[base:base + cnt].astype(np.int64), total)
-        assert np.all(np.diff(segs) > 0)
         seen = set()
-        for u in range(cnt):
-            for pos in range(segs[u], segs[u + 1]):
-                t, c = int(order[tile, pos]) >> 5, int(order[tile, pos]) & 31
-                assert slot_lid[tile, c, t] == u and (t, c) not in seen
-                assert wsort[tile, pos].view(np.uint32) == slot_w[tile, c, t].view(np.uint32)
-                seen.add((t, c))
-        assert len(seen) == total
+        u = -1
+        for pos in range(total):
+            e = int(order[tile, pos])
+            t, start = e >> 1, e & 1
+            assert start == (1 if pos == 0 else start)
+            u += start
+            cs = [c for c in range(K) if slot_lid[tile, c, t] == u]
+            assert len(cs) == 1 and (t, cs[0]) not in seen, (tile, pos)
+            assert wsort[tile, pos].view(np.uint32) == slot_w[tile, cs[0], t].view(np.uint32)
+            seen.add((t, cs[0]))
+            if pos % K == 0:
+                assert first_lid[tile, pos // K] == u, (tile, pos)
+        assert len(seen) == total and u + 1 == cnt
 
     # blur neighbours
     nbr = _view(lb, lat_off["nbr"], M * K * 2, np.int32).reshape(K, M, 2)
