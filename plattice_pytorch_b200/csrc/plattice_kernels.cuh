@@ -212,10 +212,12 @@ __device__ __forceinline__ int f2s16(float x) {
 
 // Greedy remainder-0 point g, simplex rank and barycentric weights of one
 // feature vector.  Operation order of permutohedral.cu:165-233; the
-// multiply-adds are the fused ones of the reference build.
+// multiply-adds are the fused ones of the reference build.  `col` is this
+// thread's column (stride P) of 2K ints of shared scratch.
 template <int PD>
 __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& ec, int (&g)[PD + 1],
-                                      int (&rank)[PD + 1], float (&bary)[PD + 1]) {
+                                      int (&rank)[PD + 1], float (&bary)[PD + 1], int* col) {
+    constexpr int P = Cfg<PD>::P;
     constexpr int K = PD + 1;
     float e[K];
     e[PD] = __fmul_rn(__fmul_rn((float)(-PD), f[PD - 1]), ec.sf[PD - 1]);
@@ -269,21 +271,33 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
 
     // barycentric weights.  Position k receives +delta_i from the coordinate of
     // rank PD-k and -delta_i from the coordinate of rank PD+1-k, applied in
-    // increasing i as fused multiply-adds starting from 0: the reference's
-    // scatter, evaluated position by position so that it stays in registers.
+    // increasing i as fused multiply-adds starting from 0 (the reference's
+    // scatter).  The deltas and coordinate indices are put in rank order
+    // through this thread's shared-memory column, then read position by
+    // position.
 #pragma unroll
-    for (int i = 0; i < K; ++i) d[i] = __fsub_rn(e[i], (float)g[i]);
-    float b[K + 1];
-#pragma unroll
-    for (int k = 0; k <= K; ++k) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i < K; ++i) {
-            if (k <= PD && rank[i] == PD - k) acc = __fmaf_rn(d[i], ec.rk, acc);
-            if (k >= 1 && rank[i] == PD + 1 - k) acc = __fmaf_rn(-d[i], ec.rk, acc);
-        }
-        b[k] = acc;
+    for (int i = 0; i < K; ++i) {
+        col[rank[i] * P] = __float_as_int(__fsub_rn(e[i], (float)g[i]));
+        col[(K + rank[i]) * P] = i;
     }
+    float dr[K];
+    int ir[K];
+#pragma unroll
+    for (int r = 0; r < K; ++r) {
+        dr[r] = __int_as_float(col[r * P]);
+        ir[r] = col[(K + r) * P];
+    }
+    float b[K + 1];
+    b[0] = __fmaf_rn(dr[PD], ec.rk, 0.0f);
+#pragma unroll
+    for (int k = 1; k <= PD; ++k) {
+        const float dp = dr[PD - k], dm = dr[PD + 1 - k];
+        const bool plus_first = ir[PD - k] < ir[PD + 1 - k];
+        const float first = plus_first ? dp : -dm;
+        const float second = plus_first ? -dm : dp;
+        b[k] = __fmaf_rn(second, ec.rk, __fmaf_rn(first, ec.rk, 0.0f));
+    }
+    b[K] = __fmaf_rn(-dr[0], ec.rk, 0.0f);
     b[0] = __fadd_rn(b[0], __fadd_rn(1.0f, b[K]));
 #pragma unroll
     for (int k = 0; k < K; ++k) bary[k] = b[k];
@@ -351,6 +365,16 @@ __host__ __device__ constexpr int tile_build_smem_bytes() {
     return Cfg<PD>::SLOTS * Cfg<PD>::CW * 16 + Cfg<PD>::SC * 4 + Cfg<PD>::SLOTS * 2;
 }
 
+// CTAs of k_tile_build that fit on an SM by shared memory (228 KB, 1 KB of it
+// reserved per CTA), at most 2048 threads: the register budget is set so that
+// registers do not become the tighter limit.
+template <int PD>
+__host__ __device__ constexpr int tile_build_ctas_per_sm() {
+    constexpr int by_smem = (228 * 1024) / (tile_build_smem_bytes<PD>() + 1024 + 64);
+    constexpr int by_threads = 2048 / Cfg<PD>::P;
+    return by_smem < 1 ? 1 : (by_smem < by_threads ? by_smem : by_threads);
+}
+
 // Per tile of P pixels (one thread per pixel):
 //  1. lattice embedding in registers;
 //  2. every slot (pixel, corner) writes its key record to shared memory; one
@@ -364,7 +388,7 @@ __host__ __device__ constexpr int tile_build_smem_bytes() {
 //     [base, base + U) of the lattice value buffers zeroed (the union of all
 //     tiles' rows covers every vertex id, since ids are < the staged count).
 template <int PD>
-__global__ void __launch_bounds__(Cfg<PD>::P)
+__global__ void __launch_bounds__(Cfg<PD>::P, tile_build_ctas_per_sm<PD>())
 k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L, ScrView S,
              float* zero_f, int cpf, float* zero_b, int cpb) {
     using C = Cfg<PD>;
@@ -383,7 +407,6 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     const bool active = x < geo.w && y < geo.h;
     const size_t p = (size_t)y * geo.w + x;
 
-    for (int i = t; i < SC; i += P) stab[i] = -1;
     if (t == 0) s_count = 0;
 
     float f[PD];
@@ -391,7 +414,10 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     for (int i = 0; i < PD; ++i) f[i] = active ? __ldg(feat + p * PD + i) : 0.0f;
     int g[K], rank[K];
     float bary[K];
-    embed<PD>(f, ec, g, rank, bary);
+    static_assert(2 * K * P <= SC, "embed scratch must fit in the tile table");
+    embed<PD>(f, ec, g, rank, bary, stab + t);
+    // the tile table: entries t + j*P are this thread's own scratch column
+    for (int i = t; i < SC; i += P) stab[i] = -1;
 
     // 2a. candidate key records (visible to other lanes' CAS winners after the fence)
     uint32_t keys[KEEP_KEYS ? K : 1][NW];
