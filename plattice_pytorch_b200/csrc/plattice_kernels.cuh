@@ -365,6 +365,18 @@ __host__ __device__ constexpr int tile_build_smem_bytes() {
     return Cfg<PD>::SLOTS * Cfg<PD>::CW * 16 + Cfg<PD>::SC * 4 + Cfg<PD>::SLOTS * 2;
 }
 
+// Zero n floats from p by the P threads of a CTA (float4 stores when p is
+// 16-byte aligned and n a multiple of 4).
+template <int P>
+__device__ __forceinline__ void zero_rows_block(float* p, int n, bool vec4) {
+    if (vec4) {
+        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int i = threadIdx.x; 4 * i < n; i += P) reinterpret_cast<float4*>(p)[i] = z;
+    } else {
+        for (int i = threadIdx.x; i < n; i += P) p[i] = 0.0f;
+    }
+}
+
 // CTAs of k_tile_build that fit on an SM by shared memory (228 KB, 1 KB of it
 // reserved per CTA), at most 2048 threads: the register budget is set so that
 // registers do not become the tighter limit.
@@ -440,6 +452,8 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     // 2b. one CAS per distinct key of the warp; the cell stores the owning candidate
     const unsigned amask = __ballot_sync(kFull, active);
     int mine[K];
+    unsigned hgrp[K];   // lanes with my key (valid where bit c of huse is set)
+    unsigned huse = 0u;  // warp-uniform: bit c set when no lane met a hash collision at corner c
 #pragma unroll
     for (int c = 0; c < K; ++c) {
         const int cand = t * K + c;
@@ -479,18 +493,35 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
         }
         const int lres = __shfl_sync(kFull, res, leader);
         mine[c] = (active && same) ? lres : res;
+        hgrp[c] = grp;
+        if (__ballot_sync(kFull, active && !same) == 0u) huse |= 1u << c;
     }
     __syncthreads();
 
     // 3. compact local ids for owners, staging, slot records, value rows
+    {   // one shared atomic per warp for all its owners
+        unsigned om[K];
+        int n = 0;
 #pragma unroll
-    for (int c = 0; c < K; ++c)
-        if (active && mine[c] == t * K + c) cand_lid[t * K + c] = (int16_t)atomicAdd(&s_count, 1);
+        for (int c = 0; c < K; ++c) {
+            om[c] = __ballot_sync(kFull, active && mine[c] == t * K + c);
+            n += __popc(om[c]);
+        }
+        int wb = 0;
+        if (lane == 0 && n) wb = atomicAdd(&s_count, n);
+        wb = __shfl_sync(kFull, wb, 0);
+        const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+        for (int c = 0; c < K; ++c) {
+            if ((om[c] >> lane) & 1u) cand_lid[t * K + c] = (int16_t)(wb + __popc(om[c] & lt));
+            wb += __popc(om[c]);
+        }
+    }
     __syncthreads();
     const int U = s_count;
     // the tile hash table is dead from here on: reuse it for the counting sort
     int* cnt = stab;                                                     // [U + 1]
-    uint16_t* ord = reinterpret_cast<uint16_t*>(stab + SLOTS + 1);      // [SLOTS]
+    uint16_t* ord = reinterpret_cast<uint16_t*>(stab + ((SLOTS + 4) & ~3));   // [SLOTS], 16-byte aligned
     for (int i = t; i <= U; i += P) cnt[i] = 0;
     if (t == 0) {
         const int b = atomicAdd(&L.hdr->u_total, U);
@@ -520,8 +551,10 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     int rk[K];
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        const unsigned grp = __match_any_sync(kFull, active ? lid[c] : (1 << 20) + lane);
-        const int leader = __ffs(grp) - 1;
+        // the branch is warp-uniform: every lane calls the match or none does
+        const unsigned grp = ((huse >> c) & 1u) ? hgrp[c]
+                                                : __match_any_sync(kFull, active ? lid[c] : (1 << 20) + lane);
+        const int leader = active ? __ffs(grp) - 1 : lane;
         int b = 0;
         if (active && lane == leader) b = atomicAdd(&cnt[lid[c]], __popc(grp));
         b = __shfl_sync(kFull, b, leader);
@@ -543,13 +576,14 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     const int total = cnt[U];
     uint16_t* gord = L.slot_order + (size_t)tile * SLOTS;
     float* gws = L.slot_wsort + (size_t)tile * SLOTS;
-    for (int i = t; i < total; i += P) {
-        gord[i] = ord[i];
-        gws[i] = wsort[i];
-    }
-    if (zero_f)
-        for (int i = t; i < U * cpf; i += P) zero_f[(size_t)base * cpf + i] = 0.0f;
-    for (int i = t; i < U * cpb; i += P) zero_b[(size_t)base * cpb + i] = 0.0f;
+    // 16-byte copies; the tile's regions are 16-byte aligned and a multiple of
+    // 16 bytes long, so the tail copies stay inside them
+    for (int i = t; 16 * i < 2 * total; i += P)
+        reinterpret_cast<uint4*>(gord)[i] = reinterpret_cast<const uint4*>(ord)[i];
+    for (int i = t; 16 * i < 4 * total; i += P)
+        reinterpret_cast<float4*>(gws)[i] = reinterpret_cast<const float4*>(wsort)[i];
+    if (zero_f) zero_rows_block<P>(zero_f + (size_t)base * cpf, U * cpf, cpf % 4 == 0);
+    zero_rows_block<P>(zero_b + (size_t)base * cpb, U * cpb, cpb % 4 == 0);
 }
 
 // ---------------------------------------------------------------- K_clear
