@@ -802,9 +802,10 @@ __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S
 // run-start flag.  Thread t sums the K sorted positions [t*K, t*K + K),
 // starting from the local id recorded for position t*K and stepping to the
 // next id at every run start, and adds each piece of a run that falls in its
-// positions to the lattice with one vector red.global.add (a run that spans
-// several threads is summed in L2).  Balanced work per thread, no search and
-// no cross-lane scan; no shared-memory float atomics.
+// positions to the lattice with one vector red.global.add; the pieces of a
+// run that crosses lanes are first merged by a segmented warp scan, so that
+// about one red per run and warp remains.  Balanced work per thread, no
+// search; no shared-memory float atomics.
 template <int CP, int NC>
 __device__ __forceinline__ void red_run(float* lat, int vid, const float (&s)[NC]) {
     float r[CP];
@@ -895,16 +896,26 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
         svid[u] = vid;
     }
     __syncthreads();
-    if (nq == 0) return;
+    // my pieces: the first (it may continue the previous lane's run), complete
+    // runs in between (added at once), and the last (it may continue into the
+    // next lane); the first and last are the same piece when no run starts
+    // after my first position
     int l = first;
-    float cur[NC];
+    bool multi = false;
+    float cur[NC], head[NC];
 #pragma unroll
-    for (int j = 0; j < NC; ++j) cur[j] = 0.0f;
+    for (int j = 0; j < NC; ++j) cur[j] = head[j] = 0.0f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
         if (k < nq) {
-            if (k > 0 && (code[k] & 1)) {   // a new run starts: the previous piece is complete
-                if (svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
+            if (k > 0 && (code[k] & 1)) {   // a run starts: the piece before it is complete
+                if (!multi) {
+#pragma unroll
+                    for (int j = 0; j < NC; ++j) head[j] = cur[j];
+                    multi = true;
+                } else if (svid[l] >= 0) {
+                    red_run<CP, NC>(lat, svid[l], cur);
+                }
                 ++l;
 #pragma unroll
                 for (int j = 0; j < NC; ++j) cur[j] = 0.0f;
@@ -921,7 +932,35 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
             for (int j = 0; j < NC; ++j) cur[j] = __fadd_rn(cur[j], (FWD && j == V) ? w : __fmul_rn(r[j], w));
         }
     }
-    if (svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
+    // merge the pieces of a run that crosses lanes: a segmented inclusive sum
+    // of the last pieces, segments starting at every lane whose last piece
+    // starts inside it or whose first position starts a run
+    const int lane = t & 31;
+    const bool cont = lane > 0 && nq > 0 && !(code[0] & 1);   // my first piece continues lane-1's run
+    const unsigned below = 0xffffffffu >> (31 - lane);
+    const unsigned heads = __ballot_sync(kFull, multi || !cont);
+    const int start = 31 - __clz(heads & below);
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+            const float o = __shfl_up_sync(kFull, cur[j], d);
+            if (lane - d >= start) cur[j] = __fadd_rn(cur[j], o);
+        }
+    }
+    float prev[NC];
+#pragma unroll
+    for (int j = 0; j < NC; ++j) prev[j] = __shfl_up_sync(kFull, cur[j], 1);
+    const bool next_cont = __shfl_down_sync(kFull, cont ? 1 : 0, 1) != 0;
+    if (nq == 0) return;
+    if (multi) {   // my first piece closes a run: add what the lanes before me carried
+        if (cont) {
+#pragma unroll
+            for (int j = 0; j < NC; ++j) head[j] = __fadd_rn(head[j], prev[j]);
+        }
+        if (svid[first] >= 0) red_run<CP, NC>(lat, svid[first], head);
+    }
+    if ((lane == 31 || !next_cont) && svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
 }
 
 // ---------------------------------------------------------------- blur
