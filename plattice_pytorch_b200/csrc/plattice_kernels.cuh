@@ -1017,7 +1017,7 @@ __device__ __forceinline__ void blur_row(const float (&me)[CP], const float (&a)
 // data written inside this launch goes to L2 (ld.global.cg), never to a
 // stale L1 line.
 //
-// Rows of at most 4 channels and at most R vertices per thread: a thread keeps the same
+// At most R vertices per thread (R = 2 for rows of up to 4 channels, else 1): a thread keeps the same
 // vertices throughout, their rows in registers, and runs the passes in pairs.
 // For passes s, s+1 it evaluates pass s at its vertex v and at v's two
 // neighbours along the axis of pass s+1 (each from the rows pass s reads
@@ -1047,27 +1047,29 @@ __device__ __forceinline__ BlurIdx blur_idx(const int2* nbr, int M, int v, int a
     return I;
 }
 
-// pass s evaluated at vertex u (u >= 0) whose first-axis neighbours are n
-template <int CP>
-__device__ __forceinline__ void blur_at(const float* x, int u, int2 n, float (&r)[CP]) {
-    float me[CP], a[CP], b[CP];
-    load_row_cg<CP>(x + (size_t)u * CP, me);
-    if (n.x >= 0) load_row_cg<CP>(x + (size_t)n.x * CP, a);
-    if (n.y >= 0) load_row_cg<CP>(x + (size_t)n.y * CP, b);
-    blur_row<CP>(me, a, b, n, r);
+// pass s evaluated at vertex u (u >= 0) whose first-axis neighbours are n, on
+// W channels of rows of stride CP (x points at the first of the W channels)
+template <int W, int CP>
+__device__ __forceinline__ void blur_at(const float* x, int u, int2 n, float (&r)[W]) {
+    float me[W], a[W], b[W];
+    load_row_cg<W>(x + (size_t)u * CP, me);
+    if (n.x >= 0) load_row_cg<W>(x + (size_t)n.x * CP, a);
+    if (n.y >= 0) load_row_cg<W>(x + (size_t)n.y * CP, b);
+    blur_row<W>(me, a, b, n, r);
 }
 
 template <int PD, int CP>
 __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse) {
     constexpr int K = PD + 1;
-    constexpr int R = 2;   // vertices per thread kept in registers (rows of up to 4 channels)
+    constexpr int R = CP <= 4 ? 2 : 1;        // vertices per thread kept in registers
+    constexpr int W = CP < 4 ? CP : 4;         // channels per group (the stencil is per channel)
     const int M = L.hdr->m;
     const int stride = gridDim.x * blockDim.x;
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned phase = 0;
     float* x = buf0;
     float* y = buf1;
-    if (CP <= 4 && M <= stride * R) {
+    if (M <= stride * R) {
         auto axis = [&](int k) { return k >= K ? -1 : (reverse ? K - 1 - k : k); };
         float me[R][CP];
         BlurIdx idx[R];
@@ -1085,22 +1087,27 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
                 const int v = tid + r * stride;
                 if (v >= M) continue;
                 const BlurIdx& I = idx[r];
-                float a[CP], b[CP], o[CP];
-                if (I.s.x >= 0) load_row_cg<CP>(x + (size_t)I.s.x * CP, a);
-                if (I.s.y >= 0) load_row_cg<CP>(x + (size_t)I.s.y * CP, b);
-                blur_row<CP>(me[r], a, b, I.s, o);
-                if (pair) {
-                    float pa[CP], pb[CP];
-                    if (I.t.x >= 0) blur_at<CP>(x, I.t.x, I.ta, pa);
-                    if (I.t.y >= 0) blur_at<CP>(x, I.t.y, I.tb, pb);
-                    float q[CP];
-                    blur_row<CP>(o, pa, pb, I.t, q);
 #pragma unroll
-                    for (int j = 0; j < CP; ++j) o[j] = q[j];
+                for (int c0 = 0; c0 < CP; c0 += W) {
+                    const float* xc = x + c0;
+                    float mine[W], a[W], b[W], o[W];
+#pragma unroll
+                    for (int j = 0; j < W; ++j) mine[j] = me[r][c0 + j];
+                    if (I.s.x >= 0) load_row_cg<W>(xc + (size_t)I.s.x * CP, a);
+                    if (I.s.y >= 0) load_row_cg<W>(xc + (size_t)I.s.y * CP, b);
+                    blur_row<W>(mine, a, b, I.s, o);
+                    if (pair) {
+                        float pa[W], pb[W], q[W];
+                        if (I.t.x >= 0) blur_at<W, CP>(xc, I.t.x, I.ta, pa);
+                        if (I.t.y >= 0) blur_at<W, CP>(xc, I.t.y, I.tb, pb);
+                        blur_row<W>(o, pa, pb, I.t, q);
+#pragma unroll
+                        for (int j = 0; j < W; ++j) o[j] = q[j];
+                    }
+                    store_row<W>(y + (size_t)v * CP + c0, o);
+#pragma unroll
+                    for (int j = 0; j < W; ++j) me[r][c0 + j] = o[j];
                 }
-                store_row<CP>(y + (size_t)v * CP, o);
-#pragma unroll
-                for (int j = 0; j < CP; ++j) me[r][j] = o[j];
             }
             float* t = x; x = y; y = t;
             if (k + 2 < K) {
@@ -1132,7 +1139,7 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
                 const int v = v0 + k * stride;
                 if (v >= M) continue;
                 float r[CP];
-                blur_at<CP>(x, v, n[k], r);
+                blur_at<CP, CP>(x, v, n[k], r);
                 store_row<CP>(y + (size_t)v * CP, r);
             }
         }
