@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define PLATTICE_ABI_VERSION 1
+#define PLATTICE_ABI_VERSION 2
 
 /* status codes */
 #define PLATTICE_OK 0
@@ -74,14 +74,39 @@ int plattice_forward(float* weight_out, float* out, const float* values, const f
 
 /* Value gradient: grad_values_out = S^T B^T S'(grad * weight_in), the blur in
  * axis order pd..0.  lattice_state: 0 = `lattice` does not hold the lattice of
- * `features` (it is rebuilt, `scratch` required); 1 = it holds the lattice
- * built by the last plattice_forward on these features and no backward has
- * used it yet; 2 = it holds that lattice and was used by an earlier backward.
- * Replaces permuto_filter_grad (permutohedral.cu:717), which always rebuilds. */
+ * `features` (it is rebuilt, `scratch` and `features` required); 1 = it holds
+ * the lattice built by the last plattice_forward on these features and no
+ * backward has used it yet; 2 = it holds that lattice and was used by an
+ * earlier backward.  `features` is read only by a rebuild and may be NULL
+ * otherwise.  Replaces permuto_filter_grad (permutohedral.cu:717), which
+ * always rebuilds. */
 int plattice_backward(float* grad_values_out, const float* grad, const float* weight_in,
                       const float* features, void* lattice, size_t lattice_bytes,
                       int lattice_state, void* scratch, size_t scratch_bytes, int pd, int vd,
                       int w, int h, void* stream);
+
+/* Kept lattice: filter further value tensors on the lattice that a
+ * plattice_forward call built (same h, w, pd; any vd), without rebuilding it
+ * -- e.g. the iterations of a mean-field CRF.  No counterpart in the
+ * reference, which rebuilds the lattice on every call (permutohedral.cu:549-570
+ * in the forward, 615-635 in the backward).
+ *
+ * plattice_filter: the forward filter of `values` (same outputs as
+ * plattice_forward: out and weight_out) using `lattice`.
+ * plattice_filter_backward: the value gradient of such a call, given its
+ * weight_out as weight_in (same result as plattice_backward).
+ * `values_ws` holds the lattice value rows of the call
+ * (plattice_filter_workspace_size bytes; any allocator, reusable across
+ * calls).  `lattice_bytes` may be the buffer size of a forward with any vd.
+ * Both calls update bookkeeping in the lattice header, so calls on one
+ * lattice must be issued one after the other (one stream). */
+int plattice_filter_workspace_size(int h, int w, int pd, int vd, size_t* bytes);
+int plattice_filter(float* weight_out, float* out, const float* values, void* lattice,
+                    size_t lattice_bytes, void* values_ws, size_t values_ws_bytes, int pd, int vd,
+                    int w, int h, void* stream);
+int plattice_filter_backward(float* grad_values_out, const float* grad, const float* weight_in,
+                             void* lattice, size_t lattice_bytes, void* values_ws,
+                             size_t values_ws_bytes, int pd, int vd, int w, int h, void* stream);
 
 /* Synchronises `stream` and reads the lattice header: device status bits,
  * vertex count m, number of tile-unique keys staged, log2 of the hash-table

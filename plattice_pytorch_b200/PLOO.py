@@ -27,7 +27,7 @@ import torch
 from . import _lib
 
 __all__ = ["forward", "backward", "Lattice", "lattice_forward", "lattice_backward",
-           "lattice_info", "vertex_keys"]
+           "lattice_filter", "lattice_filter_backward", "lattice_info", "vertex_keys"]
 
 _CHECK = os.environ.get("PLATTICE_CHECK", "0") not in ("", "0")
 
@@ -177,6 +177,64 @@ def lattice_backward(features, grad_values, weight_saved, lattice=None, saved=Fa
         if _CHECK and h * w > 0:
             chk = lattice if lattice is not None else Lattice(features, vd, buf, None)
             _sync_check(chk, "plattice_backward")
+    return out
+
+
+def _check_kept(lattice, t, name):
+    _require(isinstance(lattice, Lattice), "lattice must be a Lattice from lattice_forward")
+    _check_input(t, name)
+    _require(t.dim() == 3, f"{name} must be [H, W, vd]")
+    _require(t.dtype == torch.float32, f"{name} must be float32")
+    _require((int(t.shape[0]), int(t.shape[1])) == (lattice.h, lattice.w),
+             f"{name} must match the lattice's H, W")
+    _require(t.device == lattice.device, f"{name} must be on the lattice's device")
+    vd = int(t.shape[2])
+    _check_dims(lattice.pd, vd)
+    return vd
+
+
+def lattice_filter(lattice, values):
+    """Forward filter of ``values`` on a kept lattice (the lattice that
+    :func:`lattice_forward` built, still holding its features' lattice; any
+    vd): the same ``(weight [H,W,1], out [H,W,vd])`` as ``forward`` on those
+    features, without rebuilding the lattice.  Calls on one lattice must run
+    on one stream (they update its header)."""
+    vd = _check_kept(lattice, values, "values")
+    h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
+    with torch.cuda.device(dev):
+        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
+        weight = torch.empty((h, w, 1), dtype=torch.float32, device=dev)
+        wsb = _lib.filter_workspace_size(h, w, pd, vd)
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        rc = _lib.lib().plattice_filter(_ptr(weight), _ptr(out), _ptr(values), _ptr(lattice.buf),
+                                        lattice.buf.numel(), _ptr(ws), wsb, pd, vd, w, h, _stream(dev))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError("plattice_filter", rc, f"h={h} w={w} pd={pd} vd={vd}")
+        if _CHECK and h * w > 0:
+            _sync_check(lattice, "plattice_filter")
+    return weight, out
+
+
+def lattice_filter_backward(lattice, grad_values, weight_saved):
+    """Value gradient of a :func:`lattice_filter` call on the same kept
+    lattice, given that call's ``weight``; returns ``grad [H,W,vd]``."""
+    vd = _check_kept(lattice, grad_values, "grad_values")
+    _check_input(weight_saved, "weight_saved")
+    _require(weight_saved.dim() == 3 and tuple(weight_saved.shape) == (lattice.h, lattice.w, 1),
+             "weight_saved must be [H, W, 1]")
+    _require(weight_saved.dtype == torch.float32, "weight_saved must be float32")
+    h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
+    with torch.cuda.device(dev):
+        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
+        wsb = _lib.filter_workspace_size(h, w, pd, vd)
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        rc = _lib.lib().plattice_filter_backward(_ptr(out), _ptr(grad_values), _ptr(weight_saved),
+                                                 _ptr(lattice.buf), lattice.buf.numel(), _ptr(ws), wsb,
+                                                 pd, vd, w, h, _stream(dev))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError("plattice_filter_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
+        if _CHECK and h * w > 0:
+            _sync_check(lattice, "plattice_filter_backward")
     return out
 
 

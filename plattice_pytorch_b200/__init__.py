@@ -6,6 +6,6 @@ plattice.py (PermutoLatticeFunction, PermutoLattice).  The work is done by
 libplattice_b200.so through the C ABI of include/plattice.h.
 """
 from . import PLOO
-from .plattice import PermutoLattice, PermutoLatticeFunction
+from .plattice import LatticeFilterFunction, PermutoLattice, PermutoLatticeFunction
 
-__all__ = ["PLOO", "PermutoLattice", "PermutoLatticeFunction"]
+__all__ = ["PLOO", "PermutoLattice", "PermutoLatticeFunction", "LatticeFilterFunction"]

@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "libplattice_b200.so")
 
 OK, ERR_INVALID, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
 DEV_TABLE_FULL, DEV_WAIT_LIMIT, DEV_ROUND_LIMIT = 2, 4, 8
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lock = threading.Lock()
 _lib = None
@@ -61,6 +61,12 @@ def lib():
         L.plattice_forward.argtypes = [P, P, P, P, P, S, P, S, I, I, I, I, P]
         L.plattice_backward.restype = I
         L.plattice_backward.argtypes = [P, P, P, P, P, S, I, P, S, I, I, I, I, P]
+        L.plattice_filter_workspace_size.restype = I
+        L.plattice_filter_workspace_size.argtypes = [I, I, I, I, ctypes.POINTER(S)]
+        L.plattice_filter.restype = I
+        L.plattice_filter.argtypes = [P, P, P, P, S, P, S, I, I, I, I, P]
+        L.plattice_filter_backward.restype = I
+        L.plattice_filter_backward.argtypes = [P, P, P, P, S, P, S, I, I, I, I, P]
         L.plattice_lattice_info.restype = I
         L.plattice_lattice_info.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I),
                                             ctypes.POINTER(I), ctypes.POINTER(I), P]
@@ -94,6 +100,14 @@ def workspace_sizes(h, w, pd, vd):
     if rc != OK:
         raise PlatticeError("plattice_workspace_sizes", rc, f"h={h} w={w} pd={pd} vd={vd}")
     return lb.value, sb.value
+
+
+def filter_workspace_size(h, w, pd, vd):
+    b = ctypes.c_size_t(0)
+    rc = lib().plattice_filter_workspace_size(h, w, pd, vd, ctypes.byref(b))
+    if rc != OK:
+        raise PlatticeError("plattice_filter_workspace_size", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    return b.value
 
 
 PROFILE_STAGES = 11

@@ -14,6 +14,7 @@ namespace pl {
 #define PL_DECLARE_PD(N)                                                                    \
     extern template cudaError_t run_forward<N>(const CallArgs&);                             \
     extern template cudaError_t run_backward<N>(const CallArgs&);                            \
+    extern template cudaError_t run_filter<N>(const CallArgs&);                              \
     extern template cudaError_t run_export_keys<N>(const void*, const void*, const PlLayout&, \
                                                    int16_t*, int, cudaStream_t);
 PL_DECLARE_PD(1) PL_DECLARE_PD(2) PL_DECLARE_PD(3) PL_DECLARE_PD(4)
@@ -139,6 +140,12 @@ static cudaError_t dispatch_forward(const pl::CallArgs& a) {
 #undef PL_FWD
 }
 
+static cudaError_t dispatch_filter(const pl::CallArgs& a) {
+#define PL_FIL(N) pl::run_filter<N>(a)
+    PL_PD_SWITCH(a.lay.pd, PL_FIL)
+#undef PL_FIL
+}
+
 static cudaError_t dispatch_backward(const pl::CallArgs& a) {
 #define PL_BWD(N) pl::run_backward<N>(a)
     PL_PD_SWITCH(a.lay.pd, PL_BWD)
@@ -243,8 +250,8 @@ int plattice_backward(float* grad_values_out, const float* grad, const float* we
     if (rc != PLATTICE_OK) return rc;
     if (h == 0 || w == 0) return PLATTICE_OK;
     if (lattice_state < 0 || lattice_state > 2) return PLATTICE_ERR_INVALID;
-    if (!grad_values_out || !grad || !weight_in || !features || !lattice) return PLATTICE_ERR_INVALID;
-    if (lattice_state == 0 && !scratch) return PLATTICE_ERR_INVALID;
+    if (!grad_values_out || !grad || !weight_in || !lattice) return PLATTICE_ERR_INVALID;
+    if (lattice_state == 0 && (!scratch || !features)) return PLATTICE_ERR_INVALID;
     pl::CallArgs a = {};
     pl_layout(&a.lay, h, w, pd, vd);
     if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
@@ -257,6 +264,76 @@ int plattice_backward(float* grad_values_out, const float* grad, const float* we
     a.lattice_state = lattice_state;
     a.cap_override_log2 = g_cap_override_log2;
     return cuda_status(dispatch_backward(a), "plattice_backward");
+}
+
+// ---------------------------------------------------------------- kept lattice
+
+// Value rows of a filter call: two buffers of slots x pad(vd+1) floats.
+static size_t filter_ws_half(const PlLayout& L) { return pl_align((size_t)L.slots * (size_t)L.CPf * 4); }
+
+int plattice_filter_workspace_size(int h, int w, int pd, int vd, size_t* bytes) {
+    const int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (!bytes) return PLATTICE_ERR_INVALID;
+    *bytes = 256;
+    if (h > 0 && w > 0) {
+        PlLayout L;
+        pl_layout(&L, h, w, pd, vd);
+        *bytes = 2 * filter_ws_half(L);
+    }
+    return PLATTICE_OK;
+}
+
+// The checks shared by the two kept-lattice calls; fills the layout and the
+// value buffers.
+static int kept_lattice_args(pl::CallArgs& a, size_t lattice_bytes, void* ws, size_t ws_bytes, int pd, int vd,
+                             int w, int h, void* stream) {
+    pl_layout(&a.lay, h, w, pd, vd);
+    // the arrays a filter reads precede the backward value rows, whose size
+    // is the only part of the lattice that depends on vd
+    if (lattice_bytes < a.lay.off_vb0) return PLATTICE_ERR_WORKSPACE;
+    const size_t half = filter_ws_half(a.lay);
+    if (ws_bytes < 2 * half) return PLATTICE_ERR_WORKSPACE;
+    a.vbuf0 = static_cast<float*>(ws);
+    a.vbuf1 = reinterpret_cast<float*>(static_cast<char*>(ws) + half);
+    a.stream = static_cast<cudaStream_t>(stream);
+    a.sm_count = sm_count_current();
+    a.cap_override_log2 = g_cap_override_log2;
+    return PLATTICE_OK;
+}
+
+int plattice_filter(float* weight_out, float* out, const float* values, void* lattice, size_t lattice_bytes,
+                    void* values_ws, size_t values_ws_bytes, int pd, int vd, int w, int h, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (h == 0 || w == 0) return PLATTICE_OK;
+    if (!weight_out || !out || !values || !lattice || !values_ws) return PLATTICE_ERR_INVALID;
+    pl::CallArgs a = {};
+    rc = kept_lattice_args(a, lattice_bytes, values_ws, values_ws_bytes, pd, vd, w, h, stream);
+    if (rc != PLATTICE_OK) return rc;
+    a.values = values;
+    a.out = out;
+    a.wout = weight_out;
+    a.lattice = lattice;
+    return cuda_status(dispatch_filter(a), "plattice_filter");
+}
+
+int plattice_filter_backward(float* grad_values_out, const float* grad, const float* weight_in, void* lattice,
+                             size_t lattice_bytes, void* values_ws, size_t values_ws_bytes, int pd, int vd, int w,
+                             int h, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (h == 0 || w == 0) return PLATTICE_OK;
+    if (!grad_values_out || !grad || !weight_in || !lattice || !values_ws) return PLATTICE_ERR_INVALID;
+    pl::CallArgs a = {};
+    rc = kept_lattice_args(a, lattice_bytes, values_ws, values_ws_bytes, pd, vd, w, h, stream);
+    if (rc != PLATTICE_OK) return rc;
+    a.values = grad;
+    a.weight_in = weight_in;
+    a.out = grad_values_out;
+    a.lattice = lattice;
+    a.lattice_state = 2;   // kept lattice: zero the value rows, no rebuild
+    return cuda_status(dispatch_backward(a), "plattice_filter_backward");
 }
 
 int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total, int* cap_log2, void* stream) {

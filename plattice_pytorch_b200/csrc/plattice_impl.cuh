@@ -24,6 +24,8 @@ struct CallArgs {
     int sm_count;
     int lattice_state;       // backward: 0 rebuild, 1 fresh from forward, 2 reuse (re-zero)
     int cap_override_log2;
+    float* vbuf0;            // value buffers of a filter call on a kept lattice (else null:
+    float* vbuf1;            // the forward's scratch rows / the lattice's backward rows)
 };
 
 inline LatView lat_view(void* base, const PlLayout& L) {
@@ -215,8 +217,12 @@ template <int PD, int V>
 cudaError_t backward_v(const CallArgs& a) {
     constexpr int CPB = pad_ch(V);
     const Geo geo = make_geo(a);
-    const LatView Lv = lat_view(a.lattice, a.lay);
-    const ScrView Sv = scr_view(a.scratch, a.lay);
+    LatView Lv = lat_view(a.lattice, a.lay);
+    const ScrView Sv = a.scratch ? scr_view(a.scratch, a.lay) : ScrView{};
+    if (a.vbuf0) {   // a filter on a kept lattice: the caller's value rows
+        Lv.vb0 = a.vbuf0;
+        Lv.vb1 = a.vbuf1;
+    }
     const int grid = a.sm_count * 8;
     cudaError_t e = cudaSuccess;
     auto splat = [&] {
@@ -249,6 +255,32 @@ cudaError_t backward_v(const CallArgs& a) {
     return e;
 }
 
+// Forward filter of new values on a kept lattice (built by a forward call on
+// the same image): zero the value rows, splat, blur, slice.  No rebuild.
+template <int PD, int V>
+cudaError_t filter_v(const CallArgs& a) {
+    constexpr int CPF = pad_ch(V + 1);
+    const Geo geo = make_geo(a);
+    const LatView Lv = lat_view(a.lattice, a.lay);
+    const ScrView Sv = {};
+    const int grid = a.sm_count * 8;
+    cudaError_t e;
+    PL_LAUNCH(STAGE_ZERO, a.stream,
+              e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.vbuf0,
+                           (const LatticeHeader*)Lv.hdr, CPF));
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
+              e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                           a.values, (const float*)nullptr, geo, Lv, Sv, 0, a.vbuf0));
+    if (e != cudaSuccess) return e;
+    e = launch_blur_all<PD, CPF>(a, Lv, a.vbuf0, a.vbuf1, 0);
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
+              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.out,
+                           a.wout, geo, Lv, (const float*)a.vbuf0, (const float*)a.vbuf1));
+    return e;
+}
+
 #define PL_DISPATCH_V(FN, PDV, ARGS)                      \
     switch ((ARGS).lay.vd) {                              \
         case 1: return FN<PDV, 1>(ARGS);                  \
@@ -267,6 +299,9 @@ cudaError_t run_forward(const CallArgs& a) { PL_DISPATCH_V(forward_v, PD, a) }
 
 template <int PD>
 cudaError_t run_backward(const CallArgs& a) { PL_DISPATCH_V(backward_v, PD, a) }
+
+template <int PD>
+cudaError_t run_filter(const CallArgs& a) { PL_DISPATCH_V(filter_v, PD, a) }
 
 template <int PD>
 cudaError_t run_export_keys(const void* lattice, const void* scratch, const PlLayout& lay, int16_t* out,

@@ -7,6 +7,11 @@ reference (plattice.py:19).  ``PermutoLattice`` is the nn.Module wrapper.
 
 Unlike the reference, the lattice that forward builds is kept on the autograd
 context and reused by backward (no rebuild).
+
+``LatticeFilterFunction`` (no counterpart in the reference) filters further
+values on a kept lattice -- the ``PLOO.Lattice`` of an earlier forward on the
+same features -- without rebuilding it, as the iterations of a mean-field CRF
+do; its backward is the value gradient on the same lattice.
 """
 import torch
 from torch.autograd import Function
@@ -15,7 +20,7 @@ from torch.nn import Module
 
 from . import PLOO
 
-__all__ = ["PermutoLatticeFunction", "PermutoLattice"]
+__all__ = ["PermutoLatticeFunction", "PermutoLattice", "LatticeFilterFunction"]
 
 
 class PermutoLatticeFunction(Function):
@@ -38,3 +43,21 @@ class PermutoLatticeFunction(Function):
 class PermutoLattice(Module):
     def forward(self, feature, values):
         return PermutoLatticeFunction.apply(feature, values)
+
+
+class LatticeFilterFunction(Function):
+    """``LatticeFilterFunction.apply(values, lattice) -> out``: the forward filter
+    of ``values`` on the kept ``lattice``; gradient to ``values`` only."""
+
+    @staticmethod
+    def forward(ctx, values, lattice):
+        weight, out = PLOO.lattice_filter(lattice, values)
+        ctx.save_for_backward(weight)
+        ctx.lattice = lattice
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        (weight,) = ctx.saved_tensors
+        return PLOO.lattice_filter_backward(ctx.lattice, grad_output.contiguous(), weight), None

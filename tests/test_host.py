@@ -59,6 +59,33 @@ def test_workspace_sizes_and_argument_checks(lib):
     assert lib.plattice_forward(None, None, None, None, None, 0, None, 0, 5, 3, 8, 8, None) == _lib.ERR_INVALID
 
 
+def test_kept_lattice_sizes_and_argument_checks(lib):
+    """plattice_filter / plattice_filter_backward refuse bad arguments and
+    undersized buffers before any CUDA call."""
+    from plattice_pytorch_b200 import _lib
+    b = _lib.filter_workspace_size(1024, 1024, 5, 3)
+    lb, _ = _lib.workspace_sizes(1024, 1024, 5, 3)
+    assert b >= 2 * 1024 * 1024 * 6 * 4 * 4   # two value-row buffers of slots x 4 floats
+    assert _lib.filter_workspace_size(0, 5, 5, 3) == 256
+    for pd, vd in [(0, 3), (17, 3), (5, 0), (5, 9)]:
+        with pytest.raises(_lib.PlatticeError):
+            _lib.filter_workspace_size(8, 8, pd, vd)
+    fake = ctypes.c_void_p(256)   # never dereferenced: every call below returns before using it
+    # invalid dimensions, missing pointers
+    assert lib.plattice_filter(fake, fake, fake, fake, lb, fake, b, 0, 3, 8, 8, None) == _lib.ERR_INVALID
+    assert lib.plattice_filter(None, fake, fake, fake, lb, fake, b, 5, 3, 8, 8, None) == _lib.ERR_INVALID
+    assert lib.plattice_filter_backward(fake, fake, None, fake, lb, fake, b, 5, 3, 8, 8, None) == _lib.ERR_INVALID
+    # undersized lattice or value workspace
+    lb8, _ = _lib.workspace_sizes(8, 8, 5, 3)
+    b8 = _lib.filter_workspace_size(8, 8, 5, 3)
+    assert lib.plattice_filter(fake, fake, fake, fake, 1000, fake, b8, 5, 3, 8, 8, None) == _lib.ERR_WORKSPACE
+    assert lib.plattice_filter(fake, fake, fake, fake, lb8, fake, b8 - 1, 5, 3, 8, 8, None) == _lib.ERR_WORKSPACE
+    assert lib.plattice_filter_backward(fake, fake, fake, fake, lb8, fake, 16, 5, 3, 8, 8, None) == _lib.ERR_WORKSPACE
+    # a rebuild needs the features
+    assert lib.plattice_backward(fake, fake, fake, None, fake, lb8, 0, fake, 1 << 30, 5, 3, 8, 8,
+                                 None) == _lib.ERR_INVALID
+
+
 def test_python_checks_raise_reference_messages():
     from plattice_pytorch_b200 import PLOO
     f = torch.zeros(4, 4, 5)
@@ -67,6 +94,8 @@ def test_python_checks_raise_reference_messages():
         PLOO.forward(f, v)
     with pytest.raises(RuntimeError, match="features must be CUDA"):
         PLOO.backward(f, v, torch.zeros(4, 4, 1))
+    with pytest.raises(RuntimeError, match="lattice must be a Lattice"):
+        PLOO.lattice_filter(object(), v)
 
 
 def _free_port():
