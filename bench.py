@@ -58,6 +58,9 @@ def parse_args():
                     help="untimed steps before warm-up so that clocks settle under load")
     ap.add_argument("--mode", choices=["full", "device"], default="full",
                     help="device: only the warm-up and the K device-timed steps (for profilers)")
+    ap.add_argument("--kept-lattice", action="store_true",
+                    help="time filter forward + backward on a lattice built once (a mean-field "
+                         "iteration), next to the full forward + backward; 1 GPU, ours only")
     return ap.parse_args()
 
 
@@ -217,6 +220,41 @@ def timed_device(fn, batch, steps, flush):
         evs.append((e0, e1))
     torch.cuda.synchronize()
     return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def kept_lattice_line(args, dev):
+    """One JSON line: filter forward + value-gradient backward on a kept lattice
+    (LatticeFilterFunction), per step, against the full forward + backward
+    (PermutoLatticeFunction, lattice rebuilt every step); L2 flushed between
+    steps, CUDA events on the launching stream."""
+    from plattice_pytorch_b200 import PLOO, LatticeFilterFunction, PermutoLatticeFunction
+    from plattice_pytorch_b200.workloads import make_workload
+    wl = make_workload(args.workload, seed=0)
+    f = torch.from_numpy(wl["features"]).to(dev)
+    v = torch.from_numpy(wl["values"]).to(dev).requires_grad_(True)
+    g = torch.from_numpy(wl["grad"]).to(dev)
+    h, w, pd = f.shape
+    _, _, lat = PLOO.lattice_forward(f, v.detach())
+
+    class Kept:   # the step() protocol over the kept lattice
+        @staticmethod
+        def apply(ff, vv):
+            return LatticeFilterFunction.apply(vv, lat)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    res = {}
+    for name, fn in (("kept", Kept), ("full", PermutoLatticeFunction)):
+        for _ in range(args.warmup):
+            step(fn, f, v, g)
+        res[name] = timed_device(fn, [(f, v, g)], args.steps, flush) / args.steps
+    n = h * w
+    return {"metric": "Mpixel/s filter fwd+bwd on a kept lattice (mean-field iteration)",
+            "value": n / (res["kept"] * 1e-3) / 1e6, "unit": "Mpixel/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["kept"], "higher_is_better": True,
+            "full_ms_per_step": res["full"], "speedup_vs_rebuild": res["full"] / res["kept"],
+            "lattice": PLOO.lattice_info(lat), "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "h": int(h), "w": int(w), "pd": int(pd),
+                       "vd": int(v.shape[2]), "l2": "flushed between timed steps"}}
 
 
 def timed_e2e(fn, host, steps, dev):
@@ -387,6 +425,11 @@ def main():
     args = parse_args()
     rank, world, local = dist_setup()
     dev = torch.device("cuda", local)
+
+    if args.kept_lattice:
+        if rank == 0 and args.impl == "ours":
+            print(json.dumps(kept_lattice_line(args, dev)))
+        return
 
     if args.impl == "reference":
         if rank != 0:
