@@ -58,6 +58,9 @@ def parse_args():
                     help="untimed steps before warm-up so that clocks settle under load")
     ap.add_argument("--mode", choices=["full", "device"], default="full",
                     help="device: only the warm-up and the K device-timed steps (for profilers)")
+    ap.add_argument("--batched", action="store_true",
+                    help="ours: the images of a rank go through one batch call per step "
+                         "(PermutoLatticeBatchFunction) instead of one call per image")
     ap.add_argument("--kept-lattice", action="store_true",
                     help="time filter forward + backward on a lattice built once (a mean-field "
                          "iteration), next to the full forward + backward; 1 GPU, ours only")
@@ -448,12 +451,20 @@ def main():
     h, w, pd = imgs[0]["features"].shape
     vd = imgs[0]["values"].shape[2]
     n = h * w
+    n_images = len(imgs)
     batch = []
     for im in imgs:
         f = torch.from_numpy(im["features"]).to(dev)
         v = torch.from_numpy(im["values"]).to(dev).requires_grad_(True)
         g = torch.from_numpy(im["grad"]).to(dev)
         batch.append((f, v, g))
+    per_image_fn, per_image_batch = fn, batch
+    batched = args.batched and args.impl == "ours"
+    if batched:   # one [B,H,W,...] triple, one library call per step
+        from plattice_pytorch_b200 import PermutoLatticeBatchFunction
+        fn = PermutoLatticeBatchFunction
+        batch = [(torch.stack([b[0] for b in batch]), torch.stack([b[1].detach() for b in batch]).requires_grad_(True),
+                  torch.stack([b[2] for b in batch]))]
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
     if args.mode == "device":
@@ -489,6 +500,8 @@ def main():
     # end to end from pinned host buffers
     host = [(torch.from_numpy(im["features"]).pin_memory(), torch.from_numpy(im["values"]).pin_memory(),
              torch.from_numpy(im["grad"]).pin_memory()) for im in imgs]
+    if batched:
+        host = [tuple(torch.stack([hh[k] for hh in host]).pin_memory() for k in range(3))]
     for _ in range(max(1, args.warmup // 2)):
         timed_e2e(fn, host, 1, dev)
     barrier(world_eff)
@@ -497,7 +510,7 @@ def main():
     t_e2e = max_over_ranks(t_e2e, world_eff)
     clk = clocks.stop()
 
-    px_total = world_eff * len(batch) * n * args.steps
+    px_total = world_eff * n_images * n * args.steps
     value = px_total / (t_dev * 1e-3) / 1e6
     h2d = sum(int(x.numel()) * 4 for hh in host for x in hh)
     d2h = sum(2 * int(hh[1].numel()) * 4 for hh in host)
@@ -506,10 +519,11 @@ def main():
         "warmup": args.warmup, "ms_per_step": t_dev / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": args.workload, "h": h, "w": w, "pd": pd, "vd": vd,
-                   "images_per_gpu": len(batch),
+                   "images_per_gpu": n_images,
                    "l2": "flushed between timed steps (256 MiB write, outside the events)",
                    "parallelism": "one image lattice per rank, no collective" if world_eff > 1 else "1 GPU",
-                   "api": "PermutoLatticeFunction forward + torch.autograd.grad backward"},
+                   "api": ("PermutoLatticeBatchFunction (one call per batch)" if batched else
+                           "PermutoLatticeFunction forward") + " + torch.autograd.grad backward"},
         "e2e": {"value": px_total / (t_e2e * 1e-3) / 1e6, "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "pipeline": "H2D on an input stream, filter on the default stream, D2H on an output "
@@ -521,7 +535,7 @@ def main():
         res["reference_build"] = "reference permuto.cpp + permutohedral.cu, unmodified, nvcc sm_100a"
 
     if args.impl == "ours":
-        info, prof = profile_ours(fn, batch, args.profile_steps, flush, n, pd, vd)
+        info, prof = profile_ours(per_image_fn, per_image_batch, args.profile_steps, flush, n, pd, vd)
         m, u, cap = info["m"], info["u_total"], info["cap_log2"]
         peak, peak_kind = hbm_peak()
         per_stage = {}
@@ -558,7 +572,7 @@ def main():
             "frac_all_kernels": (b_fwd + b_bwd) / (all_ms * 1e-3) / 1e9 / peak}
         res["stages"] = per_stage
         res["lattice"] = {"m": m, "u_total": u, "cap_log2": cap}
-        res["gpu_launches"] = int(round(launches_per_step * args.steps * len(batch)))
+        res["gpu_launches"] = int(round(launches_per_step * args.steps * n_images))
 
     if rank == 0 and world_eff == 1 and not args.no_cpu_baseline:
         im = imgs[0]

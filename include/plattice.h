@@ -85,6 +85,24 @@ int plattice_backward(float* grad_values_out, const float* grad, const float* we
                       int lattice_state, void* scratch, size_t scratch_bytes, int pd, int vd,
                       int w, int h, void* stream);
 
+/* Batches: B images of one shape, [B][h][w][...] contiguous (features,
+ * values, outputs), in one call -- the dense-CRF use of many images.  The
+ * images' lattices lie one after the other in `lattice` (kept for the
+ * backward); one image-sized `scratch` serves them all, since the images run
+ * one after the other on `stream`.  Sizes from plattice_batch_workspace_sizes.
+ * The reference has no batch call (its callers loop over images in Python,
+ * permuto.cpp:71-158 per image).  plattice_backward_batch takes the same
+ * lattice_state values as plattice_backward, for all B images at once. */
+int plattice_batch_workspace_sizes(int b, int h, int w, int pd, int vd, size_t* lattice_bytes,
+                                   size_t* scratch_bytes);
+int plattice_forward_batch(float* weight_out, float* out, const float* values, const float* features,
+                           void* lattice, size_t lattice_bytes, void* scratch, size_t scratch_bytes,
+                           int b, int pd, int vd, int w, int h, void* stream);
+int plattice_backward_batch(float* grad_values_out, const float* grad, const float* weight_in,
+                            const float* features, void* lattice, size_t lattice_bytes,
+                            int lattice_state, void* scratch, size_t scratch_bytes, int b, int pd,
+                            int vd, int w, int h, void* stream);
+
 /* Kept lattice: filter further value tensors on the lattice that a
  * plattice_forward call built (same h, w, pd; any vd), without rebuilding it
  * -- e.g. the iterations of a mean-field CRF.  No counterpart in the

@@ -27,7 +27,8 @@ import torch
 from . import _lib
 
 __all__ = ["forward", "backward", "Lattice", "lattice_forward", "lattice_backward",
-           "lattice_filter", "lattice_filter_backward", "lattice_info", "vertex_keys"]
+           "lattice_filter", "lattice_filter_backward", "BatchLattice", "batch_forward",
+           "batch_backward", "forward_batch", "backward_batch", "lattice_info", "vertex_keys"]
 
 _CHECK = os.environ.get("PLATTICE_CHECK", "0") not in ("", "0")
 
@@ -236,6 +237,128 @@ def lattice_filter_backward(lattice, grad_values, weight_saved):
         if _CHECK and h * w > 0:
             _sync_check(lattice, "plattice_filter_backward")
     return out
+
+
+class BatchLattice:
+    """The lattices of a batch of images built by :func:`batch_forward`, kept
+    for the batch's backward (one buffer, one lattice per image)."""
+
+    __slots__ = ("buf", "shape", "vd", "device", "used", "_feat_ref", "_feat_version", "_feat_ptr",
+                 "__weakref__")
+
+    def __init__(self, features, vd, buf):
+        self.buf = buf
+        self.shape = tuple(int(s) for s in features.shape)
+        self.vd = int(vd)
+        self.device = features.device
+        self.used = False
+        self._feat_ref = weakref.ref(features)
+        self._feat_version = features._version
+        self._feat_ptr = features.data_ptr()
+
+    def matches(self, features, vd, same_object=True):
+        if same_object and self._feat_ref() is not features:
+            return False
+        return (features.data_ptr() == self._feat_ptr and int(vd) == self.vd
+                and tuple(features.shape) == self.shape and features.device == self.device
+                and (not same_object or features._version == self._feat_version))
+
+
+def _check_batch(features, t, name):
+    _check_input(features, "features")
+    _check_input(t, name)
+    _require(features.dim() == 4, "features must be [B, H, W, pd]")
+    _require(t.dim() == 4, f"{name} must be [B, H, W, vd]")
+    _require(features.dtype == torch.float32, "features must be float32")
+    _require(t.dtype == torch.float32, f"{name} must be float32")
+    _require(tuple(features.shape[:3]) == tuple(t.shape[:3]), f"features and {name} must have matching B, H, W")
+    _require(t.device == features.device, f"features and {name} must be on the same device")
+    b, h, w, pd = (int(x) for x in features.shape)
+    vd = int(t.shape[3])
+    _check_dims(pd, vd)
+    return b, h, w, pd, vd
+
+
+def batch_forward(features, values):
+    """Forward filter of B images in one call, each image on its own lattice:
+    ``features [B,H,W,pd]``, ``values [B,H,W,vd]`` -> ``(weight [B,H,W,1],
+    out [B,H,W,vd], BatchLattice)``; the same per image as :func:`lattice_forward`."""
+    b, h, w, pd, vd = _check_batch(features, values, "values")
+    dev = features.device
+    with torch.cuda.device(dev):
+        out = torch.empty((b, h, w, vd), dtype=torch.float32, device=dev)
+        weight = torch.empty((b, h, w, 1), dtype=torch.float32, device=dev)
+        lb, sb = _lib.batch_workspace_sizes(b, h, w, pd, vd)
+        buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+        scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+        rc = _lib.lib().plattice_forward_batch(_ptr(weight), _ptr(out), _ptr(values), _ptr(features), _ptr(buf),
+                                               lb, _ptr(scratch), sb, b, pd, vd, w, h, _stream(dev))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError("plattice_forward_batch", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
+        lat = BatchLattice(features, vd, buf)
+        if _CHECK and b * h * w > 0:
+            _sync_check_batch(lat, b, h, w, pd, "plattice_forward_batch")
+    return weight, out, lat
+
+
+def batch_backward(features, grad_values, weight_saved, lattice=None, saved=False):
+    """Value gradient of :func:`batch_forward`; reuses ``lattice`` when it was
+    built from ``features`` as they are now, else rebuilds every image."""
+    b, h, w, pd, vd = _check_batch(features, grad_values, "grad_values")
+    _check_input(weight_saved, "weight_saved")
+    _require(tuple(weight_saved.shape) == (b, h, w, 1), "weight_saved must be [B, H, W, 1]")
+    _require(weight_saved.dtype == torch.float32, "weight_saved must be float32")
+    dev = features.device
+    with torch.cuda.device(dev):
+        out = torch.empty((b, h, w, vd), dtype=torch.float32, device=dev)
+        lb, sb = _lib.batch_workspace_sizes(b, h, w, pd, vd)
+        if lattice is not None and lattice.matches(features, vd, same_object=not saved):
+            state = 2 if lattice.used else 1
+            buf, scratch, sbytes = lattice.buf, None, 0
+        else:
+            state = 0
+            lattice = None
+            buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+            scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+            sbytes = sb
+        rc = _lib.lib().plattice_backward_batch(_ptr(out), _ptr(grad_values), _ptr(weight_saved),
+                                                _ptr(features), _ptr(buf), lb, state, _ptr(scratch), sbytes,
+                                                b, pd, vd, w, h, _stream(dev))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError("plattice_backward_batch", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
+        if lattice is not None:
+            lattice.used = True
+        if _CHECK and b * h * w > 0:
+            _sync_check_batch(BatchLattice(features, vd, buf), b, h, w, pd, "plattice_backward_batch")
+    return out
+
+
+def _sync_check_batch(lat, b, h, w, pd, call):
+    lb, _ = _lib.workspace_sizes(h, w, pd, lat.vd)
+    stride = (lb + 255) & ~255
+    for i in range(b):
+        st = ctypes.c_int(0)
+        rc = _lib.lib().plattice_lattice_info(ctypes.c_void_p(lat.buf.data_ptr() + i * stride),
+                                              ctypes.byref(st), None, None, None, _stream(lat.device))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError(call, rc, f"image {i}: device status bits {st.value:#x}")
+
+
+# The most recent batch forward's lattices, for a standalone batch backward.
+_last_batch = None
+
+
+def forward_batch(features, values):
+    """``forward`` over ``[B,H,W,...]`` -> ``[weight [B,H,W,1], out [B,H,W,vd]]``."""
+    global _last_batch
+    weight, out, lat = batch_forward(features, values)
+    _last_batch = lat
+    return [weight, out]
+
+
+def backward_batch(features, grad_values, weight_saved):
+    """``backward`` over ``[B,H,W,...]``; reuses the last batch forward's lattices."""
+    return batch_backward(features, grad_values, weight_saved, _last_batch)
 
 
 # The most recent forward's lattice, for a standalone backward on the same

@@ -6,6 +6,8 @@ plattice.py (PermutoLatticeFunction, PermutoLattice).  The work is done by
 libplattice_b200.so through the C ABI of include/plattice.h.
 """
 from . import PLOO
-from .plattice import LatticeFilterFunction, PermutoLattice, PermutoLatticeFunction
+from .plattice import (LatticeFilterFunction, PermutoLattice, PermutoLatticeBatchFunction,
+                       PermutoLatticeFunction)
 
-__all__ = ["PLOO", "PermutoLattice", "PermutoLatticeFunction", "LatticeFilterFunction"]
+__all__ = ["PLOO", "PermutoLattice", "PermutoLatticeFunction", "PermutoLatticeBatchFunction",
+           "LatticeFilterFunction"]

@@ -61,6 +61,12 @@ def lib():
         L.plattice_forward.argtypes = [P, P, P, P, P, S, P, S, I, I, I, I, P]
         L.plattice_backward.restype = I
         L.plattice_backward.argtypes = [P, P, P, P, P, S, I, P, S, I, I, I, I, P]
+        L.plattice_batch_workspace_sizes.restype = I
+        L.plattice_batch_workspace_sizes.argtypes = [I, I, I, I, I, ctypes.POINTER(S), ctypes.POINTER(S)]
+        L.plattice_forward_batch.restype = I
+        L.plattice_forward_batch.argtypes = [P, P, P, P, P, S, P, S, I, I, I, I, I, P]
+        L.plattice_backward_batch.restype = I
+        L.plattice_backward_batch.argtypes = [P, P, P, P, P, S, I, P, S, I, I, I, I, I, P]
         L.plattice_filter_workspace_size.restype = I
         L.plattice_filter_workspace_size.argtypes = [I, I, I, I, ctypes.POINTER(S)]
         L.plattice_filter.restype = I
@@ -99,6 +105,14 @@ def workspace_sizes(h, w, pd, vd):
     rc = lib().plattice_workspace_sizes(h, w, pd, vd, ctypes.byref(lb), ctypes.byref(sb))
     if rc != OK:
         raise PlatticeError("plattice_workspace_sizes", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    return lb.value, sb.value
+
+
+def batch_workspace_sizes(b, h, w, pd, vd):
+    lb, sb = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    rc = lib().plattice_batch_workspace_sizes(b, h, w, pd, vd, ctypes.byref(lb), ctypes.byref(sb))
+    if rc != OK:
+        raise PlatticeError("plattice_batch_workspace_sizes", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
     return lb.value, sb.value
 
 

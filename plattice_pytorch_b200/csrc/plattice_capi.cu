@@ -266,6 +266,70 @@ int plattice_backward(float* grad_values_out, const float* grad, const float* we
     return cuda_status(dispatch_backward(a), "plattice_backward");
 }
 
+// ---------------------------------------------------------------- batches
+
+// B images of one shape: their lattices one after the other in `lattice`
+// (each lattice region padded to 256 bytes), one scratch region shared by
+// the images, which run one after the other on the caller's stream.
+static size_t batch_lattice_stride(const PlLayout& L) { return pl_align(L.lattice_bytes); }
+
+int plattice_batch_workspace_sizes(int b, int h, int w, int pd, int vd, size_t* lattice_bytes,
+                                   size_t* scratch_bytes) {
+    if (b < 0) return PLATTICE_ERR_INVALID;
+    size_t lb = 0, sb = 0;
+    const int rc = plattice_workspace_sizes(h, w, pd, vd, &lb, &sb);
+    if (rc != PLATTICE_OK) return rc;
+    if (lattice_bytes) *lattice_bytes = pl_align(lb) * (size_t)(b > 0 ? b : 1);
+    if (scratch_bytes) *scratch_bytes = sb;
+    return PLATTICE_OK;
+}
+
+int plattice_forward_batch(float* weight_out, float* out, const float* values, const float* features,
+                           void* lattice, size_t lattice_bytes, void* scratch, size_t scratch_bytes, int b,
+                           int pd, int vd, int w, int h, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (b < 0) return PLATTICE_ERR_INVALID;
+    if (b == 0 || h == 0 || w == 0) return PLATTICE_OK;
+    if (!weight_out || !out || !values || !features || !lattice || !scratch) return PLATTICE_ERR_INVALID;
+    PlLayout L;
+    pl_layout(&L, h, w, pd, vd);
+    const size_t stride = batch_lattice_stride(L);
+    if (lattice_bytes < stride * (size_t)b || scratch_bytes < L.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
+    const size_t n = (size_t)h * w;
+    for (int i = 0; i < b; ++i) {
+        rc = plattice_forward(weight_out + i * n, out + i * n * vd, values + i * n * vd, features + i * n * pd,
+                              static_cast<char*>(lattice) + i * stride, stride, scratch, scratch_bytes, pd, vd, w,
+                              h, stream);
+        if (rc != PLATTICE_OK) return rc;
+    }
+    return PLATTICE_OK;
+}
+
+int plattice_backward_batch(float* grad_values_out, const float* grad, const float* weight_in, const float* features,
+                            void* lattice, size_t lattice_bytes, int lattice_state, void* scratch,
+                            size_t scratch_bytes, int b, int pd, int vd, int w, int h, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (b < 0 || lattice_state < 0 || lattice_state > 2) return PLATTICE_ERR_INVALID;
+    if (b == 0 || h == 0 || w == 0) return PLATTICE_OK;
+    if (!grad_values_out || !grad || !weight_in || !lattice) return PLATTICE_ERR_INVALID;
+    if (lattice_state == 0 && (!scratch || !features)) return PLATTICE_ERR_INVALID;
+    PlLayout L;
+    pl_layout(&L, h, w, pd, vd);
+    const size_t stride = batch_lattice_stride(L);
+    if (lattice_bytes < stride * (size_t)b) return PLATTICE_ERR_WORKSPACE;
+    if (lattice_state == 0 && scratch_bytes < L.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
+    const size_t n = (size_t)h * w;
+    for (int i = 0; i < b; ++i) {
+        rc = plattice_backward(grad_values_out + i * n * vd, grad + i * n * vd, weight_in + i * n,
+                               features ? features + i * n * pd : nullptr, static_cast<char*>(lattice) + i * stride,
+                               stride, lattice_state, scratch, scratch_bytes, pd, vd, w, h, stream);
+        if (rc != PLATTICE_OK) return rc;
+    }
+    return PLATTICE_OK;
+}
+
 // ---------------------------------------------------------------- kept lattice
 
 // Value rows of a filter call: two buffers of slots x pad(vd+1) floats.

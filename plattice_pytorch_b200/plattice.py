@@ -8,6 +8,10 @@ reference (plattice.py:19).  ``PermutoLattice`` is the nn.Module wrapper.
 Unlike the reference, the lattice that forward builds is kept on the autograd
 context and reused by backward (no rebuild).
 
+``PermutoLatticeBatchFunction`` (no counterpart in the reference) is
+``PermutoLatticeFunction`` over a batch ``[B,H,W,...]`` in one library call,
+one lattice per image.
+
 ``LatticeFilterFunction`` (no counterpart in the reference) filters further
 values on a kept lattice -- the ``PLOO.Lattice`` of an earlier forward on the
 same features -- without rebuilding it, as the iterations of a mean-field CRF
@@ -20,7 +24,7 @@ from torch.nn import Module
 
 from . import PLOO
 
-__all__ = ["PermutoLatticeFunction", "PermutoLattice", "LatticeFilterFunction"]
+__all__ = ["PermutoLatticeFunction", "PermutoLattice", "LatticeFilterFunction", "PermutoLatticeBatchFunction"]
 
 
 class PermutoLatticeFunction(Function):
@@ -61,3 +65,22 @@ class LatticeFilterFunction(Function):
     def backward(ctx, grad_output):
         (weight,) = ctx.saved_tensors
         return PLOO.lattice_filter_backward(ctx.lattice, grad_output.contiguous(), weight), None
+
+
+class PermutoLatticeBatchFunction(Function):
+    """``PermutoLatticeBatchFunction.apply(features [B,H,W,pd], values [B,H,W,vd])``."""
+
+    @staticmethod
+    def forward(ctx, feature, values):
+        weight, out, lat = PLOO.batch_forward(feature, values)
+        ctx.save_for_backward(weight, feature)
+        ctx.lattice = lat
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        weight, feature = ctx.saved_tensors
+        grad_values = PLOO.batch_backward(feature, grad_output.contiguous(), weight,
+                                          getattr(ctx, "lattice", None), saved=True)
+        return None, grad_values

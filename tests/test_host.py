@@ -86,6 +86,27 @@ def test_kept_lattice_sizes_and_argument_checks(lib):
                                  None) == _lib.ERR_INVALID
 
 
+def test_batch_sizes_and_argument_checks(lib):
+    from plattice_pytorch_b200 import _lib
+    lb, sb = _lib.workspace_sizes(512, 512, 5, 3)
+    blb, bsb = _lib.batch_workspace_sizes(64, 512, 512, 5, 3)
+    assert blb == 64 * ((lb + 255) // 256 * 256) and bsb == sb   # lattices kept per image, scratch shared
+    with pytest.raises(_lib.PlatticeError):
+        _lib.batch_workspace_sizes(-1, 8, 8, 5, 3)
+    fake = ctypes.c_void_p(256)
+    assert lib.plattice_forward_batch(fake, fake, fake, fake, fake, blb, fake, bsb, -2, 5, 3, 8, 8,
+                                      None) == _lib.ERR_INVALID
+    assert lib.plattice_forward_batch(fake, fake, fake, fake, fake, blb, fake, bsb, 3, 0, 3, 8, 8,
+                                      None) == _lib.ERR_INVALID
+    lb8, sb8 = _lib.batch_workspace_sizes(3, 8, 8, 5, 3)
+    assert lib.plattice_forward_batch(fake, fake, fake, fake, fake, lb8 - 1, fake, sb8, 3, 5, 3, 8, 8,
+                                      None) == _lib.ERR_WORKSPACE
+    assert lib.plattice_backward_batch(fake, fake, fake, None, fake, lb8, 0, fake, sb8, 3, 5, 3, 8, 8,
+                                       None) == _lib.ERR_INVALID
+    assert lib.plattice_forward_batch(None, None, None, None, None, 0, None, 0, 0, 5, 3, 8, 8,
+                                      None) == _lib.OK   # an empty batch is a no-op
+
+
 def test_python_checks_raise_reference_messages():
     from plattice_pytorch_b200 import PLOO
     f = torch.zeros(4, 4, 5)
@@ -96,6 +117,8 @@ def test_python_checks_raise_reference_messages():
         PLOO.backward(f, v, torch.zeros(4, 4, 1))
     with pytest.raises(RuntimeError, match="lattice must be a Lattice"):
         PLOO.lattice_filter(object(), v)
+    with pytest.raises(RuntimeError, match="features must be CUDA"):
+        PLOO.forward_batch(torch.zeros(2, 4, 4, 5), torch.zeros(2, 4, 4, 3))
 
 
 def _free_port():
