@@ -50,6 +50,8 @@ def lib():
         L.po_forward.restype = Lg
         L.po_backward.argtypes = [P, P, P, Lg, I, I, I, P]
         L.po_backward.restype = Lg
+        L.po_feature_grad.argtypes = [P, P, P, Lg, I, I, I, P]
+        L.po_feature_grad.restype = Lg
         L.po_brute_gaussian.argtypes = [P, P, P, Lg, I, I, Lg, Lg, I, I, P]
         L.po_brute_gaussian.restype = I
         L.po_scale_factors_out.argtypes = [I, P]
@@ -115,6 +117,21 @@ def forward(features, values, variant=DEFAULT_VARIANT):
     if m < 0:
         raise ValueError(f"po_forward failed with status {-m}")
     return wo, out, int(m)
+
+
+def feature_grad(features, values, grad, variant=DEFAULT_VARIANT):
+    """Gradient ``[..., pd]`` of ``sum(grad * forward(features, values).out)``
+    with respect to the features (the reference provides none); see
+    po_feature_grad in plattice_oracle.c."""
+    f, n, pd = _dims(features)
+    v = _f32(values)
+    g = _f32(grad)
+    vd = v.shape[-1]
+    out = np.zeros(f.shape, np.float32)
+    m = lib().po_feature_grad(_ptr(f), _ptr(v), _ptr(g), n, pd, vd, variant, _ptr(out))
+    if m < 0:
+        raise ValueError(f"po_feature_grad failed with status {-m}")
+    return out.reshape(np.shape(features))
 
 
 def backward(features, grad, weight, variant=DEFAULT_VARIANT):

@@ -28,6 +28,14 @@
  * the candidates and is pinned against golden vectors produced by the
  * reference build itself (tests/golden).
  *
+ * Also here: the gradient of the forward filter with respect to the features
+ * (the reference returns none, plattice.py:19), derived from the forward above:
+ * the features enter only through the barycentric weights (the vertex
+ * assignment is piecewise constant), so with R = blurred lattice values,
+ * Z_p = the normaliser, G_p = dL/dout_p and H = B^T S'(G/Z, -(G.out)/Z):
+ *   dL/dw_pc = (G_p . R[v][0:V] - (G_p . out_p) R[v][V]) / Z_p + H[v] . (val_p, 1),
+ *   dL/de_i(r) = (dL/dw_{pd-r} - dL/dw_{(pd+1-r) mod K}) / K   (i(r): coordinate of rank r),
+ * and dL/df through the elevation recurrence of permutohedral.cu:165-173.
  * Also here: a brute-force dense Gaussian filter out_p = sum_q g_pq v_q /
  * sum_q g_pq with g_pq = exp(-|f_p - f_q|^2 / 2), the generalisation to any
  * features of the reference test's brute_force_bilateral
@@ -77,7 +85,7 @@ static int po_f2s16(float x) {
  * each, the (pd+1)-th is implied by the zero sum) and K barycentric weights.
  * permutohedral.cu:165-250 */
 static void po_embed(const float* f, int pd, const float* sf, int var,
-                     int16_t* keys /* [K][pd] */, float* w /* [K] */) {
+                     int16_t* keys /* [K][pd] */, float* w /* [K] */, int* rank_out /* [K] or NULL */) {
     const int K = pd + 1;
     float e[PO_MAX_PD + 1];
     int g[PO_MAX_PD + 1];
@@ -163,6 +171,8 @@ static void po_embed(const float* f, int pd, const float* sf, int var,
         }
         w[c] = b[c];
     }
+    if (rank_out)
+        for (int i = 0; i <= pd; i++) rank_out[i] = rank[i];
 }
 
 /* ------------------------------------------------------------------------ */
@@ -251,7 +261,7 @@ static int po_lattice_build(po_lattice* L, const float* feat, long n, int pd, in
     if (!L->slot_vid || !L->slot_w) return PO_ENOMEM;
     if (po_table_init(&L->tab, pd, n * K + 1) != PO_OK) return PO_ENOMEM;
     for (long p = 0; p < n; p++) {
-        po_embed(feat + (size_t)p * pd, pd, sf, var, keys, w);
+        po_embed(feat + (size_t)p * pd, pd, sf, var, keys, w, NULL);
         for (int c = 0; c < K; c++) {
             L->slot_vid[p * K + c] = (int32_t)po_table_find(&L->tab, keys + c * pd, 1);
             L->slot_w[p * K + c] = w[c];
@@ -323,7 +333,7 @@ int po_embed_all(const float* feat, long n, int pd, int var, int16_t* keys, floa
     float sf[PO_MAX_PD];
     po_scale_factors(pd, sf);
     for (long p = 0; p < n; p++)
-        po_embed(feat + (size_t)p * pd, pd, sf, var, keys + (size_t)p * K * pd, w + (size_t)p * K);
+        po_embed(feat + (size_t)p * pd, pd, sf, var, keys + (size_t)p * K * pd, w + (size_t)p * K, NULL);
     return PO_OK;
 }
 
@@ -418,6 +428,122 @@ long po_backward(const float* feat, const float* grad, const float* weight_in, l
     }
     long m = L.m;
     free(acc); free(x); free(y); po_lattice_free(&L);
+    return m;
+}
+
+/* one [1 2 1]/4 pass in double (the gradient's lattice sweeps) */
+static double* po_blur_d(const po_lattice* L, int C, double* x, double* y, int reverse) {
+    const int K = L->pd + 1;
+    for (int s = 0; s < K; s++) {
+        const int c = reverse ? (K - 1 - s) : s;
+        for (long v = 0; v < L->m; v++) {
+            const int32_t a = L->nbr[(v * K + c) * 2 + 0], b = L->nbr[(v * K + c) * 2 + 1];
+            for (int j = 0; j < C; j++) {
+                double acc = 2.0 * x[v * C + j];
+                if (a >= 0) acc += x[(long)a * C + j];
+                if (b >= 0) acc += x[(long)b * C + j];
+                y[v * C + j] = 0.25 * acc;
+            }
+        }
+        double* t = x; x = y; y = t;
+    }
+    return x;
+}
+
+/* Feature gradient dL/df [n][pd] of L = sum_p grad_p . out_p, out = the
+ * forward filter of (features, values).  Lattice sweeps in double; the
+ * forward lattice values as po_forward computes them.  Returns m or -status. */
+long po_feature_grad(const float* feat, const float* vals, const float* grad, long n, int pd, int vd, int var,
+                     float* grad_feat) {
+    if (pd < 1 || pd > PO_MAX_PD || vd < 1 || vd > 8 || n < 0) return -PO_EINVAL;
+    const int K = pd + 1, C = vd + 1;
+    po_lattice L;
+    if (po_lattice_build(&L, feat, n, pd, var) != PO_OK) { po_lattice_free(&L); return -PO_ENOMEM; }
+    const size_t mc = (size_t)L.m * C + 1;
+    double* acc = (double*)calloc(mc, sizeof(double));
+    float* x = (float*)malloc(mc * sizeof(float));
+    float* y = (float*)malloc(mc * sizeof(float));
+    double* hx = (double*)calloc(mc, sizeof(double));
+    double* hy = (double*)malloc(mc * sizeof(double));
+    double* zp = (double*)malloc(((size_t)n + 1) * sizeof(double));
+    double* go = (double*)malloc(((size_t)n + 1) * sizeof(double));   /* G_p . out_p */
+    if (!acc || !x || !y || !hx || !hy || !zp || !go) {
+        free(acc); free(x); free(y); free(hx); free(hy); free(zp); free(go); po_lattice_free(&L);
+        return -PO_ENOMEM;
+    }
+    /* forward lattice values R, as po_forward */
+    for (long p = 0; p < n; p++)
+        for (int c = 0; c < K; c++) {
+            long v = L.slot_vid[p * K + c];
+            float w = L.slot_w[p * K + c];
+            for (int j = 0; j < vd; j++) acc[v * C + j] += (double)(vals[p * vd + j] * w);
+            acc[v * C + vd] += (double)w;
+        }
+    for (size_t i = 0; i + 1 < mc; i++) x[i] = (float)acc[i];
+    const float* R = po_blur(&L, C, x, y, 0);
+    /* per pixel: Z, out, G.out; splat of d_p = (G/Z, -(G.out)/Z) */
+    for (long p = 0; p < n; p++) {
+        double a[8] = {0}, z = 0.0;
+        for (int c = 0; c < K; c++) {
+            long v = L.slot_vid[p * K + c];
+            double w = L.slot_w[p * K + c];
+            for (int j = 0; j < vd; j++) a[j] += w * R[v * C + j];
+            z += w * R[v * C + vd];
+        }
+        double gdot = 0.0;
+        for (int j = 0; j < vd; j++) gdot += (double)grad[p * vd + j] * (a[j] / z);
+        zp[p] = z;
+        go[p] = gdot;
+        for (int c = 0; c < K; c++) {
+            long v = L.slot_vid[p * K + c];
+            double w = L.slot_w[p * K + c];
+            for (int j = 0; j < vd; j++) hx[v * C + j] += w * (double)grad[p * vd + j] / z;
+            hx[v * C + vd] -= w * gdot / z;
+        }
+    }
+    const double* H = po_blur_d(&L, C, hx, hy, 1);
+    /* per pixel: dL/dw, then dL/de by rank, then dL/df through the elevation */
+    float sf[PO_MAX_PD];
+    po_scale_factors(pd, sf);
+    int16_t keys[(PO_MAX_PD + 1) * PO_MAX_PD];
+    float wt[PO_MAX_PD + 1];
+    int rank[PO_MAX_PD + 1], coord_of_rank[PO_MAX_PD + 1];
+    for (long p = 0; p < n; p++) {
+        po_embed(feat + (size_t)p * pd, pd, sf, var, keys, wt, rank);
+        for (int i = 0; i < K; i++) coord_of_rank[rank[i]] = i;
+        double dw[PO_MAX_PD + 1];
+        for (int c = 0; c < K; c++) {
+            long v = L.slot_vid[p * K + c];
+            double sl = 0.0, sp = H[v * C + vd];
+            for (int j = 0; j < vd; j++) {
+                sl += (double)grad[p * vd + j] * R[v * C + j];
+                sp += H[v * C + j] * (double)vals[p * vd + j];
+            }
+            sl = (sl - go[p] * R[v * C + vd]) / zp[p];
+            dw[c] = sl + sp;
+        }
+        double de[PO_MAX_PD + 1];
+        for (int r = 0; r < K; r++)
+            de[coord_of_rank[r]] = (dw[pd - r] - dw[(pd + 1 - r) % K]) / (double)K;
+        /* elevation: e[pd] = -pd f[pd-1] sf[pd-1]; e[i] = e[i+1] - i f[i-1] sf[i-1]
+         * + (i+2) f[i] sf[i]; e[0] = e[1] + 2 f[0] sf[0] (permutohedral.cu:166-173) */
+        double gf[PO_MAX_PD] = {0};
+        double carry = 0.0;   /* dL/de[i] accumulated down the recurrence */
+        for (int i = 0; i <= pd; i++) {
+            carry += de[i];
+            if (i == 0) {
+                gf[0] += 2.0 * sf[0] * carry;
+            } else if (i < pd) {
+                gf[i - 1] -= (double)i * sf[i - 1] * carry;
+                gf[i] += (double)(i + 2) * sf[i] * carry;
+            } else {
+                gf[pd - 1] -= (double)pd * sf[pd - 1] * carry;
+            }
+        }
+        for (int i = 0; i < pd; i++) grad_feat[(size_t)p * pd + i] = (float)gf[i];
+    }
+    long m = L.m;
+    free(acc); free(x); free(y); free(hx); free(hy); free(zp); free(go); po_lattice_free(&L);
     return m;
 }
 

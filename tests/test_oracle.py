@@ -129,3 +129,41 @@ def test_collapsed_features_have_pd_plus_one_vertices():
     f[..., 0], f[..., 1] = 0.3, 0.7
     vk, _ = oracle.vertex_keys(f)
     assert vk.shape[0] == 3
+
+
+def _loss(f, v, g):
+    _, out, _ = oracle.forward(f, v)
+    return float(np.sum(out.astype(np.float64) * g))
+
+
+@pytest.mark.parametrize("pd,vd,seed", [(2, 3, 0), (3, 2, 1), (5, 3, 2), (8, 1, 3)])
+def test_feature_gradient_matches_finite_differences(pd, vd, seed):
+    """The oracle's analytic feature gradient equals central differences of
+    its own forward, coordinate by coordinate.  The filter is linear in the
+    features while no pixel changes simplex, so a perturbation that leaves the
+    pixel's vertex keys unchanged gives the exact slope up to float rounding;
+    the rare perturbations that cross a simplex boundary are skipped."""
+    rng = np.random.default_rng(seed)
+    h, w = 6, 7
+    f = (rng.normal(size=(h, w, pd)) * 0.4).astype(np.float32)   # dense: pixels share vertices
+    v = rng.uniform(0.1, 1.0, size=(h, w, vd)).astype(np.float32)
+    g = rng.normal(size=(h, w, vd)).astype(np.float32)
+    gf = oracle.feature_grad(f, v, g)
+    eps = 1e-2
+    checked = 0
+    for y in range(h):
+        for x in range(w):
+            k0, _ = oracle.embed(f[y:y + 1, x:x + 1])
+            for i in range(pd):
+                fp, fm = f.copy(), f.copy()
+                fp[y, x, i] += eps
+                fm[y, x, i] -= eps
+                kp, _ = oracle.embed(fp[y:y + 1, x:x + 1])
+                km, _ = oracle.embed(fm[y:y + 1, x:x + 1])
+                if not (np.array_equal(kp, k0) and np.array_equal(km, k0)):
+                    continue   # the pixel changes simplex inside the interval
+                fd = (_loss(fp, v, g) - _loss(fm, v, g)) / (2 * eps)
+                assert abs(fd - gf[y, x, i]) <= 2e-3 + 1e-2 * abs(fd), (y, x, i, fd, gf[y, x, i])
+                checked += 1
+    assert checked >= 0.8 * h * w * pd
+    assert np.mean(np.abs(gf) > 1e-3) > 0.5   # most slopes are non-zero: the check has teeth
