@@ -126,6 +126,21 @@ int plattice_filter_backward(float* grad_values_out, const float* grad, const fl
                              void* lattice, size_t lattice_bytes, void* values_ws,
                              size_t values_ws_bytes, int pd, int vd, int w, int h, void* stream);
 
+/* Gradient of the forward filter with respect to the features (no
+ * counterpart in the reference, whose Function returns None for them,
+ * plattice.py:19): grad_features_out [h][w][pd] = dL/dfeatures for
+ * dL/dout = `grad`, given the forward's `out` and `weight` (weight_out) on
+ * `values`, and `lattice` as that forward on `features` left it.  The slope
+ * is that of the piecewise-linear filter inside each pixel's simplex (the
+ * vertex assignment is piecewise constant).  `ws`:
+ * plattice_feature_grad_workspace_size bytes.  Updates lattice header
+ * bookkeeping like plattice_filter (one stream per lattice). */
+int plattice_feature_grad_workspace_size(int h, int w, int pd, int vd, size_t* bytes);
+int plattice_feature_grad(float* grad_features_out, const float* grad, const float* out,
+                          const float* weight, const float* values, const float* features,
+                          void* lattice, size_t lattice_bytes, void* ws, size_t ws_bytes, int pd,
+                          int vd, int w, int h, void* stream);
+
 /* Synchronises `stream` and reads the lattice header: device status bits,
  * vertex count m, number of tile-unique keys staged, log2 of the hash-table
  * capacity used.  Any pointer may be NULL.  Returns PLATTICE_ERR_DEVICE when

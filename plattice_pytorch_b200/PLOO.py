@@ -27,7 +27,7 @@ import torch
 from . import _lib
 
 __all__ = ["forward", "backward", "Lattice", "lattice_forward", "lattice_backward",
-           "lattice_filter", "lattice_filter_backward", "BatchLattice", "batch_forward",
+           "lattice_filter", "lattice_filter_backward", "feature_grad", "BatchLattice", "batch_forward",
            "batch_backward", "forward_batch", "backward_batch", "lattice_info", "vertex_keys"]
 
 _CHECK = os.environ.get("PLATTICE_CHECK", "0") not in ("", "0")
@@ -237,6 +237,36 @@ def lattice_filter_backward(lattice, grad_values, weight_saved):
         if _CHECK and h * w > 0:
             _sync_check(lattice, "plattice_filter_backward")
     return out
+
+
+def feature_grad(lattice, features, values, grad_out, weight, out):
+    """Gradient ``[H,W,pd]`` of the forward filter with respect to ``features``
+    for ``dL/dout = grad_out``, given the forward's ``weight`` and ``out`` on
+    ``values`` and ``lattice``, the Lattice that forward built from ``features``
+    (the reference returns no feature gradient).  The slope is that of the
+    piecewise-linear filter inside each pixel's simplex."""
+    _require(isinstance(lattice, Lattice), "lattice must be a Lattice from lattice_forward")
+    _require(lattice.matches(features, lattice.vd, same_object=False),
+             "lattice was not built from these features")
+    for t, name in ((values, "values"), (grad_out, "grad_out"), (out, "out")):
+        vd = _check_kept(lattice, t, name)
+    _require(int(values.shape[2]) == int(grad_out.shape[2]) == int(out.shape[2]),
+             "values, grad_out and out must have the same vd")
+    _check_input(weight, "weight")
+    _require(tuple(weight.shape) == (lattice.h, lattice.w, 1), "weight must be [H, W, 1]")
+    h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
+    with torch.cuda.device(dev):
+        gf = torch.empty((h, w, pd), dtype=torch.float32, device=dev)
+        wsb = _lib.feature_grad_workspace_size(h, w, pd, vd)
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        rc = _lib.lib().plattice_feature_grad(_ptr(gf), _ptr(grad_out), _ptr(out), _ptr(weight), _ptr(values),
+                                              _ptr(features), _ptr(lattice.buf), lattice.buf.numel(), _ptr(ws),
+                                              wsb, pd, vd, w, h, _stream(dev))
+        if rc != _lib.OK:
+            raise _lib.PlatticeError("plattice_feature_grad", rc, f"h={h} w={w} pd={pd} vd={vd}")
+        if _CHECK and h * w > 0:
+            _sync_check(lattice, "plattice_feature_grad")
+    return gf
 
 
 class BatchLattice:

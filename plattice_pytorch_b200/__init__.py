@@ -7,7 +7,7 @@ libplattice_b200.so through the C ABI of include/plattice.h.
 """
 from . import PLOO
 from .plattice import (LatticeFilterFunction, PermutoLattice, PermutoLatticeBatchFunction,
-                       PermutoLatticeFunction)
+                       PermutoLatticeFeatureFunction, PermutoLatticeFunction)
 
 __all__ = ["PLOO", "PermutoLattice", "PermutoLatticeFunction", "PermutoLatticeBatchFunction",
-           "LatticeFilterFunction"]
+           "PermutoLatticeFeatureFunction", "LatticeFilterFunction"]

@@ -67,6 +67,10 @@ def lib():
         L.plattice_forward_batch.argtypes = [P, P, P, P, P, S, P, S, I, I, I, I, I, P]
         L.plattice_backward_batch.restype = I
         L.plattice_backward_batch.argtypes = [P, P, P, P, P, S, I, P, S, I, I, I, I, I, P]
+        L.plattice_feature_grad_workspace_size.restype = I
+        L.plattice_feature_grad_workspace_size.argtypes = [I, I, I, I, ctypes.POINTER(S)]
+        L.plattice_feature_grad.restype = I
+        L.plattice_feature_grad.argtypes = [P, P, P, P, P, P, P, S, P, S, I, I, I, I, P]
         L.plattice_filter_workspace_size.restype = I
         L.plattice_filter_workspace_size.argtypes = [I, I, I, I, ctypes.POINTER(S)]
         L.plattice_filter.restype = I
@@ -114,6 +118,14 @@ def batch_workspace_sizes(b, h, w, pd, vd):
     if rc != OK:
         raise PlatticeError("plattice_batch_workspace_sizes", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
     return lb.value, sb.value
+
+
+def feature_grad_workspace_size(h, w, pd, vd):
+    b = ctypes.c_size_t(0)
+    rc = lib().plattice_feature_grad_workspace_size(h, w, pd, vd, ctypes.byref(b))
+    if rc != OK:
+        raise PlatticeError("plattice_feature_grad_workspace_size", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    return b.value
 
 
 def filter_workspace_size(h, w, pd, vd):

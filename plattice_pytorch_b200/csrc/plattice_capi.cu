@@ -15,6 +15,7 @@ namespace pl {
     extern template cudaError_t run_forward<N>(const CallArgs&);                             \
     extern template cudaError_t run_backward<N>(const CallArgs&);                            \
     extern template cudaError_t run_filter<N>(const CallArgs&);                              \
+    extern template cudaError_t run_feature_grad<N>(const CallArgs&);                        \
     extern template cudaError_t run_export_keys<N>(const void*, const void*, const PlLayout&, \
                                                    int16_t*, int, cudaStream_t);
 PL_DECLARE_PD(1) PL_DECLARE_PD(2) PL_DECLARE_PD(3) PL_DECLARE_PD(4)
@@ -144,6 +145,12 @@ static cudaError_t dispatch_filter(const pl::CallArgs& a) {
 #define PL_FIL(N) pl::run_filter<N>(a)
     PL_PD_SWITCH(a.lay.pd, PL_FIL)
 #undef PL_FIL
+}
+
+static cudaError_t dispatch_feature_grad(const pl::CallArgs& a) {
+#define PL_FG(N) pl::run_feature_grad<N>(a)
+    PL_PD_SWITCH(a.lay.pd, PL_FG)
+#undef PL_FG
 }
 
 static cudaError_t dispatch_backward(const pl::CallArgs& a) {
@@ -398,6 +405,73 @@ int plattice_filter_backward(float* grad_values_out, const float* grad, const fl
     a.lattice = lattice;
     a.lattice_state = 2;   // kept lattice: zero the value rows, no rebuild
     return cuda_status(dispatch_backward(a), "plattice_filter_backward");
+}
+
+// ---------------------------------------------------------------- feature gradient
+
+// Workspace: two result flags, four lattice row buffers (R and H, ping-pong)
+// of slots x pad(vd+1) floats, and the per-pixel (G, -G.out) rows.
+struct FgradWs {
+    size_t flags, r0, r1, h0, h1, ev, total;
+};
+
+static FgradWs fgrad_ws(const PlLayout& L) {
+    FgradWs W;
+    const size_t rows = pl_align((size_t)L.slots * (size_t)L.CPf * 4);
+    W.flags = 0;
+    W.r0 = 256;
+    W.r1 = W.r0 + rows;
+    W.h0 = W.r1 + rows;
+    W.h1 = W.h0 + rows;
+    W.ev = W.h1 + rows;
+    W.total = W.ev + pl_align((size_t)L.h * L.w * (size_t)(L.vd + 1) * 4);
+    return W;
+}
+
+int plattice_feature_grad_workspace_size(int h, int w, int pd, int vd, size_t* bytes) {
+    const int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (!bytes) return PLATTICE_ERR_INVALID;
+    *bytes = 256;
+    if (h > 0 && w > 0) {
+        PlLayout L;
+        pl_layout(&L, h, w, pd, vd);
+        *bytes = fgrad_ws(L).total;
+    }
+    return PLATTICE_OK;
+}
+
+int plattice_feature_grad(float* grad_features_out, const float* grad, const float* out, const float* weight,
+                          const float* values, const float* features, void* lattice, size_t lattice_bytes,
+                          void* ws, size_t ws_bytes, int pd, int vd, int w, int h, void* stream) {
+    int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (h == 0 || w == 0) return PLATTICE_OK;
+    if (!grad_features_out || !grad || !out || !weight || !values || !features || !lattice || !ws)
+        return PLATTICE_ERR_INVALID;
+    pl::CallArgs a = {};
+    pl_layout(&a.lay, h, w, pd, vd);
+    if (lattice_bytes < a.lay.off_vb0) return PLATTICE_ERR_WORKSPACE;
+    const FgradWs W = fgrad_ws(a.lay);
+    if (ws_bytes < W.total) return PLATTICE_ERR_WORKSPACE;
+    char* b = static_cast<char*>(ws);
+    a.flags = reinterpret_cast<int*>(b + W.flags);
+    a.vbuf0 = reinterpret_cast<float*>(b + W.r0);
+    a.vbuf1 = reinterpret_cast<float*>(b + W.r1);
+    a.hbuf0 = reinterpret_cast<float*>(b + W.h0);
+    a.hbuf1 = reinterpret_cast<float*>(b + W.h1);
+    a.evec = reinterpret_cast<float*>(b + W.ev);
+    a.features = features;
+    a.values = values;
+    a.weight_in = weight;
+    a.grad_in = grad;
+    a.out_in = out;
+    a.out = grad_features_out;
+    a.lattice = lattice;
+    a.stream = static_cast<cudaStream_t>(stream);
+    a.sm_count = sm_count_current();
+    a.cap_override_log2 = g_cap_override_log2;
+    return cuda_status(dispatch_feature_grad(a), "plattice_feature_grad");
 }
 
 int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total, int* cap_log2, void* stream) {

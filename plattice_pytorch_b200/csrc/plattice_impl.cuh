@@ -26,6 +26,13 @@ struct CallArgs {
     int cap_override_log2;
     float* vbuf0;            // value buffers of a filter call on a kept lattice (else null:
     float* vbuf1;            // the forward's scratch rows / the lattice's backward rows)
+    // feature gradient: dL/dout, the forward's out, and lattice rows / flags in the workspace
+    const float* grad_in;
+    const float* out_in;
+    float* hbuf0;
+    float* hbuf1;
+    float* evec;
+    int* flags;
 };
 
 inline LatView lat_view(void* base, const PlLayout& L) {
@@ -168,7 +175,9 @@ cudaError_t neighbors_alongside(const CallArgs& a, const Geo& geo, const LatView
 constexpr int kCoopPerSm = 1;
 
 template <int PD, int CP>
-cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1, int reverse) {
+cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1, int reverse,
+                            int* final_flag = nullptr) {
+    if (!final_flag) final_flag = &Lv.hdr->blur_final;
     static int per_sm[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -183,7 +192,7 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
               e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), 0, a.stream, true, Lv, b0, b1,
-                             reverse));
+                           reverse, final_flag));
     return e;
 }
 
@@ -281,6 +290,41 @@ cudaError_t filter_v(const CallArgs& a) {
     return e;
 }
 
+// Gradient of the forward filter with respect to the features, on a kept
+// lattice: R = blur(splat(values)), H = blur_reverse(splat((G, -G.out) / Z)),
+// then per pixel the chain rule through the weights and the elevation.
+template <int PD, int V>
+cudaError_t fgrad_v(const CallArgs& a) {
+    constexpr int CPF = pad_ch(V + 1);
+    const Geo geo = make_geo(a);
+    const LatView Lv = lat_view(a.lattice, a.lay);
+    const ScrView Sv = {};
+    const int grid = a.sm_count * 8;
+    cudaError_t e;
+    // R: the forward's lattice values
+    e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.vbuf0, (const LatticeHeader*)Lv.hdr, CPF);
+    if (e != cudaSuccess) return e;
+    e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.values,
+                 (const float*)nullptr, geo, Lv, Sv, 0, a.vbuf0);
+    if (e != cudaSuccess) return e;
+    e = launch_blur_all<PD, CPF>(a, Lv, a.vbuf0, a.vbuf1, 0, a.flags);
+    if (e != cudaSuccess) return e;
+    // H: the lattice gradient, V+1 channels of (G, -G.out) weighted by 1/Z
+    const size_t n = (size_t)a.lay.h * a.lay.w;
+    e = launch_k(k_fgrad_prep<V>, dim3(grid), dim3(256), 0, a.stream, false, a.evec, a.grad_in, a.out_in, n);
+    if (e != cudaSuccess) return e;
+    e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.hbuf0, (const LatticeHeader*)Lv.hdr, CPF);
+    if (e != cudaSuccess) return e;
+    e = launch_k(k_splat<PD, V + 1, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                 (const float*)a.evec, a.weight_in, geo, Lv, Sv, 0, a.hbuf0);
+    if (e != cudaSuccess) return e;
+    e = launch_blur_all<PD, CPF>(a, Lv, a.hbuf0, a.hbuf1, 1, a.flags + 1);
+    if (e != cudaSuccess) return e;
+    return launch_k(k_fgrad<PD, V>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.out, a.features,
+                    a.values, a.grad_in, a.out_in, a.weight_in, geo, embed_consts(PD), Lv, (const float*)a.vbuf0,
+                    (const float*)a.vbuf1, (const float*)a.hbuf0, (const float*)a.hbuf1, (const int*)a.flags);
+}
+
 #define PL_DISPATCH_V(FN, PDV, ARGS)                      \
     switch ((ARGS).lay.vd) {                              \
         case 1: return FN<PDV, 1>(ARGS);                  \
@@ -302,6 +346,9 @@ cudaError_t run_backward(const CallArgs& a) { PL_DISPATCH_V(backward_v, PD, a) }
 
 template <int PD>
 cudaError_t run_filter(const CallArgs& a) { PL_DISPATCH_V(filter_v, PD, a) }
+
+template <int PD>
+cudaError_t run_feature_grad(const CallArgs& a) { PL_DISPATCH_V(fgrad_v, PD, a) }
 
 template <int PD>
 cudaError_t run_export_keys(const void* lattice, const void* scratch, const PlLayout& lay, int16_t* out,

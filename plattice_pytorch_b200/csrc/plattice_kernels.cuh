@@ -1012,7 +1012,8 @@ __device__ __forceinline__ void blur_row(const float (&me)[CP], const float (&a)
 }
 
 // The K blur passes, axis order 0..PD or PD..0 (reverse), from buf0 over the
-// pair buf0/buf1; hdr->blur_final names the buffer that holds the result.
+// pair buf0/buf1; *final_flag (normally hdr->blur_final) is set to the buffer
+// (0 or 1) that holds the result.
 // One cooperative launch: grid barriers separate the steps; every read of
 // data written inside this launch goes to L2 (ld.global.cg), never to a
 // stale L1 line.
@@ -1059,7 +1060,8 @@ __device__ __forceinline__ void blur_at(const float* x, int u, int2 n, float (&r
 }
 
 template <int PD, int CP>
-__global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse) {
+__global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse,
+                                                             int* final_flag) {
     constexpr int K = PD + 1;
     constexpr int R = CP <= 4 ? 2 : 1;        // vertices per thread kept in registers
     constexpr int W = CP < 4 ? CP : 4;         // channels per group (the stencil is per channel)
@@ -1119,7 +1121,7 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
                 grid_barrier(L.hdr, phase);
             }
         }
-        if (tid == 0) L.hdr->blur_final = (x == buf1) ? 1 : 0;
+        if (tid == 0) *final_flag = (x == buf1) ? 1 : 0;
         return;
     }
     constexpr int VPT = 2;   // vertices per thread and pass held in flight
@@ -1146,7 +1148,7 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
         if (s + 1 < K) grid_barrier(L.hdr, phase);
         float* t = x; x = y; y = t;
     }
-    if (tid == 0) L.hdr->blur_final = (x == buf1) ? 1 : 0;
+    if (tid == 0) *final_flag = (x == buf1) ? 1 : 0;
 }
 
 // ---------------------------------------------------------------- slice
@@ -1218,6 +1220,125 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
             for (int j = 0; j < V; ++j) out[p * V + j] = acc[r][j];
         }
     }
+}
+
+// ---------------------------------------------------------------- feature gradient
+
+// The features enter the filter only through the barycentric weights (the
+// vertex assignment is piecewise constant).  With R = the blurred forward
+// lattice values, Z_p = 1 / weight_p, G_p = dL/dout_p and H = B^T S'(d),
+// d_p = (G_p, -(G_p . out_p)) / Z_p:
+//   dL/dw_pc = (G_p . R[v][0:V] - (G_p . out_p) R[v][V]) / Z_p + H[v] . (val_p, 1),
+//   dL/de_i  = (dL/dw_{PD-rank_i} - dL/dw_{(PD+1-rank_i) mod K}) / K,
+// (the derivative of permutohedral.cu:224-233), and dL/df through the
+// elevation recurrence of permutohedral.cu:166-173.  The reference has no
+// feature gradient (plattice.py:19 returns None).
+
+// e_p = (G_p, -(G_p . out_p)): the V+1 channels splatted (times 1/Z_p) for H
+template <int V>
+static __global__ void k_fgrad_prep(float* __restrict__ ev, const float* __restrict__ grad,
+                                    const float* __restrict__ out, size_t n) {
+    for (size_t p = (size_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += (size_t)gridDim.x * blockDim.x) {
+        float dot = 0.0f;
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const float gj = __ldg(grad + p * V + j);
+            dot = __fmaf_rn(gj, __ldg(out + p * V + j), dot);
+            ev[p * (V + 1) + j] = gj;
+        }
+        ev[p * (V + 1) + V] = -dot;
+    }
+}
+
+template <int PD, int V>
+__global__ void __launch_bounds__(Cfg<PD>::P)
+k_fgrad(float* __restrict__ gfeat, const float* __restrict__ feat, const float* __restrict__ vals,
+        const float* __restrict__ grad, const float* __restrict__ outp, const float* __restrict__ winv, Geo geo,
+        EmbedConsts ec, LatView L, const float* R0, const float* R1, const float* H0, const float* H1,
+        const int* flags) {
+    using C = Cfg<PD>;
+    constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
+    constexpr int CP = pad_ch(V + 1);
+    __shared__ int svid[SLOTS];
+    __shared__ int scol[2 * K * P];   // embed scratch, then dL/dw by corner; column t per thread
+    const float* __restrict__ R = flags[0] ? R1 : R0;
+    const float* __restrict__ H = flags[1] ? H1 : H0;
+    const int t = threadIdx.x, tile = blockIdx.x;
+    const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
+    const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
+    const bool act = x < geo.w && y < geo.h;
+    const size_t p = (size_t)y * geo.w + x;
+    const size_t so = (size_t)tile * K * P + t;
+    int lid[K];
+    float w[K];
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        lid[c] = act ? (int)L.slot_lid[so + (size_t)c * P] : 0;
+        w[c] = act ? L.slot_w[so + (size_t)c * P] : 0.0f;
+    }
+    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
+    for (int u = t; u < cnt; u += P) svid[u] = L.staged_vid[off + u];
+    float f[PD];
+#pragma unroll
+    for (int i = 0; i < PD; ++i) f[i] = act ? __ldg(feat + p * PD + i) : 0.0f;
+    int g[K], rank[K];
+    float bary[K];
+    embed<PD>(f, ec, g, rank, bary, scol + t);
+    __syncthreads();
+    if (!act) return;
+    float G[V], vv[V];
+    float gdot = 0.0f;
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+        G[j] = __ldg(grad + p * V + j);
+        vv[j] = __ldg(vals + p * V + j);
+        gdot = __fmaf_rn(G[j], __ldg(outp + p * V + j), gdot);
+    }
+    const float zinv = __ldg(winv + p);
+    float* dwc = reinterpret_cast<float*>(scol) + t;   // dL/dw of corner c at dwc[c * P]
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        const int vid = svid[lid[c]];
+        float dw = 0.0f;
+        if (vid >= 0) {
+            float r[CP], hh[CP];
+            load_row<CP>(R + (size_t)vid * CP, r);
+            load_row<CP>(H + (size_t)vid * CP, hh);
+            float sl = 0.0f, sp = hh[V];
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                sl = __fmaf_rn(G[j], r[j], sl);
+                sp = __fmaf_rn(hh[j], vv[j], sp);
+            }
+            sl = __fmaf_rn(-gdot, r[V], sl);
+            dw = __fmaf_rn(sl, zinv, sp);
+        }
+        dwc[c * P] = dw;
+    }
+    float de[K];
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+        const int r = rank[i];
+        de[i] = (dwc[(PD - r) * P] - dwc[(r == 0 ? 0 : PD + 1 - r) * P]) * ec.rk;
+    }
+    float gf[PD];
+#pragma unroll
+    for (int i = 0; i < PD; ++i) gf[i] = 0.0f;
+    float carry = 0.0f;
+#pragma unroll
+    for (int i = 0; i <= PD; ++i) {
+        carry += de[i];
+        if (i == 0) {
+            gf[0] = __fmaf_rn(2.0f * ec.sf[0], carry, gf[0]);
+        } else if (i < PD) {
+            gf[i - 1] = __fmaf_rn(-(float)i * ec.sf[i - 1], carry, gf[i - 1]);
+            gf[i] = __fmaf_rn((float)(i + 2) * ec.sf[i], carry, gf[i]);
+        } else {
+            gf[PD - 1] = __fmaf_rn(-(float)PD * ec.sf[PD - 1], carry, gf[PD - 1]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < PD; ++i) gfeat[p * PD + i] = gf[i];
 }
 
 // ---------------------------------------------------------------- key export (tests)

@@ -12,6 +12,10 @@ context and reused by backward (no rebuild).
 ``PermutoLatticeFunction`` over a batch ``[B,H,W,...]`` in one library call,
 one lattice per image.
 
+``PermutoLatticeFeatureFunction`` (no counterpart in the reference) is
+``PermutoLatticeFunction`` with a gradient for the features as well: the
+slope of the piecewise-linear filter inside each pixel's simplex.
+
 ``LatticeFilterFunction`` (no counterpart in the reference) filters further
 values on a kept lattice -- the ``PLOO.Lattice`` of an earlier forward on the
 same features -- without rebuilding it, as the iterations of a mean-field CRF
@@ -24,7 +28,8 @@ from torch.nn import Module
 
 from . import PLOO
 
-__all__ = ["PermutoLatticeFunction", "PermutoLattice", "LatticeFilterFunction", "PermutoLatticeBatchFunction"]
+__all__ = ["PermutoLatticeFunction", "PermutoLattice", "LatticeFilterFunction", "PermutoLatticeBatchFunction",
+           "PermutoLatticeFeatureFunction"]
 
 
 class PermutoLatticeFunction(Function):
@@ -84,3 +89,28 @@ class PermutoLatticeBatchFunction(Function):
         grad_values = PLOO.batch_backward(feature, grad_output.contiguous(), weight,
                                           getattr(ctx, "lattice", None), saved=True)
         return None, grad_values
+
+
+class PermutoLatticeFeatureFunction(Function):
+    """``PermutoLatticeFeatureFunction.apply(features, values) -> out`` with
+    gradients for both inputs."""
+
+    @staticmethod
+    def forward(ctx, feature, values):
+        weight, out, lat = PLOO.lattice_forward(feature, values)
+        ctx.save_for_backward(weight, feature, values, out)
+        ctx.lattice = lat
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        weight, feature, values, out = ctx.saved_tensors
+        g = grad_output.contiguous()
+        grad_features = None
+        if ctx.needs_input_grad[0]:
+            grad_features = PLOO.feature_grad(ctx.lattice, feature, values, g, weight, out)
+        grad_values = None
+        if ctx.needs_input_grad[1]:
+            grad_values = PLOO.lattice_backward(feature, g, weight, ctx.lattice, saved=True)
+        return grad_features, grad_values

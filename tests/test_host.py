@@ -107,6 +107,25 @@ def test_batch_sizes_and_argument_checks(lib):
                                       None) == _lib.OK   # an empty batch is a no-op
 
 
+def test_feature_grad_sizes_and_argument_checks(lib):
+    from plattice_pytorch_b200 import _lib
+    b = _lib.feature_grad_workspace_size(512, 512, 5, 3)
+    slots = 512 * 512 * 6   # tiles x K x P for a 512 x 512 image at pd 5
+    assert b >= 4 * slots * 4 * 4 + 512 * 512 * 4 * 4   # R and H ping-pong rows + (G, -G.out) rows
+    with pytest.raises(_lib.PlatticeError):
+        _lib.feature_grad_workspace_size(8, 8, 17, 3)
+    fake = ctypes.c_void_p(256)
+    lb8, _ = _lib.workspace_sizes(8, 8, 5, 3)
+    b8 = _lib.feature_grad_workspace_size(8, 8, 5, 3)
+    args = [fake] * 7 + [lb8, fake, b8, 5, 3, 8, 8, None]
+    bad = list(args); bad[5] = None   # no features
+    assert lib.plattice_feature_grad(*bad) == _lib.ERR_INVALID
+    small = list(args); small[9] = b8 - 1
+    assert lib.plattice_feature_grad(*small) == _lib.ERR_WORKSPACE
+    small = list(args); small[7] = 100
+    assert lib.plattice_feature_grad(*small) == _lib.ERR_WORKSPACE
+
+
 def test_python_checks_raise_reference_messages():
     from plattice_pytorch_b200 import PLOO
     f = torch.zeros(4, 4, 5)
