@@ -61,6 +61,9 @@ def parse_args():
     ap.add_argument("--batched", action="store_true",
                     help="ours: the images of a rank go through one batch call per step "
                          "(PermutoLatticeBatchFunction) instead of one call per image")
+    ap.add_argument("--feature-grad", action="store_true",
+                    help="time forward + backward with the feature gradient as well "
+                         "(PermutoLatticeFeatureFunction) next to the value gradient only; 1 GPU, ours only")
     ap.add_argument("--kept-lattice", action="store_true",
                     help="time filter forward + backward on a lattice built once (a mean-field "
                          "iteration), next to the full forward + backward; 1 GPU, ours only")
@@ -260,6 +263,50 @@ def kept_lattice_line(args, dev):
                        "vd": int(v.shape[2]), "l2": "flushed between timed steps"}}
 
 
+def feature_grad_line(args, dev):
+    """One JSON line: forward + backward for both inputs (features and values)
+    per step, against forward + value gradient only; L2 flushed between
+    steps, CUDA events on the launching stream."""
+    from plattice_pytorch_b200 import PermutoLatticeFeatureFunction, PermutoLatticeFunction
+    from plattice_pytorch_b200.workloads import make_workload
+    wl = make_workload(args.workload, seed=0)
+    f = torch.from_numpy(wl["features"]).to(dev).requires_grad_(True)
+    v = torch.from_numpy(wl["values"]).to(dev).requires_grad_(True)
+    g = torch.from_numpy(wl["grad"]).to(dev)
+    h, w, pd = f.shape
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def both():
+        out = PermutoLatticeFeatureFunction.apply(f, v)
+        torch.autograd.grad(out, (f, v), (g,))
+
+    def values_only():
+        out = PermutoLatticeFunction.apply(f.detach(), v)
+        torch.autograd.grad(out, (v,), (g,))
+
+    res = {}
+    for name, fn in (("both", both), ("values", values_only)):
+        for _ in range(args.warmup):
+            fn()
+        evs = []
+        for _ in range(args.steps):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        res[name] = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    n = h * w
+    return {"metric": "Mpixel/s fwd + bwd with feature and value gradients",
+            "value": n / (res["both"] * 1e-3) / 1e6, "unit": "Mpixel/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": res["both"], "higher_is_better": True,
+            "value_grad_only_ms_per_step": res["values"], "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload, "h": int(h), "w": int(w), "pd": int(pd),
+                       "vd": int(v.shape[2]), "l2": "flushed between timed steps"}}
+
+
 def timed_e2e(fn, host, steps, dev):
     """Whole-loop CUDA-event time (ms) of `steps` end-to-end steps from pinned
     host buffers, including H2D of the inputs and D2H of out and grad.
@@ -428,6 +475,11 @@ def main():
     args = parse_args()
     rank, world, local = dist_setup()
     dev = torch.device("cuda", local)
+
+    if args.feature_grad:
+        if rank == 0 and args.impl == "ours":
+            print(json.dumps(feature_grad_line(args, dev)))
+        return
 
     if args.kept_lattice:
         if rank == 0 and args.impl == "ours":
