@@ -326,13 +326,14 @@ constexpr unsigned kFull = 0xffffffffu;
 
 // ---------------------------------------------------------------- block scan
 
-// Exclusive prefix sum of a[0..n) in place by the P threads of the CTA, with
-// a[n] set to the total.  Contains barriers: every thread must call it.
-template <int P>
-__device__ __forceinline__ void block_scan_excl(int* a, int n, int* warp_tot) {
-    const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
-    const int per = (n + P - 1) / P;
-    const int b = t * per, e = min(n, b + per);
+// Exclusive prefix sum of a[0..n) in place by warp 0 alone (a few elements
+// per lane), a[n] = the total.  The caller synchronises before (counts
+// complete) and after (offsets visible).
+__device__ __forceinline__ void warp0_scan_excl(int* a, int n) {
+    const int lane = threadIdx.x;
+    if (lane >= 32) return;
+    const int per = (n + 31) / 32;
+    const int b = lane * per, e = min(n, b + per);
     int sum = 0;
     for (int i = b; i < e; ++i) sum += a[i];
     int x = sum;
@@ -341,21 +342,13 @@ __device__ __forceinline__ void block_scan_excl(int* a, int n, int* warp_tot) {
         const int y = __shfl_up_sync(kFull, x, d);
         if (lane >= d) x += y;
     }
-    if (lane == 31) warp_tot[wid] = x;
-    __syncthreads();
     int run = x - sum;
-    for (int k = 0; k < wid; ++k) run += warp_tot[k];
     for (int i = b; i < e; ++i) {
         const int v = a[i];
         a[i] = run;
         run += v;
     }
-    if (t == P - 1) {
-        int tot = 0;
-        for (int k = 0; k < P / 32; ++k) tot += warp_tot[k];
-        a[n] = tot;
-    }
-    __syncthreads();
+    if (lane == 31) a[n] = x;
 }
 
 // ---------------------------------------------------------------- K1: tile build
@@ -410,7 +403,7 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     uint4* ukeys = reinterpret_cast<uint4*>(smem_raw);                  // [SLOTS][CW]
     int* stab = reinterpret_cast<int*>(ukeys + SLOTS * CW);             // [SC]
     int16_t* cand_lid = reinterpret_cast<int16_t*>(stab + SC);          // [SLOTS]
-    __shared__ int s_count, s_base, s_wtot[P / 32];
+    __shared__ int s_count, s_base;
 
     const int t = threadIdx.x, lane = t & 31;
     const int tile = blockIdx.x;
@@ -561,19 +554,22 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
         rk[c] = b + __popc(grp & ((1u << lane) - 1u));
     }
     __syncthreads();
-    block_scan_excl<P>(cnt, U, s_wtot);   // cnt[u] = first sorted position of id u, cnt[U] = total
-    float* wsort = reinterpret_cast<float*>(ukeys);   // key records are staged: reuse their space
+    warp0_scan_excl(cnt, U);   // cnt[u] = first sorted position of id u, cnt[U] = total
+    __syncthreads();
+    float* wsort = reinterpret_cast<float*>(ukeys);      // key records are staged: reuse their space
+    int16_t* slid = cand_lid;                             // dead since the local ids were read
     if (active) {
 #pragma unroll
         for (int c = 0; c < K; ++c) {
             const int pos = cnt[lid[c]] + rk[c];
             ord[pos] = (uint16_t)((t << 1) | (rk[c] == 0 ? 1 : 0));   // pixel, run start
             wsort[pos] = bary[c];
-            if (pos % K == 0) L.first_lid[(size_t)tile * P + pos / K] = (uint16_t)lid[c];
+            slid[pos] = (int16_t)lid[c];
         }
     }
     __syncthreads();
     const int total = cnt[U];
+    if (t * K < total) L.first_lid[(size_t)tile * P + t] = (uint16_t)slid[t * K];
     uint16_t* gord = L.slot_order + (size_t)tile * SLOTS;
     float* gws = L.slot_wsort + (size_t)tile * SLOTS;
     // 16-byte copies; the tile's regions are 16-byte aligned and a multiple of
