@@ -237,7 +237,7 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
         const float v = __fmul_rn(e[i], ec.rk);
         const float up = __fmul_rn(ceilf(v), ec.kf);
         const float dn = __fmul_rn(floorf(v), ec.kf);
-        g[i] = (__fsub_rn(up, e[i]) < __fsub_rn(e[i], dn)) ? f2s16(up) : f2s16(dn);
+        g[i] = f2s16((__fsub_rn(up, e[i]) < __fsub_rn(e[i], dn)) ? up : dn);   // one conversion
         sum = (int16_t)(sum + g[i]);
     }
     sum = (int16_t)(sum / K);
