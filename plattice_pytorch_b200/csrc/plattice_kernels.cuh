@@ -189,17 +189,46 @@ __device__ __forceinline__ uint32_t fmix32(uint32_t h) {
     return h;
 }
 
-// hash of a key record's coordinate words (word 0 is the hash slot itself):
-// multiply-xorshift per word, one final avalanche
-template <int NW>
-__device__ __forceinline__ uint32_t key_hash(const uint32_t (&kw)[NW]) {
-    uint32_t h = 0x9E3779B9u;
-#pragma unroll
-    for (int k = 1; k < NW; ++k) {
-        h = (h ^ kw[k]) * 0x85EBCA77u;
-        h ^= h >> 15;
+// Key hash.  Its linear part is the sum of the int16 coordinates
+// (sign-extended) times odd per-coordinate multipliers, mod 2^32, so that a
+// step of the key by a vector d moves it by sum d_i * mul_i: a blur
+// neighbour's hash is the vertex's plus a per-axis constant (the same idea as
+// the reference's hash offsets, permutohedral.cu:50-53).  The stored hash is
+// that sum after an avalanche (fmix32), for the table positions and tags.
+__host__ __device__ constexpr uint32_t coord_mul(int i) {
+    switch (i) {
+        case 0: return 0x2AE75E2Fu;  case 1: return 0x9C2B9D9Fu;  case 2: return 0x4F876AA3u;
+        case 3: return 0x02FF349Du;  case 4: return 0xBAEC4EF7u;  case 5: return 0xE06C85AFu;
+        case 6: return 0x21F64545u;  case 7: return 0xE7158A81u;  case 8: return 0x819ED6B7u;
+        case 9: return 0x3C95AD21u;  case 10: return 0x8BE9794Du; case 11: return 0x3C7BA9E3u;
+        case 12: return 0x022DD18Du; case 13: return 0x4D317C69u; case 14: return 0x7965C0FFu;
+        default: return 0x8ECA7365u;
     }
-    return fmix32(h);
+}
+
+__device__ __forceinline__ uint32_t hash_of_lin(uint32_t lin) { return fmix32(lin ^ 0x9E3779B9u); }
+
+// coordinate i (sign-extended int16) of a packed key record
+__device__ __forceinline__ int key_coord(const uint32_t* kw, int i) {
+    return (int)(int16_t)(uint16_t)(kw[1 + i / 2] >> (16 * (i & 1)));
+}
+
+template <int PD>
+__device__ __forceinline__ uint32_t key_lin_words(const uint32_t* kw) {
+    uint32_t lin = 0u;
+#pragma unroll
+    for (int i = 0; i < PD; ++i) lin += (uint32_t)key_coord(kw, i) * coord_mul(i);
+    return lin;
+}
+
+// the change of the linear part for the blur step along axis c: every
+// coordinate +1, and coordinate c -K when c < PD (permutohedral.cu:368-375)
+template <int PD>
+__device__ __forceinline__ uint32_t axis_lin_step(int c) {
+    uint32_t s = 0u;
+#pragma unroll
+    for (int i = 0; i < PD; ++i) s += coord_mul(i) * (i == c ? (uint32_t)(1 - (PD + 1)) : 1u);
+    return s;
 }
 
 // ---------------------------------------------------------------- lattice embedding
@@ -315,9 +344,9 @@ __device__ __forceinline__ void make_key(const int (&g)[PD + 1], const int (&ran
 #pragma unroll
     for (int i = 0; i < PD; ++i) {
         const int v = g[i] + c - ((rank[i] > PD - c) ? (PD + 1) : 0);
-        kw[1 + i / 2] |= ((uint32_t)(uint16_t)(int16_t)v) << (16 * (i & 1));
+        kw[1 + i / 2] |= ((uint32_t)(uint16_t)(int16_t)v) << (16 * (i & 1));   // int16 wrap-around
     }
-    kw[0] = key_hash<NW>(kw);
+    kw[0] = hash_of_lin(key_lin_words<PD>(kw));
 }
 
 // ---------------------------------------------------------------- warp helpers
@@ -650,22 +679,45 @@ __device__ __forceinline__ TableFmt table_fmt(const Geo& g) {
 
 __device__ __forceinline__ uint32_t cell_tag(uint32_t hash, TableFmt f) { return hash & ~f.idx_mask; }
 
-// Continue a probe for kw (word 0 = hash) whose cell at pos has been read as
-// c: the staged index of the owner of kw, or -1 when kw is not in the table.
-// Read-only use, after the table is complete.
-template <int CW>
-__device__ __forceinline__ int table_probe(const uint32_t* __restrict__ table, uint32_t mask, TableFmt f,
-                                           const uint4* __restrict__ skeys, const uint32_t (&kw)[4 * CW],
-                                           uint32_t pos, uint32_t c, int* status) {
-    const uint32_t tag = cell_tag(kw[0], f);
+// The key of the blur neighbour of `key` along axis c, direction sgn (+1/-1),
+// with int16 wrap-around per coordinate; word 0 receives `hash`.
+template <int PD>
+__device__ __forceinline__ void neighbour_key(const uint32_t (&key)[Cfg<PD>::NW], int c, int sgn, uint32_t hash,
+                                              uint32_t (&kw)[Cfg<PD>::NW]) {
+    constexpr int K = PD + 1, NW = Cfg<PD>::NW;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) kw[k] = key[k];   // padding words stay as they are (0)
+#pragma unroll
+    for (int k = 1; k <= 1 + (PD - 1) / 2; ++k) {  // the words that hold coordinates
+        const int lo = 2 * (k - 1), hi = lo + 1;
+        const int dlo = lo < PD ? 1 - (c == lo ? K : 0) : 0;
+        const int dhi = hi < PD ? 1 - (c == hi ? K : 0) : 0;
+        kw[k] = hw_add(key[k], pack_hw(sgn * dlo, sgn * dhi));
+    }
+    kw[0] = hash;
+}
+
+// Continue a probe for the neighbour (c, sgn) of `key`, whose hash is h and
+// whose cell at pos has been read as `cell`: the vertex id of the neighbour,
+// or -1 when it is not a lattice vertex.  Its key words are formed only when a
+// cell's tag matches.  Read-only use, after the table is complete.
+template <int PD>
+__device__ __forceinline__ int neighbour_find(const uint32_t* __restrict__ table, uint32_t mask, TableFmt f,
+                                              const uint4* __restrict__ skeys, const int* __restrict__ vid_of,
+                                              const uint32_t (&key)[Cfg<PD>::NW], int c, int sgn, uint32_t h,
+                                              uint32_t pos, uint32_t cell, int* status) {
+    constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
+    const uint32_t tag = cell_tag(h, f);
     for (uint32_t probe = 0; probe <= mask; ++probe) {
-        if (c == 0u) return -1;
-        if ((c & ~f.idx_mask) == tag) {
-            const int o = (int)(c & f.idx_mask) - 1;
-            if (key_equal<CW>(skeys + (size_t)o * CW, kw)) return o;
+        if (cell == 0u) return -1;
+        if ((cell & ~f.idx_mask) == tag) {
+            const int o = (int)(cell & f.idx_mask) - 1;
+            uint32_t kw[NW];
+            neighbour_key<PD>(key, c, sgn, h, kw);
+            if (key_equal<CW>(skeys + (size_t)o * CW, kw)) return __ldg(vid_of + o);
         }
         pos = (pos + 1) & mask;
-        c = __ldg(table + pos);
+        cell = __ldg(table + pos);
     }
     atomicOr(status, PL_ST_TABLE_FULL);
     return -1;
@@ -745,7 +797,9 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
 // coordinate +1 (or -1) (permutohedral.cu:368-375).  A thread takes one
 // vertex and a group of axes (all of them when there are enough vertices to
 // occupy the grid), loads the vertex key once and issues the two lookups of
-// an axis together.
+// an axis together.  The vertex keys and the neighbour pairs are streamed
+// with evict-first hints, so that the hash table, which every lookup probes at
+// random, stays resident in L2.
 template <int PD>
 __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S) {
     constexpr int K = PD + 1, CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
@@ -761,28 +815,41 @@ __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S
         const int g = (int)(idx / M);
         const int v = (int)(idx - (size_t)g * M);
         uint32_t key[NW];
-        load_key<CW>(S.vkeys + (size_t)v * CW, key);
+#pragma unroll
+        for (int w = 0; w < CW; ++w) {   // streamed (evict-first): the table stays in L2
+            const uint4 r = __ldcs(S.vkeys + (size_t)v * CW + w);
+            key[4 * w] = r.x; key[4 * w + 1] = r.y; key[4 * w + 2] = r.z; key[4 * w + 3] = r.w;
+        }
+        // hashes of the neighbours from the linear part of the key; a key within
+        // K of the int16 limits may wrap a coordinate, so its neighbours' linear
+        // parts are recomputed from their words instead
+        const uint32_t lin = key_lin_words<PD>(key);
+        bool edge = false;
+#pragma unroll
+        for (int i = 0; i < PD; ++i) {
+            const int x = key_coord(key, i);
+            edge = edge || x > 32767 - K || x < -32768 + K;
+        }
         for (int c = g; c < K; c += G) {
-            uint32_t kp[NW], km[NW];
-#pragma unroll
-            for (int k = 0; k < NW; ++k) kp[k] = km[k] = key[k];   // padding words stay as they are (0)
-#pragma unroll
-            for (int k = 1; k <= 1 + (PD - 1) / 2; ++k) {          // the words that hold coordinates
-                const int lo = 2 * (k - 1), hi = lo + 1;
-                const int dlo = lo < PD ? 1 - (c == lo ? K : 0) : 0;
-                const int dhi = hi < PD ? 1 - (c == hi ? K : 0) : 0;
-                kp[k] = hw_add(key[k], pack_hw(dlo, dhi));
-                km[k] = hw_add(key[k], pack_hw(-dlo, -dhi));
+            uint32_t hp, hm;
+            if (!edge) {
+                const uint32_t d = axis_lin_step<PD>(c);
+                hp = hash_of_lin(lin + d);
+                hm = hash_of_lin(lin - d);
+            } else {
+                uint32_t kw[NW];
+                neighbour_key<PD>(key, c, 1, 0u, kw);
+                hp = hash_of_lin(key_lin_words<PD>(kw));
+                neighbour_key<PD>(key, c, -1, 0u, kw);
+                hm = hash_of_lin(key_lin_words<PD>(kw));
             }
-            kp[0] = key_hash<NW>(kp);
-            km[0] = key_hash<NW>(km);
-            const uint32_t pa = kp[0] & mask, pb = km[0] & mask;
+            const uint32_t pa = hp & mask, pb = hm & mask;
             const uint32_t ca = __ldg(S.table + pa), cb = __ldg(S.table + pb);
-            const int oa = table_probe<CW>(S.table, mask, f, S.skeys, kp, pa, ca, &L.hdr->status);
-            const int ob = table_probe<CW>(S.table, mask, f, S.skeys, km, pb, cb, &L.hdr->status);
-            const int a = oa >= 0 ? __ldg(S.vid_of + oa) : -1;
-            const int b = ob >= 0 ? __ldg(S.vid_of + ob) : -1;
-            L.nbr[(size_t)c * M + v] = make_int2(a, b);
+            const int a = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, 1, hp, pa, ca,
+                                             &L.hdr->status);
+            const int b = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, -1, hm, pb, cb,
+                                             &L.hdr->status);
+            __stcs(L.nbr + (size_t)c * M + v, make_int2(a, b));   // streamed, as the key loads
         }
     }
 }

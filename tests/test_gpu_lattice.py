@@ -4,8 +4,9 @@ The parity tests compare what the filter returns; these read the lattice and
 scratch buffers of one forward call back to the host and check the structure
 every later kernel relies on, for every feature dimension:
   * every vertex key record has its padding halfwords zero and word 0 equal to
-    the hash of words 1.. (lookups compare whole records, so a record that
-    decodes to the right coordinates but differs anywhere else is not found);
+    the hash of its coordinates (lookups compare whole records, so a record
+    that decodes to the right coordinates but differs anywhere else is not
+    found; neighbour hashes are derived incrementally from that hash);
   * every (pixel, simplex corner) slot resolves to the vertex whose key the
     oracle's embedding gives (permutohedral.cu:238-244), with the same weight;
   * each tile's slots, counting-sorted by local vertex id, cover the tile's
@@ -67,13 +68,21 @@ def _view(buf, off, n, dt):
     return buf[off:off + n * np.dtype(dt).itemsize].view(dt)
 
 
-def _key_hash(words):
-    """Hash of key records [n][NW] (word 0 excluded), as the device computes it."""
+_COORD_MUL = [0x2AE75E2F, 0x9C2B9D9F, 0x4F876AA3, 0x02FF349D, 0xBAEC4EF7, 0xE06C85AF, 0x21F64545, 0xE7158A81,
+              0x819ED6B7, 0x3C95AD21, 0x8BE9794D, 0x3C7BA9E3, 0x022DD18D, 0x4D317C69, 0x7965C0FF, 0x8ECA7365]
+
+
+def _key_hash(words, pd):
+    """Hash of key records [n][NW] as the device computes it: the sum of the
+    sign-extended int16 coordinates times per-coordinate odd multipliers
+    (mod 2^32), then an avalanche (fmix32)."""
     m32 = np.uint64(0xFFFFFFFF)
-    h = np.full(words.shape[0], 0x9E3779B9, np.uint64)
-    for k in range(1, words.shape[1]):
-        h = ((h ^ words[:, k].astype(np.uint64)) * np.uint64(0x85EBCA77)) & m32
-        h ^= h >> np.uint64(15)
+    coords, _ = _decode(words, pd)
+    lin = np.zeros(words.shape[0], np.uint64)
+    for i in range(pd):
+        c = coords[:, i].astype(np.int64) & 0xFFFFFFFF
+        lin = (lin + c.astype(np.uint64) * np.uint64(_COORD_MUL[i])) & m32
+    h = lin ^ np.uint64(0x9E3779B9)
     h ^= h >> np.uint64(16)
     h = (h * np.uint64(0x85EBCA6B)) & m32
     h ^= h >> np.uint64(13)
@@ -124,7 +133,7 @@ def test_lattice_invariants(fn, dev):
         words = _view(sb, scr_off[name], n * CW * 4, np.uint32).reshape(n, CW * 4)
         coords, padding = _decode(words, pd)
         assert not padding.any(), (name, int(np.count_nonzero(padding)))
-        assert np.array_equal(words[:, 0], _key_hash(words)), name
+        assert np.array_equal(words[:, 0], _key_hash(words, pd)), name
     vk, _ = _decode(_view(sb, scr_off["vkeys"], M * CW * 4, np.uint32).reshape(M, CW * 4), pd)
     assert len({r.tobytes() for r in vk}) == M
     vid_of_key = {r.tobytes(): i for i, r in enumerate(vk)}
