@@ -50,6 +50,7 @@ inline LatView lat_view(void* base, const PlLayout& L) {
     v.nbr = reinterpret_cast<int2*>(b + L.off_nbr);
     v.vb0 = reinterpret_cast<float*>(b + L.off_vb0);
     v.vb1 = reinterpret_cast<float*>(b + L.off_vb1);
+    v.bstate = reinterpret_cast<uint8_t*>(b + L.off_bstate);
     return v;
 }
 

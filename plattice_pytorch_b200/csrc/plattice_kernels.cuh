@@ -74,6 +74,7 @@ struct LatView {
     int2* nbr;
     float* vb0;
     float* vb1;
+    uint8_t* bstate;   // [2][slots] blur bookkeeping of large lattices
 };
 
 struct ScrView {
@@ -1060,6 +1061,15 @@ __device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase
     __syncthreads();
 }
 
+// r *= 2^-e (exact: a power of two, far from the float range limits here)
+template <int CP>
+__device__ __forceinline__ void scale_pow2(float (&r)[CP], int e) {
+    if (e == 0) return;
+    const float f = __int_as_float((127 - e) << 23);
+#pragma unroll
+    for (int j = 0; j < CP; ++j) r[j] = __fmul_rn(r[j], f);
+}
+
 // One [1 2 1]/4 stencil step of a row along one axis; a missing neighbour
 // (index -1) contributes nothing (permutohedral.cu:341-347).
 template <int CP>
@@ -1081,7 +1091,7 @@ __device__ __forceinline__ void blur_row(const float (&me)[CP], const float (&a)
 // data written inside this launch goes to L2 (ld.global.cg), never to a
 // stale L1 line.
 //
-// At most R vertices per thread (R = 2 for rows of up to 4 channels, else 1): a thread keeps the same
+// At most R vertices per thread (R = 2 for rows of up to 2 channels, else 1): a thread keeps the same
 // vertices throughout, their rows in registers, and runs the passes in pairs.
 // For passes s, s+1 it evaluates pass s at its vertex v and at v's two
 // neighbours along the axis of pass s+1 (each from the rows pass s reads
@@ -1122,11 +1132,84 @@ __device__ __forceinline__ void blur_at(const float* x, int u, int2 n, float (&r
     blur_row<W>(me, a, b, n, r);
 }
 
+// Larger lattices stream every row, one pass per step.  A vertex without a
+// neighbour along the pass's axis only halves (0.25 * (2 x) = x / 2, exact in
+// float): its row is left where it is and the halving is recorded in its
+// state byte (bit 7: the buffer holding the row, bits 0-6: pending halvings);
+// the rows that are read are scaled by their pending powers of two first,
+// which is exact too, so the values are those of the plain sequence of
+// passes.  The indices and states of VPT vertices are requested together.
+// Each thread owns the same vertices in every pass and finally gathers its
+// rows, scaled, into buf0.  (A separate function, so that its registers do
+// not weigh on the resident path.)
+template <int PD, int CP>
+__device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, LatticeHeader* hdr, float* buf0,
+                                            float* buf1, int reverse, int* final_flag, int M, int tid, int stride) {
+    constexpr int K = PD + 1;
+    constexpr int VPT = 4;
+    unsigned phase = 0;
+    uint8_t* const st0 = bstate;
+    uint8_t* const st1 = bstate + M;
+#pragma unroll 1
+    for (int s = 0; s < K; ++s) {
+        const int ax = reverse ? K - 1 - s : s;
+        const int2* nb = nbr + (size_t)ax * M;
+        const uint8_t* sc = (s & 1) ? st1 : st0;
+        uint8_t* sn = (s & 1) ? st0 : st1;
+        for (int v0 = tid; v0 < M; v0 += stride * VPT) {
+            int2 n[VPT];
+            int cv[VPT], ca[VPT], cb[VPT];
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int v = v0 + k * stride;
+                n[k] = v < M ? __ldg(nb + v) : make_int2(-1, -1);
+                cv[k] = (s == 0 || v >= M) ? 0 : (int)__ldcg(sc + v);
+            }
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                ca[k] = (s == 0 || n[k].x < 0) ? 0 : (int)__ldcg(sc + n[k].x);
+                cb[k] = (s == 0 || n[k].y < 0) ? 0 : (int)__ldcg(sc + n[k].y);
+            }
+#pragma unroll
+            for (int k = 0; k < VPT; ++k) {
+                const int v = v0 + k * stride;
+                if (v >= M) continue;
+                const int bv = cv[k] >> 7, ev = cv[k] & 127;
+                if (n[k].x < 0 && n[k].y < 0) {
+                    sn[v] = (uint8_t)((bv << 7) | (ev + 1));
+                    continue;
+                }
+                float me[CP], a[CP], b[CP], r[CP];
+                load_row_cg<CP>((bv ? buf1 : buf0) + (size_t)v * CP, me);
+                if (n[k].x >= 0) load_row_cg<CP>(((ca[k] >> 7) ? buf1 : buf0) + (size_t)n[k].x * CP, a);
+                if (n[k].y >= 0) load_row_cg<CP>(((cb[k] >> 7) ? buf1 : buf0) + (size_t)n[k].y * CP, b);
+                scale_pow2<CP>(me, ev);
+                if (n[k].x >= 0) scale_pow2<CP>(a, ca[k] & 127);
+                if (n[k].y >= 0) scale_pow2<CP>(b, cb[k] & 127);
+                blur_row<CP>(me, a, b, n[k], r);
+                store_row<CP>((bv ? buf0 : buf1) + (size_t)v * CP, r);
+                sn[v] = (uint8_t)((1 - bv) << 7);
+            }
+        }
+        if (s + 1 < K) grid_barrier(hdr, phase);
+    }
+    const uint8_t* sf = (K & 1) ? st1 : st0;
+    for (int v = tid; v < M; v += stride) {   // my own vertices: written by me in the last pass
+        const int c = (int)sf[v];
+        if (c == 0) continue;
+        float r[CP];
+        load_row_cg<CP>(((c >> 7) ? buf1 : buf0) + (size_t)v * CP, r);
+        scale_pow2<CP>(r, c & 127);
+        store_row<CP>(buf0 + (size_t)v * CP, r);
+    }
+    if (tid == 0) *final_flag = 0;
+}
+
 template <int PD, int CP>
 __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse,
                                                              int* final_flag) {
     constexpr int K = PD + 1;
-    constexpr int R = CP <= 4 ? 2 : 1;        // vertices per thread kept in registers
+    constexpr int R = CP <= 2 ? 2 : 1;        // vertices per thread kept in registers
     constexpr int W = CP < 4 ? CP : 4;         // channels per group (the stencil is per channel)
     const int M = L.hdr->m;
     const int stride = gridDim.x * blockDim.x;
@@ -1187,31 +1270,7 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
         if (tid == 0) *final_flag = (x == buf1) ? 1 : 0;
         return;
     }
-    constexpr int VPT = 2;   // vertices per thread and pass held in flight
-#pragma unroll 1
-    for (int s = 0; s < K; ++s) {
-        const int ax = reverse ? K - 1 - s : s;
-        const int2* nb = L.nbr + (size_t)ax * M;
-        for (int v0 = tid; v0 < M; v0 += stride * VPT) {
-            int2 n[VPT];
-#pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-                const int v = v0 + k * stride;
-                n[k] = v < M ? __ldg(nb + v) : make_int2(-1, -1);
-            }
-#pragma unroll
-            for (int k = 0; k < VPT; ++k) {
-                const int v = v0 + k * stride;
-                if (v >= M) continue;
-                float r[CP];
-                blur_at<CP, CP>(x, v, n[k], r);
-                store_row<CP>(y + (size_t)v * CP, r);
-            }
-        }
-        if (s + 1 < K) grid_barrier(L.hdr, phase);
-        float* t = x; x = y; y = t;
-    }
-    if (tid == 0) *final_flag = (x == buf1) ? 1 : 0;
+    blur_streaming<PD, CP>(L.nbr, L.bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
 }
 
 // ---------------------------------------------------------------- slice

@@ -20,6 +20,9 @@
 //   staged_vid     [U]          int32    global vertex id of each staged key
 //   nbr            [K][m]       int2     blur neighbours (+, -) per axis, -1 absent
 //   vb0, vb1       [m][CPb]     float    backward lattice values (ping-pong)
+//   bstate         [2][slots]   uint8    blur bookkeeping of large lattices: per
+//                                        vertex, the buffer holding its row and
+//                                        its pending halvings (ping-pong)
 // Scratch blob (forward build only):
 //   staged_keys    [U][CW]      uint4    each tile's unique keys (word 0: hash)
 //   table          [cap]        uint32   open-addressed hash table: 0 empty, else
@@ -68,7 +71,7 @@ typedef struct {
     long long slots;      /* tiles*K*P: bound on staged keys and on vertices */
     int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
     size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_slot_wsort, off_first_lid,
-        off_staged_vid, off_nbr, off_vb0, off_vb1, lattice_bytes;
+        off_staged_vid, off_nbr, off_vb0, off_vb1, off_bstate, lattice_bytes;
     size_t off_skeys, off_table, off_owner, off_vid_of, off_vkeys, off_vf0, off_vf1, scratch_bytes;
 } PlLayout;
 
@@ -99,6 +102,7 @@ static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
     L->off_nbr = o;        o = pl_align(o + S * L->K * 8);
     L->off_vb0 = o;        o = pl_align(o + S * L->CPb * 4);
     L->off_vb1 = o;        o = pl_align(o + S * L->CPb * 4);
+    L->off_bstate = o;     o = pl_align(o + 2 * S);
     L->lattice_bytes = o;
     o = 0;
     L->off_skeys = o;      o = pl_align(o + S * L->CW * 16);
