@@ -162,6 +162,13 @@ int plattice_vertex_keys(const void* lattice, const void* scratch, int pd, int v
  * build report PLATTICE_DEV_TABLE_FULL instead of looping. */
 void plattice_debug_set_table_cap_log2(int log2_cells);
 
+/* Test support: the table size (log2 cells) from which blur-neighbour lookups
+ * consult the miss filter (0 = automatic: 2^22 cells and more), so that small
+ * cases can exercise the filter.  No reference counterpart (the reference
+ * probes its table for every neighbour lookup, permutohedral.cu:119-141 as
+ * called from precomputeBlurNeighbors, permutohedral.cu:350-383). */
+void plattice_debug_set_miss_filter_log2(int log2_cells);
+
 /* Forward filter for callers that cannot allocate device memory (no
  * counterpart in the reference, whose host layer allocates a new workspace on
  * every call).  Same computation and outputs as plattice_forward, but the

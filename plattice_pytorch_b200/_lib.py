@@ -84,6 +84,8 @@ def lib():
         L.plattice_vertex_keys.argtypes = [P, P, I, I, I, I, P, I, ctypes.POINTER(I), P]
         L.plattice_debug_set_table_cap_log2.restype = None
         L.plattice_debug_set_table_cap_log2.argtypes = [I]
+        L.plattice_debug_set_miss_filter_log2.restype = None
+        L.plattice_debug_set_miss_filter_log2.argtypes = [I]
         L.plattice_profile_enable.restype = None
         L.plattice_profile_enable.argtypes = [I]
         L.plattice_profile_read.restype = I

@@ -25,6 +25,7 @@ PL_DECLARE_PD(13) PL_DECLARE_PD(14) PL_DECLARE_PD(15) PL_DECLARE_PD(16)
 }  // namespace pl
 
 static int g_cap_override_log2 = 0;
+static int g_filter_min_log2 = 0;
 
 // ---------------------------------------------------------------- side stream
 
@@ -247,6 +248,7 @@ int plattice_forward(float* weight_out, float* out, const float* values, const f
     a.sm_count = sm_count_current();
     a.lattice_state = 0;
     a.cap_override_log2 = g_cap_override_log2;
+    a.filter_min_log2 = g_filter_min_log2;
     return cuda_status(dispatch_forward(a), "plattice_forward");
 }
 
@@ -270,6 +272,7 @@ int plattice_backward(float* grad_values_out, const float* grad, const float* we
     a.sm_count = sm_count_current();
     a.lattice_state = lattice_state;
     a.cap_override_log2 = g_cap_override_log2;
+    a.filter_min_log2 = g_filter_min_log2;
     return cuda_status(dispatch_backward(a), "plattice_backward");
 }
 
@@ -370,6 +373,7 @@ static int kept_lattice_args(pl::CallArgs& a, size_t lattice_bytes, void* ws, si
     a.stream = static_cast<cudaStream_t>(stream);
     a.sm_count = sm_count_current();
     a.cap_override_log2 = g_cap_override_log2;
+    a.filter_min_log2 = g_filter_min_log2;
     return PLATTICE_OK;
 }
 
@@ -471,6 +475,7 @@ int plattice_feature_grad(float* grad_features_out, const float* grad, const flo
     a.stream = static_cast<cudaStream_t>(stream);
     a.sm_count = sm_count_current();
     a.cap_override_log2 = g_cap_override_log2;
+    a.filter_min_log2 = g_filter_min_log2;
     return cuda_status(dispatch_feature_grad(a), "plattice_feature_grad");
 }
 
@@ -540,6 +545,10 @@ const char* plattice_profile_stage_name(int stage) {
 
 void plattice_debug_set_table_cap_log2(int log2_cells) {
     g_cap_override_log2 = (log2_cells > 0 && log2_cells < 31) ? log2_cells : 0;
+}
+
+void plattice_debug_set_miss_filter_log2(int log2_cells) {
+    g_filter_min_log2 = (log2_cells > 0 && log2_cells < 31) ? log2_cells : 0;
 }
 
 }  // extern "C"

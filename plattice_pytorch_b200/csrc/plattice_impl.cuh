@@ -24,6 +24,7 @@ struct CallArgs {
     int sm_count;
     int lattice_state;       // backward: 0 rebuild, 1 fresh from forward, 2 reuse (re-zero)
     int cap_override_log2;
+    int filter_min_log2;     // 0: the default (tables of 2^22 cells and more)
     float* vbuf0;            // value buffers of a filter call on a kept lattice (else null:
     float* vbuf1;            // the forward's scratch rows / the lattice's backward rows)
     // feature gradient: dL/dout, the forward's out, and lattice rows / flags in the workspace
@@ -59,6 +60,7 @@ inline ScrView scr_view(void* base, const PlLayout& L) {
     ScrView v;
     v.skeys = reinterpret_cast<uint4*>(b + L.off_skeys);
     v.table = reinterpret_cast<uint32_t*>(b + L.off_table);
+    v.filter = reinterpret_cast<uint32_t*>(b + L.off_filter);
     v.owner = reinterpret_cast<int*>(b + L.off_owner);
     v.vid_of = reinterpret_cast<int*>(b + L.off_vid_of);
     v.vkeys = reinterpret_cast<uint4*>(b + L.off_vkeys);
@@ -84,6 +86,7 @@ inline Geo make_geo(const CallArgs& a) {
     g.h = a.lay.h; g.w = a.lay.w; g.tiles_x = a.lay.tiles_x; g.tiles = a.lay.tiles;
     g.cap_max_log2 = a.lay.cap_max_log2;
     g.cap_override_log2 = a.cap_override_log2;
+    g.filter_min_log2 = a.filter_min_log2 > 0 ? a.filter_min_log2 : 22;   // a 16 MB table and up
     g.idx_bits = 1;
     while (g.idx_bits < 32 && (1ll << g.idx_bits) <= a.lay.slots) ++g.idx_bits;   // 1 + index <= slots
     return g;

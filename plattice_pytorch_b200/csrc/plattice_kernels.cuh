@@ -59,6 +59,7 @@ struct Geo {
     int h, w, tiles_x, tiles;
     int cap_max_log2, cap_override_log2;
     int idx_bits;   // bits that hold 1 + any staged index of the call (global table cells)
+    int filter_min_log2;   // table size (log2 cells) from which lookups consult the miss filter
 };
 
 struct LatView {
@@ -80,6 +81,7 @@ struct LatView {
 struct ScrView {
     uint4* skeys;
     uint32_t* table;
+    uint32_t* filter;   // miss filter: one byte per table cell, used for large tables
     int* owner;     // [U] staged index of the owner of each staged key
     int* vid_of;    // [U] vertex id of each owner
     uint4* vkeys;
@@ -629,6 +631,10 @@ static __global__ void k_clear(Geo geo, LatView L, ScrView S) {
     uint4* t4 = reinterpret_cast<uint4*>(S.table);
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) t4[i] = z;
+    if (lg >= geo.filter_min_log2) {   // the miss filter: one byte per cell
+        uint4* f4 = reinterpret_cast<uint4*>(S.filter);
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4 / 4; i += stride) f4[i] = z;
+    }
 }
 
 // zero the first m rows of a lattice value buffer (a repeated backward)
@@ -679,6 +685,17 @@ __device__ __forceinline__ TableFmt table_fmt(const Geo& g) {
 }
 
 __device__ __forceinline__ uint32_t cell_tag(uint32_t hash, TableFmt f) { return hash & ~f.idx_mask; }
+
+// Miss filter of a large table: a bit array of 8 bits per cell, one bit per
+// vertex key, chosen by the key's home cell (the low bits of its hash) and the
+// top three hash bits.  A clear bit proves a key absent without touching the
+// table, whose cells are random HBM reads once it outgrows L2, while the
+// filter (a quarter of the table's size) stays in L2.  With one bit per key
+// and 8 bits per cell at a load of at most one key per two cells, at most
+// 1 - e^(-1/16) (6%) of absent keys still reach the table; a present key
+// always does (no false negatives: its owner set the bit before lookups run).
+__device__ __forceinline__ uint32_t filter_word(uint32_t hash, uint32_t mask) { return (hash & mask) >> 2; }
+__device__ __forceinline__ uint32_t filter_bit(uint32_t hash) { return 1u << (((hash & 3u) << 3) | (hash >> 29)); }
 
 // The key of the blur neighbour of `key` along axis c, direction sgn (+1/-1),
 // with int16 wrap-around per coordinate; word 0 receives `hash`.
@@ -740,6 +757,7 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
     __shared__ int s_wcnt[8], s_base;
     const int U = L.hdr->u_total;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
+    const bool use_filter = L.hdr->cap_log2 >= geo.filter_min_log2;
     const TableFmt f = table_fmt(geo);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     for (int i0 = blockIdx.x * blockDim.x; i0 < U; i0 += gridDim.x * blockDim.x) {   // block-uniform
@@ -754,6 +772,7 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
                 const uint32_t c = atomicCAS(S.table + pos, 0u, tag | (uint32_t)(i + 1));
                 if (c == 0u) {
                     owner = i;
+                    if (use_filter) atomicOr(S.filter + filter_word(kw[0], mask), filter_bit(kw[0]));
                     break;
                 }
                 if ((c & ~f.idx_mask) == tag) {
@@ -807,6 +826,7 @@ __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S
     const int M = L.hdr->m;
     if (M <= 0) return;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
+    const bool use_filter = L.hdr->cap_log2 >= geo.filter_min_log2;
     const TableFmt f = table_fmt(geo);
     const int nthreads = gridDim.x * blockDim.x;
     int G = (nthreads + M - 1) / M;   // axis groups
@@ -845,7 +865,12 @@ __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S
                 hm = hash_of_lin(key_lin_words<PD>(kw));
             }
             const uint32_t pa = hp & mask, pb = hm & mask;
-            const uint32_t ca = __ldg(S.table + pa), cb = __ldg(S.table + pb);
+            bool ina = true, inb = true;   // a cell reads as empty when the filter rules the key out
+            if (use_filter) {
+                ina = (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
+                inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
+            }
+            const uint32_t ca = ina ? __ldg(S.table + pa) : 0u, cb = inb ? __ldg(S.table + pb) : 0u;
             const int a = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, 1, hp, pa, ca,
                                              &L.hdr->status);
             const int b = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, -1, hm, pb, cb,

@@ -72,7 +72,7 @@ typedef struct {
     int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
     size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_slot_wsort, off_first_lid,
         off_staged_vid, off_nbr, off_vb0, off_vb1, off_bstate, lattice_bytes;
-    size_t off_skeys, off_table, off_owner, off_vid_of, off_vkeys, off_vf0, off_vf1, scratch_bytes;
+    size_t off_skeys, off_table, off_filter, off_owner, off_vid_of, off_vkeys, off_vf0, off_vf1, scratch_bytes;
 } PlLayout;
 
 static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
@@ -107,6 +107,7 @@ static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
     o = 0;
     L->off_skeys = o;      o = pl_align(o + S * L->CW * 16);
     L->off_table = o;      o = pl_align(o + ((size_t)1 << lg) * 4);
+    L->off_filter = o;     o = pl_align(o + ((size_t)1 << lg));
     L->off_owner = o;      o = pl_align(o + S * 4);
     L->off_vid_of = o;     o = pl_align(o + S * 4);
     L->off_vkeys = o;      o = pl_align(o + S * L->CW * 16);

@@ -57,7 +57,8 @@ def _layout(h, w, pd, vd):
         lat[name] = o
         o = _align(o + sz)
     lat_bytes, scr, o = o, {}, 0
-    for name, sz in [("skeys", S * CW * 16), ("table", (1 << lg) * 4), ("owner", S * 4), ("vid_of", S * 4),
+    for name, sz in [("skeys", S * CW * 16), ("table", (1 << lg) * 4), ("filter", 1 << lg), ("owner", S * 4),
+                     ("vid_of", S * 4),
                      ("vkeys", S * CW * 16), ("vf0", S * CPf * 4), ("vf1", S * CPf * 4)]:
         scr[name] = o
         o = _align(o + sz)
@@ -112,6 +113,24 @@ CASES = [f for f in golden_files() if f.startswith("ref_randn24x20_")] + ["ref_r
 
 @pytest.mark.parametrize("fn", CASES)
 def test_lattice_invariants(fn, dev):
+    _check_invariants(fn, dev)
+
+
+@pytest.mark.parametrize("fn", ["ref_randn24x20_pd2_vd3.npz", "ref_randn24x20_pd5_vd6.npz",
+                                "ref_randn24x20_pd16_vd1.npz", "ref_ragged13x29_pd5_vd3.npz"])
+def test_lattice_invariants_with_miss_filter(fn, dev):
+    """The neighbour lookups through the miss filter, which by default only
+    large tables use, forced on for small ones: the same exact neighbours."""
+    from plattice_pytorch_b200 import _lib
+    L = _lib.lib()
+    try:
+        L.plattice_debug_set_miss_filter_log2(6)
+        _check_invariants(fn, dev)
+    finally:
+        L.plattice_debug_set_miss_filter_log2(0)
+
+
+def _check_invariants(fn, dev):
     from plattice_pytorch_b200 import PLOO, _lib
     d = np.load(os.path.join(GOLDEN, fn))
     f, v = d["features"], d["values"]
