@@ -236,10 +236,11 @@ __device__ __forceinline__ uint32_t axis_lin_step(int c) {
 
 // ---------------------------------------------------------------- lattice embedding
 
-// float -> int16 as the device conversion does it: truncate, saturate
+// float -> int16 as the device conversion does it: truncate, saturate, NaN -> 0
 __device__ __forceinline__ int f2s16(float x) {
-    int r = __float2int_rz(x);
-    return r < -32768 ? -32768 : (r > 32767 ? 32767 : r);
+    short r;
+    asm("cvt.rzi.s16.f32 %0, %1;" : "=h"(r) : "f"(x));
+    return (int)r;
 }
 
 // Greedy remainder-0 point g, simplex rank and barycentric weights of one
@@ -262,7 +263,8 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
     }
     e[0] = __fmaf_rn(__fmul_rn(2.0f, f[0]), ec.sf[0], e[1]);
 
-    // nearest multiple of K per coordinate; the running sum is int16
+    // nearest multiple of K per coordinate; the running sum is int16 (wrapped
+    // once at the end: addition mod 2^16 does not depend on where it wraps)
     int sum = 0;
 #pragma unroll
     for (int i = 0; i < K; ++i) {
@@ -270,9 +272,9 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
         const float up = __fmul_rn(ceilf(v), ec.kf);
         const float dn = __fmul_rn(floorf(v), ec.kf);
         g[i] = f2s16((__fsub_rn(up, e[i]) < __fsub_rn(e[i], dn)) ? up : dn);   // one conversion
-        sum = (int16_t)(sum + g[i]);
+        sum += g[i];
     }
-    sum = (int16_t)(sum / K);
+    sum = (int16_t)((int16_t)sum / K);
 
     // rank by counting, ties to the lower index
     float d[K];
@@ -286,18 +288,19 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
         rank[i] = r;
     }
 
-    // move the greedy point onto the hyperplane
-    if (sum > 0) {
+    // move the greedy point onto the hyperplane, without branches: for sum > 0
+    // the coordinates of rank >= K - sum move by -K, for sum < 0 those of rank
+    // < -sum (K-1-rank >= K + sum) move by +K, for sum == 0 none (threshold K);
+    // every rank then shifts by sum plus the move
+    {
+        const bool flip = sum < 0;
+        const int thr = K - (flip ? -sum : sum);
+        const int step = flip ? K : -K;
 #pragma unroll
         for (int i = 0; i < K; ++i) {
-            if (rank[i] >= K - sum) { g[i] -= K; rank[i] += sum - K; }
-            else                    { rank[i] += sum; }
-        }
-    } else if (sum < 0) {
-#pragma unroll
-        for (int i = 0; i < K; ++i) {
-            if (rank[i] < -sum) { g[i] += K; rank[i] += K + sum; }
-            else                { rank[i] += sum; }
+            const int mv = ((flip ? K - 1 - rank[i] : rank[i]) >= thr) ? step : 0;
+            g[i] += mv;
+            rank[i] += sum + mv;
         }
     }
 
@@ -430,7 +433,6 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
              float* zero_f, int cpf, float* zero_b, int cpb) {
     using C = Cfg<PD>;
     constexpr int K = C::K, P = C::P, CW = C::CW, NW = C::NW, SLOTS = C::SLOTS, SC = C::SC;
-    constexpr bool KEEP_KEYS = K * NW <= 32;   // keep key words in registers when small
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint4* ukeys = reinterpret_cast<uint4*>(smem_raw);                  // [SLOTS][CW]
     int* stab = reinterpret_cast<int*>(ukeys + SLOTS * CW);             // [SC]
@@ -457,7 +459,6 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     for (int i = t; i < SC; i += P) stab[i] = -1;
 
     // 2a. candidate key records (visible to other lanes' CAS winners after the fence)
-    uint32_t keys[KEEP_KEYS ? K : 1][NW];
 #pragma unroll
     for (int c = 0; c < K; ++c) {
         uint32_t kw[NW];
@@ -466,10 +467,6 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
 #pragma unroll
             for (int w = 0; w < CW; ++w)
                 ukeys[(t * K + c) * CW + w] = make_uint4(kw[4 * w], kw[4 * w + 1], kw[4 * w + 2], kw[4 * w + 3]);
-        }
-        if constexpr (KEEP_KEYS) {
-#pragma unroll
-            for (int k = 0; k < NW; ++k) keys[c][k] = kw[k];
         }
     }
     __syncthreads();   // table initialised, records written
@@ -482,12 +479,11 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
 #pragma unroll
     for (int c = 0; c < K; ++c) {
         const int cand = t * K + c;
-        uint32_t kw[NW];
-        if constexpr (KEEP_KEYS) {
+        uint32_t kw[NW];   // my record, read back (an inactive lane's is never used)
 #pragma unroll
-            for (int k = 0; k < NW; ++k) kw[k] = keys[c][k];
-        } else {
-            make_key<PD>(g, rank, c, kw);
+        for (int w = 0; w < CW; ++w) {
+            const uint4 r = ukeys[cand * CW + w];
+            kw[4 * w] = r.x; kw[4 * w + 1] = r.y; kw[4 * w + 2] = r.z; kw[4 * w + 3] = r.w;
         }
         const unsigned grp = __match_any_sync(kFull, kw[0]) & amask;
         const int leader = active ? __ffs(grp) - 1 : lane;
