@@ -372,7 +372,7 @@ def kernel_bytes(stage, n, pd, vd, m, u, cap_log2):
     slot = 6 * K * n   # uint16 local id + float weight per slot
     return {
         "tile_build": n * 4 * pd + slot + u * (16 * CW + 4 * (CPF + CPB)),
-        "clear": (1 << cap_log2) * 16 * CW,
+        "clear": (1 << cap_log2) * (5 if cap_log2 >= 22 else 4),   # cells, + the miss filter's byte per cell
         "insert": u * (2 * 16 * CW + 8) + m * (2 * 16 * CW + 8),   # insert + compaction
         "splat_fwd": slot + n * 4 * vd + m * 4 * CPF,
         "neighbors": m * (16 * CW + 8 * K),
