@@ -1014,7 +1014,7 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
                 r[4 * m] = a.x; r[4 * m + 1] = a.y; r[4 * m + 2] = a.z; r[4 * m + 3] = a.w;
             }
 #pragma unroll
-            for (int j = 0; j < NC; ++j) cur[j] = __fadd_rn(cur[j], (FWD && j == V) ? w : __fmul_rn(r[j], w));
+            for (int j = 0; j < NC; ++j) cur[j] = (FWD && j == V) ? __fadd_rn(cur[j], w) : __fmaf_rn(r[j], w, cur[j]);
         }
     }
     // merge the pieces of a run that crosses lanes: a segmented inclusive sum
