@@ -67,6 +67,9 @@ def parse_args():
     ap.add_argument("--kept-lattice", action="store_true",
                     help="time filter forward + backward on a lattice built once (a mean-field "
                          "iteration), next to the full forward + backward; 1 GPU, ours only")
+    ap.add_argument("--lattice-precision", choices=["fp32", "bf16"], default="fp32",
+                    help="ours: lattice rows of the blur's streaming passes (large lattices) in float "
+                         "or bfloat16 (PLOO.set_lattice_precision; off by default)")
     return ap.parse_args()
 
 
@@ -496,6 +499,9 @@ def main():
         world_eff = 1
     else:
         fn = ours_impl()
+        if args.lattice_precision != "fp32":
+            from plattice_pytorch_b200 import PLOO
+            PLOO.set_lattice_precision(args.lattice_precision)
         dist_init(world, local)
         world_eff = world
 
@@ -569,7 +575,10 @@ def main():
     res = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_eff, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_dev / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if args.lattice_precision == "fp32" or args.impl == "reference"
+                 else "f32 (bf16 rows in the streaming blur passes)",
+        "data": "synthetic",
         "config": {"workload": args.workload, "h": h, "w": w, "pd": pd, "vd": vd,
                    "images_per_gpu": n_images,
                    "l2": "flushed between timed steps (256 MiB write, outside the events)",

@@ -169,6 +169,23 @@ void plattice_debug_set_table_cap_log2(int log2_cells);
  * called from precomputeBlurNeighbors, permutohedral.cu:350-383). */
 void plattice_debug_set_miss_filter_log2(int log2_cells);
 
+/* Reduced-precision lattice values (off by default; process-wide, read when a
+ * call is enqueued).  bits = 16: the blur passes of large lattices (more
+ * vertices than the blur grid keeps in registers, about 150 k) store the rows
+ * they write as bfloat16 and read them back widened, with float arithmetic;
+ * the splat still accumulates in float and the slice reads float rows.
+ * Outputs then differ from the float path by the bfloat16 rounding of up to
+ * pd+1 passes (about 1 % of the output's range; the tests bound it at 2 %).
+ * bits = 32 (default): float everywhere.  Returns PLATTICE_ERR_INVALID for any
+ * other value.  The reference computes in float only (permutohedral.cu:321-348). */
+int plattice_set_lattice_precision(int bits);
+int plattice_get_lattice_precision(void);
+
+/* Test support: run the blur's streaming passes (the large-lattice path, with
+ * one grid barrier per pass) for every lattice, so that small cases exercise
+ * them (0 = automatic choice by size). */
+void plattice_debug_set_blur_streaming(int on);
+
 /* Forward filter for callers that cannot allocate device memory (no
  * counterpart in the reference, whose host layer allocates a new workspace on
  * every call).  Same computation and outputs as plattice_forward, but the

@@ -434,3 +434,21 @@ def vertex_keys(lattice):
     if rc != _lib.OK:
         raise _lib.PlatticeError("plattice_vertex_keys", rc)
     return keys[:mm.value]
+
+
+def set_lattice_precision(precision):
+    """Lattice value precision of the blur passes of large lattices (more
+    vertices than the blur grid keeps in registers): ``"fp32"`` (default) or
+    ``"bf16"`` (rows stored as bfloat16 between passes, float arithmetic).
+    Process-wide; applies to calls enqueued afterwards.  No counterpart in the
+    reference, which computes in float only (permutohedral.cu:321-348)."""
+    bits = {"fp32": 32, "bf16": 16}.get(precision)
+    _require(bits is not None, f"lattice precision must be 'fp32' or 'bf16', got {precision!r}")
+    rc = _lib.lib().plattice_set_lattice_precision(bits)
+    if rc != _lib.OK:
+        raise _lib.PlatticeError("plattice_set_lattice_precision", rc)
+
+
+def get_lattice_precision():
+    """``"fp32"`` or ``"bf16"``: the setting of set_lattice_precision."""
+    return "bf16" if _lib.lib().plattice_get_lattice_precision() == 16 else "fp32"

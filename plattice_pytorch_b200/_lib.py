@@ -86,6 +86,12 @@ def lib():
         L.plattice_debug_set_table_cap_log2.argtypes = [I]
         L.plattice_debug_set_miss_filter_log2.restype = None
         L.plattice_debug_set_miss_filter_log2.argtypes = [I]
+        L.plattice_set_lattice_precision.restype = I
+        L.plattice_set_lattice_precision.argtypes = [I]
+        L.plattice_get_lattice_precision.restype = I
+        L.plattice_get_lattice_precision.argtypes = []
+        L.plattice_debug_set_blur_streaming.restype = None
+        L.plattice_debug_set_blur_streaming.argtypes = [I]
         L.plattice_profile_enable.restype = None
         L.plattice_profile_enable.argtypes = [I]
         L.plattice_profile_read.restype = I

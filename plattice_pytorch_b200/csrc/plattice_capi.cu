@@ -26,6 +26,10 @@ PL_DECLARE_PD(13) PL_DECLARE_PD(14) PL_DECLARE_PD(15) PL_DECLARE_PD(16)
 
 static int g_cap_override_log2 = 0;
 static int g_filter_min_log2 = 0;
+static int g_blur_half = 0;     // bfloat16 rows in the streaming blur passes
+static int g_blur_stream = 0;   // test support: streaming blur passes for every lattice
+
+static int blur_flags() { return (g_blur_half ? pl::kBlurHalf : 0) | (g_blur_stream ? pl::kBlurStream : 0); }
 
 // ---------------------------------------------------------------- side stream
 
@@ -249,6 +253,7 @@ int plattice_forward(float* weight_out, float* out, const float* values, const f
     a.lattice_state = 0;
     a.cap_override_log2 = g_cap_override_log2;
     a.filter_min_log2 = g_filter_min_log2;
+    a.blur_flags = blur_flags();
     return cuda_status(dispatch_forward(a), "plattice_forward");
 }
 
@@ -273,6 +278,7 @@ int plattice_backward(float* grad_values_out, const float* grad, const float* we
     a.lattice_state = lattice_state;
     a.cap_override_log2 = g_cap_override_log2;
     a.filter_min_log2 = g_filter_min_log2;
+    a.blur_flags = blur_flags();
     return cuda_status(dispatch_backward(a), "plattice_backward");
 }
 
@@ -374,6 +380,7 @@ static int kept_lattice_args(pl::CallArgs& a, size_t lattice_bytes, void* ws, si
     a.sm_count = sm_count_current();
     a.cap_override_log2 = g_cap_override_log2;
     a.filter_min_log2 = g_filter_min_log2;
+    a.blur_flags = blur_flags();
     return PLATTICE_OK;
 }
 
@@ -476,6 +483,7 @@ int plattice_feature_grad(float* grad_features_out, const float* grad, const flo
     a.sm_count = sm_count_current();
     a.cap_override_log2 = g_cap_override_log2;
     a.filter_min_log2 = g_filter_min_log2;
+    a.blur_flags = blur_flags();
     return cuda_status(dispatch_feature_grad(a), "plattice_feature_grad");
 }
 
@@ -550,5 +558,15 @@ void plattice_debug_set_table_cap_log2(int log2_cells) {
 void plattice_debug_set_miss_filter_log2(int log2_cells) {
     g_filter_min_log2 = (log2_cells > 0 && log2_cells < 31) ? log2_cells : 0;
 }
+
+int plattice_set_lattice_precision(int bits) {
+    if (bits != 32 && bits != 16) return PLATTICE_ERR_INVALID;
+    g_blur_half = bits == 16;
+    return PLATTICE_OK;
+}
+
+int plattice_get_lattice_precision(void) { return g_blur_half ? 16 : 32; }
+
+void plattice_debug_set_blur_streaming(int on) { g_blur_stream = on ? 1 : 0; }
 
 }  // extern "C"

@@ -25,6 +25,7 @@ struct CallArgs {
     int lattice_state;       // backward: 0 rebuild, 1 fresh from forward, 2 reuse (re-zero)
     int cap_override_log2;
     int filter_min_log2;     // 0: the default (tables of 2^22 cells and more)
+    int blur_flags;          // kBlurHalf (bfloat16 rows of large lattices), kBlurStream (tests)
     float* vbuf0;            // value buffers of a filter call on a kept lattice (else null:
     float* vbuf1;            // the forward's scratch rows / the lattice's backward rows)
     // feature gradient: dL/dout, the forward's out, and lattice rows / flags in the workspace
@@ -196,7 +197,7 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
               e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), 0, a.stream, true, Lv, b0, b1,
-                           reverse, final_flag));
+                           reverse, final_flag, a.blur_flags));
     return e;
 }
 

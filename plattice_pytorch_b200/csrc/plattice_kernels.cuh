@@ -27,6 +27,7 @@
 // is bit-identical to the reference and independent of this file's own
 // compiler flags.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -167,6 +168,46 @@ __device__ __forceinline__ void store_row(float* p, const float (&v)[CP]) {
 #pragma unroll
         for (int j = 0; j < CP; j += 4)
             *reinterpret_cast<float4*>(p + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    }
+}
+
+// Rows of CP bfloat16 values (the reduced-precision blur rows of large
+// lattices): a bf16 value is the upper half of a float, so widening is exact;
+// narrowing rounds to nearest even.  Rows of 4k values are 8k bytes, read and
+// written as 8-byte words (their offsets are multiples of 8 bytes).
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ uint32_t bf16_pack(float lo, float hi) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <int CP>
+__device__ __forceinline__ void load_row_bf16(const uint16_t* p, float (&v)[CP]) {
+    if constexpr (CP == 1) {
+        v[0] = __uint_as_float((uint32_t)__ldcg(reinterpret_cast<const unsigned short*>(p)) << 16);
+    } else if constexpr (CP == 2) {
+        const uint32_t w = __ldcg(reinterpret_cast<const unsigned int*>(p));
+        v[0] = bf16_lo(w); v[1] = bf16_hi(w);
+    } else {
+#pragma unroll
+        for (int j = 0; j < CP; j += 4) {
+            const uint2 w = __ldcg(reinterpret_cast<const uint2*>(p + j));
+            v[j] = bf16_lo(w.x); v[j + 1] = bf16_hi(w.x); v[j + 2] = bf16_lo(w.y); v[j + 3] = bf16_hi(w.y);
+        }
+    }
+}
+
+template <int CP>
+__device__ __forceinline__ void store_row_bf16(uint16_t* p, const float (&v)[CP]) {
+    if constexpr (CP == 1) {
+        *p = (uint16_t)(bf16_pack(v[0], 0.0f) & 0xFFFFu);
+    } else if constexpr (CP == 2) {
+        *reinterpret_cast<uint32_t*>(p) = bf16_pack(v[0], v[1]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < CP; j += 4)
+            *reinterpret_cast<uint2*>(p + j) = make_uint2(bf16_pack(v[j], v[j + 1]), bf16_pack(v[j + 2], v[j + 3]));
     }
 }
 
@@ -1153,17 +1194,41 @@ __device__ __forceinline__ void blur_at(const float* x, int u, int2 n, float (&r
     blur_row<W>(me, a, b, n, r);
 }
 
+// Where a vertex's current row of a streaming blur lives, and how many
+// halvings are still to be applied to it: one state byte per vertex and pass
+// parity, location in bits 6-7, pending halvings (at most K) in bits 0-5.
+// Locations: 0 = buf0 (float, where the splat left it), 1 = buf1 (float),
+// 2 / 3 = the two bfloat16 row arrays that share buf1's memory in the
+// reduced-precision mode.  A row is only ever rewritten into another location
+// than the one the pass reads it from.
+constexpr int kLocBuf0 = 0, kLocBuf1 = 1, kLocH0 = 2, kLocH1 = 3;
+
+template <int CP, bool HALF>
+__device__ __forceinline__ void load_loc(int loc, int v, const float* buf0, const float* buf1, const uint16_t* h0,
+                                         const uint16_t* h1, float (&r)[CP]) {
+    if (!HALF || loc < kLocH0) load_row_cg<CP>((loc == kLocBuf0 ? buf0 : buf1) + (size_t)v * CP, r);
+    else                       load_row_bf16<CP>((loc == kLocH0 ? h0 : h1) + (size_t)v * CP, r);
+}
+
+template <int CP, bool HALF>
+__device__ __forceinline__ void store_loc(int loc, int v, float* buf0, float* buf1, uint16_t* h0, uint16_t* h1,
+                                          const float (&r)[CP]) {
+    if (!HALF) store_row<CP>((loc == kLocBuf0 ? buf0 : buf1) + (size_t)v * CP, r);
+    else       store_row_bf16<CP>((loc == kLocH0 ? h0 : h1) + (size_t)v * CP, r);
+}
+
 // Larger lattices stream every row, one pass per step.  A vertex without a
 // neighbour along the pass's axis only halves (0.25 * (2 x) = x / 2, exact in
 // float): its row is left where it is and the halving is recorded in its
-// state byte (bit 7: the buffer holding the row, bits 0-6: pending halvings);
-// the rows that are read are scaled by their pending powers of two first,
-// which is exact too, so the values are those of the plain sequence of
-// passes.  The indices and states of VPT vertices are requested together.
-// Each thread owns the same vertices in every pass and finally gathers its
-// rows, scaled, into buf0.  (A separate function, so that its registers do
-// not weigh on the resident path.)
-template <int PD, int CP>
+// state byte; the rows that are read are scaled by their pending powers of
+// two first, which is exact too, so the values are those of the plain
+// sequence of passes.  The indices and states of VPT vertices are requested
+// together.  Each thread owns the same vertices in every pass and finally
+// gathers its rows, scaled, into buf0 as floats.  With HALF, the rows a pass
+// writes are stored as bfloat16 (half the row bytes; the arithmetic stays
+// float), in two arrays of M rows laid out in buf1.  (A separate function, so
+// that its registers do not weigh on the resident path.)
+template <int PD, int CP, bool HALF>
 __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, LatticeHeader* hdr, float* buf0,
                                             float* buf1, int reverse, int* final_flag, int M, int tid, int stride) {
     constexpr int K = PD + 1;
@@ -1171,6 +1236,8 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
     unsigned phase = 0;
     uint8_t* const st0 = bstate;
     uint8_t* const st1 = bstate + M;
+    uint16_t* const h0 = reinterpret_cast<uint16_t*>(buf1);
+    uint16_t* const h1 = h0 + (size_t)M * CP;
 #pragma unroll 1
     for (int s = 0; s < K; ++s) {
         const int ax = reverse ? K - 1 - s : s;
@@ -1195,40 +1262,46 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
             for (int k = 0; k < VPT; ++k) {
                 const int v = v0 + k * stride;
                 if (v >= M) continue;
-                const int bv = cv[k] >> 7, ev = cv[k] & 127;
+                const int lv = cv[k] >> 6, ev = cv[k] & 63;
                 if (n[k].x < 0 && n[k].y < 0) {
-                    sn[v] = (uint8_t)((bv << 7) | (ev + 1));
+                    sn[v] = (uint8_t)((lv << 6) | (ev + 1));
                     continue;
                 }
                 float me[CP], a[CP], b[CP], r[CP];
-                load_row_cg<CP>((bv ? buf1 : buf0) + (size_t)v * CP, me);
-                if (n[k].x >= 0) load_row_cg<CP>(((ca[k] >> 7) ? buf1 : buf0) + (size_t)n[k].x * CP, a);
-                if (n[k].y >= 0) load_row_cg<CP>(((cb[k] >> 7) ? buf1 : buf0) + (size_t)n[k].y * CP, b);
+                load_loc<CP, HALF>(lv, v, buf0, buf1, h0, h1, me);
+                if (n[k].x >= 0) load_loc<CP, HALF>(ca[k] >> 6, n[k].x, buf0, buf1, h0, h1, a);
+                if (n[k].y >= 0) load_loc<CP, HALF>(cb[k] >> 6, n[k].y, buf0, buf1, h0, h1, b);
                 scale_pow2<CP>(me, ev);
-                if (n[k].x >= 0) scale_pow2<CP>(a, ca[k] & 127);
-                if (n[k].y >= 0) scale_pow2<CP>(b, cb[k] & 127);
+                if (n[k].x >= 0) scale_pow2<CP>(a, ca[k] & 63);
+                if (n[k].y >= 0) scale_pow2<CP>(b, cb[k] & 63);
                 blur_row<CP>(me, a, b, n[k], r);
-                store_row<CP>((bv ? buf0 : buf1) + (size_t)v * CP, r);
-                sn[v] = (uint8_t)((1 - bv) << 7);
+                const int nl = HALF ? (lv == kLocH0 ? kLocH1 : kLocH0) : (lv ^ 1);
+                store_loc<CP, HALF>(nl, v, buf0, buf1, h0, h1, r);
+                sn[v] = (uint8_t)(nl << 6);
             }
         }
-        if (s + 1 < K) grid_barrier(hdr, phase);
+        // after the last pass too: the gather below rewrites buf0 rows that
+        // neighbours may still be reading in that pass
+        grid_barrier(hdr, phase);
     }
     const uint8_t* sf = (K & 1) ? st1 : st0;
-    for (int v = tid; v < M; v += stride) {   // my own vertices: written by me in the last pass
+    for (int v = tid; v < M; v += stride) {   // my own vertices
         const int c = (int)sf[v];
         if (c == 0) continue;
         float r[CP];
-        load_row_cg<CP>(((c >> 7) ? buf1 : buf0) + (size_t)v * CP, r);
-        scale_pow2<CP>(r, c & 127);
+        load_loc<CP, HALF>(c >> 6, v, buf0, buf1, h0, h1, r);
+        scale_pow2<CP>(r, c & 63);
         store_row<CP>(buf0 + (size_t)v * CP, r);
     }
     if (tid == 0) *final_flag = 0;
 }
 
+constexpr int kBlurHalf = 1;     // flags of k_blur_all: bfloat16 rows in the streaming passes
+constexpr int kBlurStream = 2;   // the streaming passes whatever the lattice's size (tests)
+
 template <int PD, int CP>
 __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse,
-                                                             int* final_flag) {
+                                                             int* final_flag, int flags) {
     constexpr int K = PD + 1;
     constexpr int R = CP <= 2 ? 2 : 1;        // vertices per thread kept in registers
     constexpr int W = CP < 4 ? CP : 4;         // channels per group (the stencil is per channel)
@@ -1238,7 +1311,7 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
     unsigned phase = 0;
     float* x = buf0;
     float* y = buf1;
-    if (M <= stride * R) {
+    if (M <= stride * R && !(flags & kBlurStream)) {
         auto axis = [&](int k) { return k >= K ? -1 : (reverse ? K - 1 - k : k); };
         float me[R][CP];
         BlurIdx idx[R];
@@ -1291,7 +1364,10 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
         if (tid == 0) *final_flag = (x == buf1) ? 1 : 0;
         return;
     }
-    blur_streaming<PD, CP>(L.nbr, L.bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
+    if (flags & kBlurHalf)
+        blur_streaming<PD, CP, true>(L.nbr, L.bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
+    else
+        blur_streaming<PD, CP, false>(L.nbr, L.bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
 }
 
 // ---------------------------------------------------------------- slice

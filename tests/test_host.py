@@ -126,6 +126,26 @@ def test_feature_grad_sizes_and_argument_checks(lib):
     assert lib.plattice_feature_grad(*small) == _lib.ERR_WORKSPACE
 
 
+def test_lattice_precision_setting(lib):
+    """Host side of the reduced-precision lattice values: only 32 and 16 bits
+    are accepted, the setting reads back, and the Python wrapper checks its
+    argument (no GPU call)."""
+    from plattice_pytorch_b200 import PLOO
+    from plattice_pytorch_b200 import _lib
+    try:
+        assert lib.plattice_get_lattice_precision() == 32
+        assert lib.plattice_set_lattice_precision(8) == _lib.ERR_INVALID
+        assert lib.plattice_get_lattice_precision() == 32
+        assert lib.plattice_set_lattice_precision(16) == _lib.OK
+        assert PLOO.get_lattice_precision() == "bf16"
+        PLOO.set_lattice_precision("fp32")
+        assert lib.plattice_get_lattice_precision() == 32
+        with pytest.raises(RuntimeError, match="lattice precision"):
+            PLOO.set_lattice_precision("fp16")
+    finally:
+        lib.plattice_set_lattice_precision(32)
+
+
 def test_python_checks_raise_reference_messages():
     from plattice_pytorch_b200 import PLOO
     f = torch.zeros(4, 4, 5)
