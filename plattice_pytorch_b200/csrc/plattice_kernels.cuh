@@ -267,12 +267,18 @@ __device__ __forceinline__ uint32_t key_lin_words(const uint32_t* kw) {
 
 // the change of the linear part for the blur step along axis c: every
 // coordinate +1, and coordinate c -K when c < PD (permutohedral.cu:368-375)
+__host__ __device__ constexpr uint32_t coord_mul_sum(int pd) { return pd <= 0 ? 0u : coord_mul(pd - 1) + coord_mul_sum(pd - 1); }
+
+static __constant__ uint32_t c_coord_mul[16] = {coord_mul(0),  coord_mul(1),  coord_mul(2),  coord_mul(3),
+                                                coord_mul(4),  coord_mul(5),  coord_mul(6),  coord_mul(7),
+                                                coord_mul(8),  coord_mul(9),  coord_mul(10), coord_mul(11),
+                                                coord_mul(12), coord_mul(13), coord_mul(14), coord_mul(15)};
+
+// (axis c may be a run-time value: one constant-bank load)
 template <int PD>
 __device__ __forceinline__ uint32_t axis_lin_step(int c) {
-    uint32_t s = 0u;
-#pragma unroll
-    for (int i = 0; i < PD; ++i) s += coord_mul(i) * (i == c ? (uint32_t)(1 - (PD + 1)) : 1u);
-    return s;
+    constexpr uint32_t all = coord_mul_sum(PD);
+    return c < PD ? all - (uint32_t)(PD + 1) * c_coord_mul[c] : all;
 }
 
 // ---------------------------------------------------------------- lattice embedding
@@ -858,7 +864,7 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
 // with evict-first hints, so that the hash table, which every lookup probes at
 // random, stays resident in L2.
 template <int PD>
-__global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S) {
+__global__ void __launch_bounds__(256, PD <= 6 ? 8 : 4) k_neighbors(Geo geo, LatView L, ScrView S) {
     constexpr int K = PD + 1, CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
     const int M = L.hdr->m;
     if (M <= 0) return;
@@ -888,7 +894,8 @@ __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S
             const int x = key_coord(key, i);
             edge = edge || x > 32767 - K || x < -32768 + K;
         }
-        for (int c = g; c < K; c += G) {
+        // the lookups of axis c: both cells read, then probed and compared
+        auto axis_pair = [&](int c) {
             uint32_t hp, hm;
             if (!edge) {
                 const uint32_t d = axis_lin_step<PD>(c);
@@ -908,11 +915,38 @@ __global__ void __launch_bounds__(256) k_neighbors(Geo geo, LatView L, ScrView S
                 inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
             }
             const uint32_t ca = ina ? __ldg(S.table + pa) : 0u, cb = inb ? __ldg(S.table + pb) : 0u;
-            const int a = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, 1, hp, pa, ca,
-                                             &L.hdr->status);
-            const int b = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, -1, hm, pb, cb,
-                                             &L.hdr->status);
-            __stcs(L.nbr + (size_t)c * M + v, make_int2(a, b));   // streamed, as the key loads
+            const int na = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, 1, hp, pa, ca,
+                                              &L.hdr->status);
+            const int nb = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, -1, hm, pb, cb,
+                                              &L.hdr->status);
+            __stcs(L.nbr + (size_t)c * M + v, make_int2(na, nb));   // streamed, as the key loads
+        };
+        // sparse lattices (large tables): a first sweep settles every axis
+        // whose two lookups the filter or an empty home cell rule out, which
+        // is most of them, with a few instructions each; the rest take the
+        // full probe and key compare after it, so a warp runs that path about
+        // as often as its busiest lane has candidates rather than once for
+        // every axis on which any lane has one
+        uint32_t pend = 0u;   // the axes still to look up, one bit each
+        if (use_filter && G == 1 && !edge) {
+#pragma unroll 1
+            for (int c = 0; c < K; ++c) {
+                const uint32_t d = axis_lin_step<PD>(c);
+                const uint32_t hp = hash_of_lin(lin + d), hm = hash_of_lin(lin - d);
+                const bool ina = (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
+                const bool inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
+                const uint32_t ca = ina ? __ldg(S.table + (hp & mask)) : 0u;
+                const uint32_t cb = inb ? __ldg(S.table + (hm & mask)) : 0u;
+                if ((ca | cb) != 0u) pend |= 1u << c;
+                else __stcs(L.nbr + (size_t)c * M + v, make_int2(-1, -1));
+            }
+        } else {
+            for (int c = g; c < K; c += G) pend |= 1u << c;
+        }
+        while (pend != 0u) {
+            const int c = __ffs(pend) - 1;
+            pend &= pend - 1u;
+            axis_pair(c);
         }
     }
 }
