@@ -325,22 +325,32 @@ def timed_e2e(fn, host, steps, dev):
     comp = torch.cuda.default_stream(dev)
     outs = [[(torch.empty(h[1].shape, pin_memory=True), torch.empty(h[1].shape, pin_memory=True))
              for h in host] for _ in range(2)]
+    # device input buffers of RING steps, reused once the step that read them
+    # has finished; the host waits for that step before reusing its slot, so it
+    # runs at most RING steps ahead (a bounded queue, as in a serving loop, and
+    # no allocator growth inside the timed loop)
+    RING = 3
+    dins = [[tuple(torch.empty(x.shape, dtype=x.dtype, device=dev) for x in hh) for hh in host]
+            for _ in range(RING)]
+    freed = [None] * RING
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(comp)
     for i in range(steps):
+        r = i % RING
+        if freed[r] is not None:
+            freed[r].synchronize()
         for k, (hf, hv, hg) in enumerate(host):
             ho, hgr = outs[i % 2][k]
+            f, v, g = dins[r][k]
             with torch.cuda.stream(s_in):
-                f = hf.to(dev, non_blocking=True)
-                v = hv.to(dev, non_blocking=True)
-                g = hg.to(dev, non_blocking=True)
+                f.copy_(hf, non_blocking=True)
+                v.copy_(hv, non_blocking=True)
+                g.copy_(hg, non_blocking=True)
             comp.wait_stream(s_in)
-            for t in (f, v, g):
-                t.record_stream(comp)
             with torch.cuda.stream(comp):
-                out, gv = step(fn, f, v.requires_grad_(True), g)
+                out, gv = step(fn, f, v.detach().requires_grad_(True), g)
                 out = out.detach()
             s_out.wait_stream(comp)
             out.record_stream(s_out)
@@ -348,6 +358,8 @@ def timed_e2e(fn, host, steps, dev):
             with torch.cuda.stream(s_out):
                 ho.copy_(out, non_blocking=True)
                 hgr.copy_(gv, non_blocking=True)
+        freed[r] = torch.cuda.Event()
+        freed[r].record(comp)
     comp.wait_stream(s_in)
     comp.wait_stream(s_out)
     e1.record(comp)
