@@ -189,15 +189,17 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     if (e != cudaSuccess) return e;
     int n = (dev >= 0 && dev < 64) ? per_sm[dev] : 0;
     if (n == 0) {
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_blur_all<PD, CP>, kBlurThreads, 0);
+        e = cudaFuncSetAttribute(k_blur_all<PD, CP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlurQueueBytes);
+        if (e != cudaSuccess) return e;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_blur_all<PD, CP>, kBlurThreads, kBlurQueueBytes);
         if (e != cudaSuccess) return e;
         if (n < 1) return cudaErrorLaunchOutOfResources;
         if (dev >= 0 && dev < 64) per_sm[dev] = n;
     }
     const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
-              e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), 0, a.stream, true, Lv, b0, b1,
-                           reverse, final_flag, a.blur_flags));
+              e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), kBlurQueueBytes, a.stream, true, Lv,
+                           b0, b1, reverse, final_flag, a.blur_flags));
     return e;
 }
 

@@ -1256,17 +1256,28 @@ __device__ __forceinline__ void store_loc(int loc, int v, float* buf0, float* bu
 // float): its row is left where it is and the halving is recorded in its
 // state byte; the rows that are read are scaled by their pending powers of
 // two first, which is exact too, so the values are those of the plain
-// sequence of passes.  The indices and states of VPT vertices are requested
-// together.  Each thread owns the same vertices in every pass and finally
-// gathers its rows, scaled, into buf0 as floats.  With HALF, the rows a pass
+// sequence of passes.  The indices and states of VPT vertices per lane are
+// requested together; the vertices of the warp's step that have neighbours go
+// through a per-warp queue in shared memory, one per lane, so that the row
+// work runs with every lane busy however sparse the axis is.  Each vertex
+// keeps its owner thread in every pass (isolated vertices) or its warp
+// (queued ones); the final gather, after a barrier, puts every row, scaled,
+// into buf0 as floats.  With HALF, the rows a pass
 // writes are stored as bfloat16 (half the row bytes; the arithmetic stays
 // float), in two arrays of M rows laid out in buf1.  (A separate function, so
 // that its registers do not weigh on the resident path.)
+constexpr int kBlurVpt = 4;   // vertices per lane whose indices and states are requested together
+constexpr int kBlurQueueBytes = kBlurThreads * kBlurVpt * 16;   // dynamic shared memory of k_blur_all
+
 template <int PD, int CP, bool HALF>
 __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, LatticeHeader* hdr, float* buf0,
                                             float* buf1, int reverse, int* final_flag, int M, int tid, int stride) {
     constexpr int K = PD + 1;
-    constexpr int VPT = 4;
+    constexpr int VPT = kBlurVpt;
+    extern __shared__ uint4 blur_queue[];   // per warp: its step's vertices with neighbours
+    const int lane = threadIdx.x & 31;
+    uint4* const q = blur_queue + (threadIdx.x >> 5) * (32 * VPT);
+    const int wbase = tid - lane;   // the warp's first vertex of a step: the loop below is warp-uniform
     unsigned phase = 0;
     uint8_t* const st0 = bstate;
     uint8_t* const st1 = bstate + M;
@@ -1278,12 +1289,12 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
         const int2* nb = nbr + (size_t)ax * M;
         const uint8_t* sc = (s & 1) ? st1 : st0;
         uint8_t* sn = (s & 1) ? st0 : st1;
-        for (int v0 = tid; v0 < M; v0 += stride * VPT) {
+        for (int w0 = wbase; w0 < M; w0 += stride * VPT) {
             int2 n[VPT];
             int cv[VPT], ca[VPT], cb[VPT];
 #pragma unroll
             for (int k = 0; k < VPT; ++k) {
-                const int v = v0 + k * stride;
+                const int v = w0 + lane + k * stride;
                 n[k] = v < M ? __ldg(nb + v) : make_int2(-1, -1);
                 cv[k] = (s == 0 || v >= M) ? 0 : (int)__ldcg(sc + v);
             }
@@ -1292,27 +1303,43 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
                 ca[k] = (s == 0 || n[k].x < 0) ? 0 : (int)__ldcg(sc + n[k].x);
                 cb[k] = (s == 0 || n[k].y < 0) ? 0 : (int)__ldcg(sc + n[k].y);
             }
+            // isolated vertices only count a halving; the others are queued, so
+            // that the lanes of the warp take them one each below
+            int total = 0;
 #pragma unroll
             for (int k = 0; k < VPT; ++k) {
-                const int v = v0 + k * stride;
-                if (v >= M) continue;
-                const int lv = cv[k] >> 6, ev = cv[k] & 63;
-                if (n[k].x < 0 && n[k].y < 0) {
-                    sn[v] = (uint8_t)((lv << 6) | (ev + 1));
-                    continue;
+                const int v = w0 + lane + k * stride;
+                const bool busy = n[k].x >= 0 || n[k].y >= 0;   // false beyond M
+                const unsigned m = __ballot_sync(kFull, busy);
+                if (busy) {
+                    q[total + __popc(m & ((1u << lane) - 1u))] =
+                        make_uint4((uint32_t)v, (uint32_t)n[k].x, (uint32_t)n[k].y,
+                                   (uint32_t)cv[k] | ((uint32_t)ca[k] << 8) | ((uint32_t)cb[k] << 16));
+                } else if (v < M) {
+                    sn[v] = (uint8_t)((cv[k] & ~63) | ((cv[k] & 63) + 1));
                 }
+                total += __popc(m);
+            }
+            __syncwarp();
+            for (int j = lane; j < total; j += 32) {
+                const uint4 e = q[j];
+                const int v = (int)e.x;
+                const int2 nv = make_int2((int)e.y, (int)e.z);
+                const int c0 = (int)(e.w & 255u), c1 = (int)((e.w >> 8) & 255u), c2 = (int)(e.w >> 16);
+                const int lv = c0 >> 6;
                 float me[CP], a[CP], b[CP], r[CP];
                 load_loc<CP, HALF>(lv, v, buf0, buf1, h0, h1, me);
-                if (n[k].x >= 0) load_loc<CP, HALF>(ca[k] >> 6, n[k].x, buf0, buf1, h0, h1, a);
-                if (n[k].y >= 0) load_loc<CP, HALF>(cb[k] >> 6, n[k].y, buf0, buf1, h0, h1, b);
-                scale_pow2<CP>(me, ev);
-                if (n[k].x >= 0) scale_pow2<CP>(a, ca[k] & 63);
-                if (n[k].y >= 0) scale_pow2<CP>(b, cb[k] & 63);
-                blur_row<CP>(me, a, b, n[k], r);
+                if (nv.x >= 0) load_loc<CP, HALF>(c1 >> 6, nv.x, buf0, buf1, h0, h1, a);
+                if (nv.y >= 0) load_loc<CP, HALF>(c2 >> 6, nv.y, buf0, buf1, h0, h1, b);
+                scale_pow2<CP>(me, c0 & 63);
+                if (nv.x >= 0) scale_pow2<CP>(a, c1 & 63);
+                if (nv.y >= 0) scale_pow2<CP>(b, c2 & 63);
+                blur_row<CP>(me, a, b, nv, r);
                 const int nl = HALF ? (lv == kLocH0 ? kLocH1 : kLocH0) : (lv ^ 1);
                 store_loc<CP, HALF>(nl, v, buf0, buf1, h0, h1, r);
                 sn[v] = (uint8_t)(nl << 6);
             }
+            __syncwarp();   // the queue is refilled by the next step
         }
         // after the last pass too: the gather below rewrites buf0 rows that
         // neighbours may still be reading in that pass
