@@ -169,7 +169,7 @@ cudaError_t neighbors_alongside(const CallArgs& a, const Geo& geo, const LatView
     cudaError_t e = side_fork(a.stream, &f);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_NEIGHBORS, f.side,
-              e = launch_k(k_neighbors<PD>, dim3(a.sm_count * 8), dim3(256), 0, f.side, false, geo, Lv, Sv));
+              e = launch_k(k_neighbors<PD>, dim3(a.sm_count * 8), dim3(kNbrThreads), 0, f.side, false, geo, Lv, Sv));
     const cudaError_t e1 = e == cudaSuccess ? main_work() : e;
     e = side_join(a.stream, &f);
     return e1 != cudaSuccess ? e1 : e;

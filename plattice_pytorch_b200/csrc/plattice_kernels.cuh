@@ -855,17 +855,81 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
     }
 }
 
-// Blur neighbours of every vertex: for axis c < PD the step is every
-// coordinate +1 (or -1) and coordinate c -K (or +K), for c == PD every
-// coordinate +1 (or -1) (permutohedral.cu:368-375).  A thread takes one
-// vertex and a group of axes (all of them when there are enough vertices to
-// occupy the grid), loads the vertex key once and issues the two lookups of
-// an axis together.  The vertex keys and the neighbour pairs are streamed
-// with evict-first hints, so that the hash table, which every lookup probes at
-// random, stays resident in L2.
+// The two blur neighbours of vertex v (key words `key`, linear part `lin`)
+// along axis c: for axis c < PD the step is every coordinate +1 (or -1) and
+// coordinate c -K (or +K), for c == PD every coordinate +1 (or -1)
+// (permutohedral.cu:368-375).  Both cells are read, then probed and compared;
+// the pair is stored streamed (evict-first).  A key within K of the int16
+// limits may wrap a coordinate (`edge`), so its neighbours' linear parts are
+// recomputed from their words.
 template <int PD>
-__global__ void __launch_bounds__(256, PD <= 6 ? 8 : 4) k_neighbors(Geo geo, LatView L, ScrView S) {
-    constexpr int K = PD + 1, CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
+__device__ __forceinline__ void neighbour_pair(const ScrView& S, const LatView& L, uint32_t mask, TableFmt f,
+                                               bool use_filter, const uint32_t (&key)[Cfg<PD>::NW], uint32_t lin,
+                                               bool edge, int v, int M, int c) {
+    constexpr int NW = Cfg<PD>::NW;
+    uint32_t hp, hm;
+    if (!edge) {
+        const uint32_t d = axis_lin_step<PD>(c);
+        hp = hash_of_lin(lin + d);
+        hm = hash_of_lin(lin - d);
+    } else {
+        uint32_t kw[NW];
+        neighbour_key<PD>(key, c, 1, 0u, kw);
+        hp = hash_of_lin(key_lin_words<PD>(kw));
+        neighbour_key<PD>(key, c, -1, 0u, kw);
+        hm = hash_of_lin(key_lin_words<PD>(kw));
+    }
+    const uint32_t pa = hp & mask, pb = hm & mask;
+    bool ina = true, inb = true;   // a cell reads as empty when the filter rules the key out
+    if (use_filter) {
+        ina = (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
+        inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
+    }
+    const uint32_t ca = ina ? __ldg(S.table + pa) : 0u, cb = inb ? __ldg(S.table + pb) : 0u;
+    const int na = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, 1, hp, pa, ca, &L.hdr->status);
+    const int nb = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, -1, hm, pb, cb, &L.hdr->status);
+    __stcs(L.nbr + (size_t)c * M + v, make_int2(na, nb));
+}
+
+template <int PD>
+__device__ __forceinline__ void load_vertex_key(const ScrView& S, int v, uint32_t (&key)[Cfg<PD>::NW], uint32_t& lin,
+                                                bool& edge) {
+    constexpr int K = PD + 1, CW = Cfg<PD>::CW;
+#pragma unroll
+    for (int w = 0; w < CW; ++w) {   // streamed (evict-first): the table stays in L2
+        const uint4 r = __ldcs(S.vkeys + (size_t)v * CW + w);
+        key[4 * w] = r.x; key[4 * w + 1] = r.y; key[4 * w + 2] = r.z; key[4 * w + 3] = r.w;
+    }
+    lin = key_lin_words<PD>(key);
+    edge = false;
+#pragma unroll
+    for (int i = 0; i < PD; ++i) {
+        const int x = key_coord(key, i);
+        edge = edge || x > 32767 - K || x < -32768 + K;
+    }
+}
+
+constexpr int kNbrThreads = 256;
+
+// Blur neighbours of every vertex.  The vertex keys and the neighbour pairs
+// are streamed with evict-first hints, so that the hash table, which every
+// lookup probes at random, stays resident in L2.
+//
+// Dense lattices (no miss filter: tables below 2^22 cells): a thread takes one
+// vertex and a group of axes (all of them when there are enough vertices to
+// occupy the grid), loads the vertex key once and issues the two lookups of an
+// axis together.
+//
+// Sparse lattices (large tables, most neighbours absent): a thread takes one
+// vertex and settles, in a first sweep, every axis whose two lookups the
+// filter or an empty home cell rule out, with a few instructions each.  The
+// remaining (vertex, axis) pairs of the warp go to a queue in shared memory
+// (with the vertices' keys) and the warp's lanes take them one each, so that
+// the full probe and key compare run with every lane busy.
+template <int PD>
+__global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo geo, LatView L, ScrView S) {
+    constexpr int K = PD + 1, NW = Cfg<PD>::NW;
+    constexpr int WARPS = kNbrThreads / 32;
     const int M = L.hdr->m;
     if (M <= 0) return;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
@@ -874,80 +938,76 @@ __global__ void __launch_bounds__(256, PD <= 6 ? 8 : 4) k_neighbors(Geo geo, Lat
     const int nthreads = gridDim.x * blockDim.x;
     int G = (nthreads + M - 1) / M;   // axis groups
     G = G < 1 ? 1 : (G > K ? K : G);
-    const size_t total = (size_t)M * G;
-    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += nthreads) {
-        const int g = (int)(idx / M);
-        const int v = (int)(idx - (size_t)g * M);
-        uint32_t key[NW];
-#pragma unroll
-        for (int w = 0; w < CW; ++w) {   // streamed (evict-first): the table stays in L2
-            const uint4 r = __ldcs(S.vkeys + (size_t)v * CW + w);
-            key[4 * w] = r.x; key[4 * w + 1] = r.y; key[4 * w + 2] = r.z; key[4 * w + 3] = r.w;
+    const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+    if (!(use_filter && G == 1)) {   // dense (uniform over the grid)
+        const size_t total = (size_t)M * G;
+        for (size_t idx = gtid; idx < total; idx += nthreads) {
+            const int g = (int)(idx / M);
+            const int v = (int)(idx - (size_t)g * M);
+            uint32_t key[NW], lin;
+            bool edge;
+            load_vertex_key<PD>(S, v, key, lin, edge);
+            for (int c = g; c < K; c += G) neighbour_pair<PD>(S, L, mask, f, use_filter, key, lin, edge, v, M, c);
         }
-        // hashes of the neighbours from the linear part of the key; a key within
-        // K of the int16 limits may wrap a coordinate, so its neighbours' linear
-        // parts are recomputed from their words instead
-        const uint32_t lin = key_lin_words<PD>(key);
-        bool edge = false;
-#pragma unroll
-        for (int i = 0; i < PD; ++i) {
-            const int x = key_coord(key, i);
-            edge = edge || x > 32767 - K || x < -32768 + K;
-        }
-        // the lookups of axis c: both cells read, then probed and compared
-        auto axis_pair = [&](int c) {
-            uint32_t hp, hm;
-            if (!edge) {
-                const uint32_t d = axis_lin_step<PD>(c);
-                hp = hash_of_lin(lin + d);
-                hm = hash_of_lin(lin - d);
+        return;
+    }
+    __shared__ uint32_t s_key[WARPS][NW][32];
+    __shared__ uint32_t s_lin[WARPS][32];
+    __shared__ uint16_t s_q[WARPS][32 * K];   // (lane << 5) | axis
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int wb = gtid - lane; wb < M; wb += nthreads) {   // warp-uniform
+        const int v = wb + lane;
+        uint32_t pend = 0u;   // my axes still to look up, one bit each
+        if (v < M) {
+            uint32_t key[NW], lin;
+            bool edge;
+            load_vertex_key<PD>(S, v, key, lin, edge);
+            if (edge) {
+                pend = (1u << K) - 1u;   // (the queue below recomputes edge hashes from the words)
             } else {
-                uint32_t kw[NW];
-                neighbour_key<PD>(key, c, 1, 0u, kw);
-                hp = hash_of_lin(key_lin_words<PD>(kw));
-                neighbour_key<PD>(key, c, -1, 0u, kw);
-                hm = hash_of_lin(key_lin_words<PD>(kw));
-            }
-            const uint32_t pa = hp & mask, pb = hm & mask;
-            bool ina = true, inb = true;   // a cell reads as empty when the filter rules the key out
-            if (use_filter) {
-                ina = (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
-                inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
-            }
-            const uint32_t ca = ina ? __ldg(S.table + pa) : 0u, cb = inb ? __ldg(S.table + pb) : 0u;
-            const int na = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, 1, hp, pa, ca,
-                                              &L.hdr->status);
-            const int nb = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, -1, hm, pb, cb,
-                                              &L.hdr->status);
-            __stcs(L.nbr + (size_t)c * M + v, make_int2(na, nb));   // streamed, as the key loads
-        };
-        // sparse lattices (large tables): a first sweep settles every axis
-        // whose two lookups the filter or an empty home cell rule out, which
-        // is most of them, with a few instructions each; the rest take the
-        // full probe and key compare after it, so a warp runs that path about
-        // as often as its busiest lane has candidates rather than once for
-        // every axis on which any lane has one
-        uint32_t pend = 0u;   // the axes still to look up, one bit each
-        if (use_filter && G == 1 && !edge) {
 #pragma unroll 1
-            for (int c = 0; c < K; ++c) {
-                const uint32_t d = axis_lin_step<PD>(c);
-                const uint32_t hp = hash_of_lin(lin + d), hm = hash_of_lin(lin - d);
-                const bool ina = (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
-                const bool inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
-                const uint32_t ca = ina ? __ldg(S.table + (hp & mask)) : 0u;
-                const uint32_t cb = inb ? __ldg(S.table + (hm & mask)) : 0u;
-                if ((ca | cb) != 0u) pend |= 1u << c;
-                else __stcs(L.nbr + (size_t)c * M + v, make_int2(-1, -1));
+                for (int c = 0; c < K; ++c) {
+                    const uint32_t d = axis_lin_step<PD>(c);
+                    const uint32_t hp = hash_of_lin(lin + d), hm = hash_of_lin(lin - d);
+                    const bool ina = (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
+                    const bool inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
+                    const uint32_t ca = ina ? __ldg(S.table + (hp & mask)) : 0u;
+                    const uint32_t cb = inb ? __ldg(S.table + (hm & mask)) : 0u;
+                    if ((ca | cb) != 0u) pend |= 1u << c;
+                    else __stcs(L.nbr + (size_t)c * M + v, make_int2(-1, -1));
+                }
             }
-        } else {
-            for (int c = g; c < K; c += G) pend |= 1u << c;
+#pragma unroll
+            for (int k = 0; k < NW; ++k) s_key[wid][k][lane] = key[k];
+            s_lin[wid][lane] = lin;
         }
-        while (pend != 0u) {
-            const int c = __ffs(pend) - 1;
-            pend &= pend - 1u;
-            axis_pair(c);
+        // my queue entries after those of the lanes below me
+        const int cnt = __popc(pend);
+        int pre = cnt;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int o = __shfl_up_sync(kFull, pre, d);
+            if (lane >= d) pre += o;
         }
+        const int qtotal = __shfl_sync(kFull, pre, 31);
+        pre -= cnt;
+        for (uint32_t m = pend; m != 0u; m &= m - 1u) s_q[wid][pre++] = (uint16_t)((lane << 5) | (__ffs(m) - 1));
+        __syncwarp();
+        for (int j = lane; j < qtotal; j += 32) {
+            const int e = s_q[wid][j];
+            const int src = e >> 5, c = e & 31;
+            uint32_t key[NW];
+#pragma unroll
+            for (int k = 0; k < NW; ++k) key[k] = s_key[wid][k][src];
+            bool edge = false;
+#pragma unroll
+            for (int i = 0; i < PD; ++i) {
+                const int x = key_coord(key, i);
+                edge = edge || x > 32767 - K || x < -32768 + K;
+            }
+            neighbour_pair<PD>(S, L, mask, f, true, key, s_lin[wid][src], edge, wb + src, M, c);
+        }
+        __syncwarp();   // the queue is refilled by the next step
     }
 }
 
