@@ -965,7 +965,7 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
             if (edge) {
                 pend = (1u << K) - 1u;   // (the queue below recomputes edge hashes from the words)
             } else {
-#pragma unroll 1
+#pragma unroll 4
                 for (int c = 0; c < K; ++c) {
                     const uint32_t d = axis_lin_step<PD>(c);
                     const uint32_t hp = hash_of_lin(lin + d), hm = hash_of_lin(lin - d);
