@@ -51,7 +51,11 @@ cudaError_t side_fork(cudaStream_t main, SideFork* f) {
     DeviceSide& d = g_side[dev];
     d.mu.lock();
     if (!d.stream) {
-        e = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking);
+        // the side stream's kernels (blur neighbours, latency-bound) are
+        // scheduled ahead of the caller's (the splat) when both wait for SMs
+        int least = 0, greatest = 0;
+        e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&d.stream, cudaStreamNonBlocking, greatest);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d.join, cudaEventDisableTiming);
         if (e != cudaSuccess) { d.mu.unlock(); return e; }
