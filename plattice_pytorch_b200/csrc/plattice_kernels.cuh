@@ -786,53 +786,87 @@ __device__ __forceinline__ int neighbour_find(const uint32_t* __restrict__ table
 
 // ---------------------------------------------------------------- K2: global insert
 
-// One thread per staged key.  The staged key records are complete before this
-// kernel starts, so a cell can name its owner the moment the owner's CAS lands:
-// a CAS of (tag | 1 + my staged index) into an empty cell makes me the owner;
-// a full cell with my tag names an owner whose record is compared word by
-// word.  No cell is ever half-written and nobody waits.  The owners of each
-// CTA's chunk then take consecutive vertex ids (one atomic per CTA and chunk)
-// and write their key to the vertex key array; cells keep the staged index,
-// and lookups map it to the vertex id through vid_of.
+// KPT staged keys per thread and chunk.  The staged key records are complete
+// before this kernel starts, so a cell can name its owner the moment the
+// owner's CAS lands: a CAS of (tag | 1 + my staged index) into an empty cell
+// makes me the owner; a full cell with my tag names an owner whose record is
+// compared word by word.  No cell is ever half-written and nobody waits.  The
+// first CAS of each of a thread's keys is issued before any result is used
+// (most keys settle there); collisions continue probing one key at a time.
+// The owners of each CTA's chunk then take consecutive vertex ids (one atomic
+// per CTA and chunk) and write their key to the vertex key array; cells keep
+// the staged index, and lookups map it to the vertex id through vid_of.
+constexpr int kInsertKpt = 4;
+
 template <int PD>
 __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
-    constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW;
+    constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW, KPT = kInsertKpt;
     __shared__ int s_wcnt[8], s_base;
     const int U = L.hdr->u_total;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
     const bool use_filter = L.hdr->cap_log2 >= geo.filter_min_log2;
     const TableFmt f = table_fmt(geo);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int i0 = blockIdx.x * blockDim.x; i0 < U; i0 += gridDim.x * blockDim.x) {   // block-uniform
-        const int i = i0 + threadIdx.x;
-        uint32_t kw[NW];
-        int owner = -1;
-        if (i < U) {
-            load_key<CW>(S.skeys + (size_t)i * CW, kw);
-            const uint32_t tag = cell_tag(kw[0], f);
-            uint32_t pos = kw[0] & mask;
-            for (uint32_t probe = 0; probe <= mask; ++probe) {
-                const uint32_t c = atomicCAS(S.table + pos, 0u, tag | (uint32_t)(i + 1));
-                if (c == 0u) {
-                    owner = i;
-                    if (use_filter) atomicOr(S.filter + filter_word(kw[0], mask), filter_bit(kw[0]));
-                    break;
-                }
-                if ((c & ~f.idx_mask) == tag) {
-                    const int o = (int)(c & f.idx_mask) - 1;
-                    if (key_equal<CW>(S.skeys + (size_t)o * CW, kw)) {
-                        owner = o;
-                        break;
-                    }
-                }
-                pos = (pos + 1) & mask;
+    // KPT keys per thread only when there are enough keys to occupy the grid that way
+    const int kpt = U >= gridDim.x * blockDim.x * KPT ? KPT : 1;
+    const int chunk = blockDim.x * kpt;
+    for (int i0 = blockIdx.x * chunk; i0 < U; i0 += gridDim.x * chunk) {   // block-uniform
+        uint32_t h[KPT], c0[KPT];
+        int owner[KPT];
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            const int i = i0 + threadIdx.x + j * blockDim.x;
+            owner[j] = -1;
+            c0[j] = 0u;
+            h[j] = 0u;
+            if (j < kpt && i < U) {
+                h[j] = __ldg(reinterpret_cast<const uint32_t*>(S.skeys + (size_t)i * CW));   // word 0: the hash
+                c0[j] = atomicCAS(S.table + (h[j] & mask), 0u, cell_tag(h[j], f) | (uint32_t)(i + 1));
             }
-            if (owner < 0) atomicOr(&L.hdr->status, PL_ST_TABLE_FULL);
-            S.owner[i] = owner;
         }
-        const bool own = i < U && owner == i;
-        const unsigned m = __ballot_sync(kFull, own);
-        if (lane == 0) s_wcnt[wid] = __popc(m);
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            const int i = i0 + threadIdx.x + j * blockDim.x;
+            if (j >= kpt || i >= U) continue;
+            if (c0[j] == 0u) {
+                owner[j] = i;
+            } else {
+                uint32_t kw[NW];
+                load_key<CW>(S.skeys + (size_t)i * CW, kw);
+                const uint32_t tag = cell_tag(h[j], f);
+                uint32_t pos = h[j] & mask;
+                uint32_t c = c0[j];
+                for (uint32_t probe = 0; probe <= mask; ++probe) {
+                    if (probe > 0) {
+                        c = atomicCAS(S.table + pos, 0u, tag | (uint32_t)(i + 1));
+                        if (c == 0u) {
+                            owner[j] = i;
+                            break;
+                        }
+                    }
+                    if ((c & ~f.idx_mask) == tag) {
+                        const int o = (int)(c & f.idx_mask) - 1;
+                        if (key_equal<CW>(S.skeys + (size_t)o * CW, kw)) {
+                            owner[j] = o;
+                            break;
+                        }
+                    }
+                    pos = (pos + 1) & mask;
+                }
+                if (owner[j] < 0) atomicOr(&L.hdr->status, PL_ST_TABLE_FULL);
+            }
+            if (owner[j] == i && use_filter) atomicOr(S.filter + filter_word(h[j], mask), filter_bit(h[j]));
+            S.owner[i] = owner[j];
+        }
+        unsigned m[KPT];
+        int wtot = 0;
+#pragma unroll
+        for (int j = 0; j < KPT; ++j) {
+            const int i = i0 + threadIdx.x + j * blockDim.x;
+            m[j] = __ballot_sync(kFull, j < kpt && i < U && owner[j] == i);
+            wtot += __popc(m[j]);
+        }
+        if (lane == 0) s_wcnt[wid] = wtot;
         __syncthreads();
         if (threadIdx.x == 0) {
             int tot = 0;
@@ -844,12 +878,17 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
             s_base = tot ? atomicAdd(&L.hdr->m, tot) : 0;
         }
         __syncthreads();
-        if (own) {
-            const int vid = s_base + s_wcnt[wid] + __popc(m & ((1u << lane) - 1u));
-            S.vid_of[i] = vid;
+        int vbase = s_base + s_wcnt[wid];
 #pragma unroll
-            for (int w = 0; w < CW; ++w)
-                S.vkeys[(size_t)vid * CW + w] = make_uint4(kw[4 * w], kw[4 * w + 1], kw[4 * w + 2], kw[4 * w + 3]);
+        for (int j = 0; j < KPT; ++j) {
+            if ((m[j] >> lane) & 1u) {
+                const int i = i0 + threadIdx.x + j * blockDim.x;
+                const int vid = vbase + __popc(m[j] & ((1u << lane) - 1u));
+                S.vid_of[i] = vid;
+#pragma unroll
+                for (int w = 0; w < CW; ++w) S.vkeys[(size_t)vid * CW + w] = __ldg(S.skeys + (size_t)i * CW + w);
+            }
+            vbase += __popc(m[j]);
         }
         __syncthreads();   // s_wcnt / s_base reused by the next chunk
     }
