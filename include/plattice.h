@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define PLATTICE_ABI_VERSION 2
+#define PLATTICE_ABI_VERSION 3
 
 /* status codes */
 #define PLATTICE_OK 0
