@@ -16,6 +16,8 @@ Named workloads (name -> what it is):
   values (r, g, b, 1).
 * ``voronoi1024_pd5_vd3``  the same image with values = rgb (the headline throughput case).
 * ``gauss512_pd16_vd8``    512x512, features i.i.d. N(0,1)*2 (pd 16), values U(-1,1) (vd 8).
+* ``gauss256_pd16_vd8``    the same distribution at 256x256 (1.1 M lattice vertices): a
+  case small enough for full profiler captures of the large-lattice kernels.
 * ``collapse512_pd2_vd8``  512x512, every feature vector (0.3, 0.7) so every pixel falls
   in one simplex (pd+1 = 3 lattice vertices), values U(-1,1) (vd 8).
 * ``crf512_pd5_vd3``       one image of a batch of 512x512 images (``index`` selects it;
@@ -105,10 +107,11 @@ def make_workload(name, seed=0, index=0):
         f = spatial_rgb_features(img, 32.0, 0.08)
         v = img if name.endswith("vd3") else np.concatenate(
             [img, np.ones(img.shape[:2] + (1,), np.float32)], axis=-1)
-    elif name == "gauss512_pd16_vd8":
+    elif name in ("gauss512_pd16_vd8", "gauss256_pd16_vd8"):
+        n = 512 if name.startswith("gauss512") else 256
         rng = np.random.default_rng(s + 4)
-        f = (rng.standard_normal((512, 512, 16)) * 2.0).astype(np.float32)
-        v = rng.uniform(-1.0, 1.0, (512, 512, 8)).astype(np.float32)
+        f = (rng.standard_normal((n, n, 16)) * 2.0).astype(np.float32)
+        v = rng.uniform(-1.0, 1.0, (n, n, 8)).astype(np.float32)
     elif name == "collapse512_pd2_vd8":
         rng = np.random.default_rng(s + 5)
         f = np.empty((512, 512, 2), np.float32)
@@ -133,6 +136,7 @@ WORKLOADS = {
     "voronoi1024_pd5_vd4": (1024, 1024, 5, 4),
     "voronoi1024_pd5_vd3": (1024, 1024, 5, 3),
     "gauss512_pd16_vd8": (512, 512, 16, 8),
+    "gauss256_pd16_vd8": (256, 256, 16, 8),
     "collapse512_pd2_vd8": (512, 512, 2, 8),
     "crf512_pd5_vd3": (512, 512, 5, 3),
 }
