@@ -904,7 +904,8 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
 template <int PD>
 __device__ __forceinline__ void neighbour_pair(const ScrView& S, const LatView& L, uint32_t mask, TableFmt f,
                                                bool use_filter, const uint32_t (&key)[Cfg<PD>::NW], uint32_t lin,
-                                               bool edge, int v, int M, int c) {
+                                               bool edge, int v, int M, int c, bool try_a = true,
+                                               bool try_b = true) {
     constexpr int NW = Cfg<PD>::NW;
     uint32_t hp, hm;
     if (!edge) {
@@ -919,10 +920,11 @@ __device__ __forceinline__ void neighbour_pair(const ScrView& S, const LatView& 
         hm = hash_of_lin(key_lin_words<PD>(kw));
     }
     const uint32_t pa = hp & mask, pb = hm & mask;
-    bool ina = true, inb = true;   // a cell reads as empty when the filter rules the key out
+    // a cell reads as empty when the key is already known to be absent or the filter rules it out
+    bool ina = try_a, inb = try_b;
     if (use_filter) {
-        ina = (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
-        inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
+        ina = ina && (__ldg(S.filter + filter_word(hp, mask)) & filter_bit(hp)) != 0u;
+        inb = inb && (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
     }
     const uint32_t ca = ina ? __ldg(S.table + pa) : 0u, cb = inb ? __ldg(S.table + pb) : 0u;
     const int na = neighbour_find<PD>(S.table, mask, f, S.skeys, S.vid_of, key, c, 1, hp, pa, ca, &L.hdr->status);
@@ -992,11 +994,13 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
     }
     __shared__ uint32_t s_key[WARPS][NW][32];
     __shared__ uint32_t s_lin[WARPS][32];
+    __shared__ unsigned long long s_side[WARPS][32];   // bits 2c, 2c+1: the + / - lookup of axis c may hit
     __shared__ uint16_t s_q[WARPS][32 * K];   // (lane << 5) | axis
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     for (int wb = gtid - lane; wb < M; wb += nthreads) {   // warp-uniform
         const int v = wb + lane;
         uint32_t pend = 0u;   // my axes still to look up, one bit each
+        unsigned long long side = ~0ull;
         if (v < M) {
             uint32_t key[NW], lin;
             bool edge;
@@ -1004,6 +1008,7 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
             if (edge) {
                 pend = (1u << K) - 1u;   // (the queue below recomputes edge hashes from the words)
             } else {
+                side = 0ull;
 #pragma unroll 4
                 for (int c = 0; c < K; ++c) {
                     const uint32_t d = axis_lin_step<PD>(c);
@@ -1012,13 +1017,18 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
                     const bool inb = (__ldg(S.filter + filter_word(hm, mask)) & filter_bit(hm)) != 0u;
                     const uint32_t ca = ina ? __ldg(S.table + (hp & mask)) : 0u;
                     const uint32_t cb = inb ? __ldg(S.table + (hm & mask)) : 0u;
-                    if ((ca | cb) != 0u) pend |= 1u << c;
-                    else __stcs(L.nbr + (size_t)c * M + v, make_int2(-1, -1));
+                    if ((ca | cb) != 0u) {
+                        pend |= 1u << c;
+                        side |= (unsigned long long)((ca != 0u ? 1u : 0u) | (cb != 0u ? 2u : 0u)) << (2 * c);
+                    } else {
+                        __stcs(L.nbr + (size_t)c * M + v, make_int2(-1, -1));
+                    }
                 }
             }
 #pragma unroll
             for (int k = 0; k < NW; ++k) s_key[wid][k][lane] = key[k];
             s_lin[wid][lane] = lin;
+            s_side[wid][lane] = side;
         }
         // my queue entries after those of the lanes below me
         const int cnt = __popc(pend);
@@ -1044,7 +1054,11 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
                 const int x = key_coord(key, i);
                 edge = edge || x > 32767 - K || x < -32768 + K;
             }
-            neighbour_pair<PD>(S, L, mask, f, true, key, s_lin[wid][src], edge, wb + src, M, c);
+            // a lookup the first sweep ruled out (filter bit clear or home cell
+            // empty) reads nothing; the other reads its home cell again
+            const unsigned sd = (unsigned)(s_side[wid][src] >> (2 * c)) & 3u;
+            neighbour_pair<PD>(S, L, mask, f, false, key, s_lin[wid][src], edge, wb + src, M, c, (sd & 1u) != 0u,
+                               (sd & 2u) != 0u);
         }
         __syncwarp();   // the queue is refilled by the next step
     }

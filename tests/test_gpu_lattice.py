@@ -210,3 +210,46 @@ def _check_invariants(fn, dev):
             nk = (vk.astype(np.int32) + sgn * step).astype(np.int16)
             expect = np.array([vid_of_key.get(r.tobytes(), -1) for r in nk], np.int32)
             assert np.array_equal(nbr[c, :, col], expect), (c, sgn, int(np.count_nonzero(nbr[c, :, col] != expect)))
+
+
+def _neighbour_keys(f, v, dev):
+    """Vertex keys [M, pd] sorted, and for each of them and each (axis, direction)
+    the neighbour's key, or a row of the int16 minimum where there is none."""
+    from plattice_pytorch_b200 import PLOO
+    h, w, pd = f.shape
+    lat_off, scr_off, g = _layout(h, w, pd, v.shape[2])
+    K, CW = g["K"], g["CW"]
+    _, _, lat = PLOO.lattice_forward(torch.from_numpy(f).to(dev), torch.from_numpy(v).to(dev), keep_scratch=True)
+    torch.cuda.synchronize()
+    assert PLOO.lattice_info(lat)["status"] == 0
+    lb, sb = lat.buf.cpu().numpy(), lat.scratch.cpu().numpy()
+    M = int(lb[:256].view(np.int32)[1])
+    vk, _ = _decode(_view(sb, scr_off["vkeys"], M * CW * 4, np.uint32).reshape(M, CW * 4), pd)
+    nbr = _view(lb, lat_off["nbr"], M * K * 2, np.int32).reshape(K, M, 2)
+    none = np.full((1, pd), -32768, np.int16)
+    table = np.concatenate([vk, none])                    # index -1 -> the sentinel row
+    nk = table[np.where(nbr < 0, M, nbr)]                 # [K, M, 2, pd]
+    order = np.lexsort(vk.T[::-1])
+    return vk[order], nk[:, order]
+
+
+def test_sparse_neighbour_path_matches_dense(dev):
+    """A lattice large enough for one vertex per thread, with the miss filter
+    forced on, takes the sparse neighbour path (first sweep, per-warp queue);
+    with the filter off the dense path.  Both give the same neighbours."""
+    from plattice_pytorch_b200 import _lib
+    rng = np.random.default_rng(7)
+    f = (rng.normal(size=(192, 192, 16)) * 2.0).astype(np.float32)   # about 627 k distinct vertices
+    v = rng.uniform(-1.0, 1.0, size=(192, 192, 1)).astype(np.float32)
+    L = _lib.lib()
+    try:
+        L.plattice_debug_set_miss_filter_log2(6)
+        keys_s, nk_s = _neighbour_keys(f, v, dev)
+        L.plattice_debug_set_miss_filter_log2(30)
+        keys_d, nk_d = _neighbour_keys(f, v, dev)
+    finally:
+        L.plattice_debug_set_miss_filter_log2(0)
+    assert keys_s.shape[0] > 148 * 8 * 256   # more vertices than the neighbour grid's threads
+    assert np.array_equal(keys_s, keys_d)
+    assert np.array_equal(nk_s, nk_d)
+    assert (nk_s[..., 0] != -32768).mean() > 0.01   # some neighbours exist
