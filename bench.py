@@ -51,6 +51,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="voronoi1024_pd5_vd3")
     ap.add_argument("--images-per-gpu", type=int, default=1)
+    ap.add_argument("--batch-split", type=int, default=0,
+                    help="a fixed batch of this many images of the workload, split by image over the "
+                         "ranks (shard_range), one batch call per rank and step (strong scaling); the "
+                         "reference arm loops over the whole batch on one GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=2048, help="output pixels of the CPU sample")
     ap.add_argument("--profile-steps", type=int, default=10)
@@ -79,6 +83,16 @@ def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    if local_world > 1:   # each rank its own share of the host cores (the host enqueues every launch)
+        cpus = sorted(os.sched_getaffinity(0))
+        per = max(1, len(cpus) // local_world)
+        mine = cpus[local * per:(local + 1) * per] or cpus
+        try:
+            os.sched_setaffinity(0, mine)
+            torch.set_num_threads(len(mine))
+        except OSError:
+            pass
     torch.cuda.set_device(local)
     return rank, world, local
 
@@ -206,29 +220,40 @@ def step(fn, f, v, g):
 
 # ---------------------------------------------------------------- measurement
 
-def load_inputs(args, rank, dev):
+def load_inputs(args, rank, world):
+    """This rank's images: `images_per_gpu` of its own (weak scaling), or its
+    contiguous share of a fixed batch of `batch_split` images (strong)."""
+    from plattice_pytorch_b200.sharding import shard_range
     from plattice_pytorch_b200.workloads import make_workload
-    imgs = []
-    for i in range(args.images_per_gpu):
-        w = make_workload(args.workload, seed=rank * args.images_per_gpu + i)
-        imgs.append(w)
-    return imgs
+    if args.batch_split:
+        start, stop = shard_range(args.batch_split, world, rank)
+        return [make_workload(args.workload, seed=i, index=i) for i in range(start, stop)]
+    return [make_workload(args.workload, seed=rank * args.images_per_gpu + i)
+            for i in range(args.images_per_gpu)]
 
 
-def timed_device(fn, batch, steps, flush):
-    """Per-step CUDA-event time (ms) summed over `steps`; L2 flushed between steps."""
+def timed_device(fn, batch, steps, flush, host_us=None):
+    """Per-step CUDA-event time (ms) summed over `steps`; L2 flushed between
+    steps.  With `host_us` (a list), also the host time of each step's
+    enqueue (the library and autograd calls, no synchronisation), in us."""
     evs = []
     for _ in range(steps):
         flush.fill_(1.0)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
+        t0 = time.perf_counter()
         for (f, v, g) in batch:
             step(fn, f, v, g)
+        if host_us is not None:
+            host_us.append((time.perf_counter() - t0) * 1e6)
         e1.record()
         evs.append((e0, e1))
     torch.cuda.synchronize()
-    return sum(a.elapsed_time(b) for a, b in evs)
+    per = [a.elapsed_time(b) for a, b in evs]
+    if host_us is None:
+        return sum(per)
+    return per
 
 
 def kept_lattice_line(args, dev):
@@ -386,7 +411,7 @@ def kernel_bytes(stage, n, pd, vd, m, u, cap_log2):
     CPF, CPB = pad(vd + 1), pad(vd)
     slot = 6 * K * n   # uint16 local id + float weight per slot
     return {
-        "tile_build": n * 4 * pd + slot + u * (16 * CW + 4 * (CPF + CPB)),
+        "tile_build": n * 4 * pd + slot + u * (16 * CW + 4 * CPF),
         "clear": (1 << cap_log2) * (5 if cap_log2 >= 22 else 4),   # cells, + the miss filter's byte per cell
         "insert": u * (2 * 16 * CW + 8) + m * (2 * 16 * CW + 8),   # insert + compaction
         "splat_fwd": slot + n * 4 * vd + m * 4 * CPF,
@@ -409,11 +434,15 @@ def stage_bytes(n, pd, vd, m):
     return b_fwd, b_bwd
 
 
-def profile_ours(fn, batch, steps, flush, n, pd, vd):
-    """Per-stage device times from CUDA events around every launch (untimed run)."""
+def profile_ours(fn, batch, steps, flush, batched):
+    """Per-stage device times from CUDA events around every launch (untimed
+    run) of the first image (or of the batch, for a batch call)."""
     from plattice_pytorch_b200 import PLOO, _lib
     f, v, g = batch[0]
-    _, _, lat = PLOO.lattice_forward(f, v.detach())
+    if batched:
+        _, _, lat = PLOO.batch_forward(f, v.detach())
+    else:
+        _, _, lat = PLOO.lattice_forward(f, v.detach())
     info = PLOO.lattice_info(lat)
     del lat
     _lib.profile_read()
@@ -517,7 +546,10 @@ def main():
         dist_init(world, local)
         world_eff = world
 
-    imgs = load_inputs(args, rank, dev)
+    if args.impl == "reference" and args.batch_split:   # the reference: the whole batch on one GPU
+        imgs = load_inputs(args, 0, 1)
+    else:
+        imgs = load_inputs(args, rank, world_eff)
     h, w, pd = imgs[0]["features"].shape
     vd = imgs[0]["values"].shape[2]
     n = h * w
@@ -529,7 +561,7 @@ def main():
         g = torch.from_numpy(im["grad"]).to(dev)
         batch.append((f, v, g))
     per_image_fn, per_image_batch = fn, batch
-    batched = args.batched and args.impl == "ours"
+    batched = (args.batched or args.batch_split > 0) and args.impl == "ours"
     if batched:   # one [B,H,W,...] triple, one library call per step
         from plattice_pytorch_b200 import PermutoLatticeBatchFunction
         fn = PermutoLatticeBatchFunction
@@ -562,10 +594,16 @@ def main():
     torch.cuda.synchronize()
     barrier(world_eff)
     torch.cuda.synchronize()
-    t_dev = timed_device(fn, batch, args.steps, flush)
+    host_us = []
+    per_step = timed_device(fn, batch, args.steps, flush, host_us)
     torch.cuda.synchronize()
     barrier(world_eff)
-    t_dev = max_over_ranks(t_dev, world_eff)
+    # the median step when there are enough steps for it to mean something,
+    # else the mean; the slowest rank sets the job's time either way
+    t_step = statistics.median(per_step) if args.steps >= 50 else sum(per_step) / len(per_step)
+    t_step = max_over_ranks(t_step, world_eff)
+    t_dev = t_step * args.steps
+    host_med = max_over_ranks(statistics.median(host_us), world_eff)
 
     # end to end from pinned host buffers
     host = [(torch.from_numpy(im["features"]).pin_memory(), torch.from_numpy(im["values"]).pin_memory(),
@@ -580,21 +618,28 @@ def main():
     t_e2e = max_over_ranks(t_e2e, world_eff)
     clk = clocks.stop()
 
-    px_total = world_eff * n_images * n * args.steps
+    imgs_job = args.batch_split if args.batch_split else world_eff * n_images
+    px_total = imgs_job * n * args.steps
     value = px_total / (t_dev * 1e-3) / 1e6
     h2d = sum(int(x.numel()) * 4 for hh in host for x in hh)
     d2h = sum(2 * int(hh[1].numel()) * 4 for hh in host)
     res = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_eff, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_dev / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
+        "scaling": "strong" if args.batch_split else "weak", "vs_baseline": None,
+        "timing": ("median" if args.steps >= 50 else "mean") + " of the K per-step CUDA-event times "
+                  "(max over ranks)",
+        "ms_per_step_mean": max_over_ranks(sum(per_step) / len(per_step), world_eff),
+        "host_enqueue_us_per_step": host_med,
         "dtype": "f32" if args.lattice_precision == "fp32" or args.impl == "reference"
                  else "f32 (bf16 rows in the streaming blur passes)",
         "data": "synthetic",
         "config": {"workload": args.workload, "h": h, "w": w, "pd": pd, "vd": vd,
-                   "images_per_gpu": n_images,
+                   "images_per_gpu": n_images, "images_per_job": imgs_job,
                    "l2": "flushed between timed steps (256 MiB write, outside the events)",
-                   "parallelism": "one image lattice per rank, no collective" if world_eff > 1 else "1 GPU",
+                   "parallelism": (f"{imgs_job} images split by image over {world_eff} rank(s), no collective"
+                                   if args.batch_split else
+                                   "one image lattice per rank, no collective" if world_eff > 1 else "1 GPU"),
                    "api": ("PermutoLatticeBatchFunction (one call per batch)" if batched else
                            "PermutoLatticeFunction forward") + " + torch.autograd.grad backward"},
         "e2e": {"value": px_total / (t_e2e * 1e-3) / 1e6, "unit": UNIT,
@@ -608,7 +653,13 @@ def main():
         res["reference_build"] = "reference permuto.cpp + permutohedral.cu, unmodified, nvcc sm_100a"
 
     if args.impl == "ours":
-        info, prof = profile_ours(per_image_fn, per_image_batch, args.profile_steps, flush, n, pd, vd)
+        if batched:
+            info, prof = profile_ours(fn, batch, args.profile_steps, flush, True)
+            n_prof, launch_mult = n * n_images, 1   # the batch's pixels, one call per step
+        else:
+            info, prof = profile_ours(per_image_fn, per_image_batch, args.profile_steps, flush, False)
+            n_prof, launch_mult = n, n_images
+        n = n_prof
         m, u, cap = info["m"], info["u_total"], info["cap_log2"]
         peak, peak_kind = hbm_peak()
         per_stage = {}
@@ -645,7 +696,7 @@ def main():
             "frac_all_kernels": (b_fwd + b_bwd) / (all_ms * 1e-3) / 1e9 / peak}
         res["stages"] = per_stage
         res["lattice"] = {"m": m, "u_total": u, "cap_log2": cap}
-        res["gpu_launches"] = int(round(launches_per_step * args.steps * n_images))
+        res["gpu_launches"] = int(round(launches_per_step * args.steps * launch_mult))
 
     if rank == 0 and world_eff == 1 and not args.no_cpu_baseline:
         im = imgs[0]

@@ -10,7 +10,16 @@
  * The reference binds them to Python through a torch extension (permuto.cpp);
  * here the boundary is plain C: device pointers, sizes, an explicit CUDA
  * stream (passed as void*) and an int status.  No call synchronises the stream
- * except plattice_lattice_info and plattice_vertex_keys.
+ * except plattice_lattice_info, plattice_vertex_keys and
+ * plattice_noalloc_status.
+ *
+ * Device-side failures (a hash table too small, a bounded wait that gave up)
+ * are reported without synchronising: the last kernel of every call writes
+ * the lattice's status word to a slot of pinned, host-mapped memory, and the
+ * first call whose start finds a failed earlier call there -- once that
+ * call's kernels have finished -- returns PLATTICE_ERR_DEVICE without
+ * enqueueing its own work (plattice_last_error_detail names the failed call).
+ * plattice_poll_status does the same check on its own.
  *
  * Tensors: features [h][w][pd], values / grad / out [h][w][vd],
  * weight [h][w] (one float per pixel), all float32, contiguous, on the current
@@ -19,8 +28,11 @@
  * Memory.  The caller allocates two device buffers, sized by
  * plattice_workspace_sizes:
  *   lattice  -- the built lattice; kept from a forward call to the backward
- *               calls that reuse it.
- *   scratch  -- transient; only needed during a call.
+ *               calls that reuse it (its size does not depend on vd).
+ *   scratch  -- transient; only needed during a call.  A call on a kept
+ *               lattice (a backward that reuses it, plattice_filter*) needs
+ *               only its front part, plattice_reuse_scratch_size bytes: the
+ *               lattice value rows of the call's blur.
  * Calls that overlap in time must not share either buffer.
  */
 #ifndef PLATTICE_H
@@ -33,14 +45,15 @@
 extern "C" {
 #endif
 
-#define PLATTICE_ABI_VERSION 3
+#define PLATTICE_ABI_VERSION 4
 
 /* status codes */
 #define PLATTICE_OK 0
 #define PLATTICE_ERR_INVALID 1   /* bad dimensions, null pointer, or image too large */
 #define PLATTICE_ERR_WORKSPACE 2 /* lattice or scratch buffer smaller than required */
 #define PLATTICE_ERR_CUDA 3      /* a CUDA runtime call or kernel launch failed */
-#define PLATTICE_ERR_DEVICE 4    /* the lattice's device status word reports a failure */
+#define PLATTICE_ERR_DEVICE 4    /* a device status word reports a failure (this lattice's,
+                                    or an earlier call's: see above) */
 
 /* device status bits reported by plattice_lattice_info */
 #define PLATTICE_DEV_TABLE_FULL 2 /* hash-table probe limit reached (table too small) */
@@ -62,6 +75,12 @@ const char* plattice_last_error_detail(void);
 int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes,
                              size_t* scratch_bytes);
 
+/* Bytes of scratch that a call on a kept lattice of b images needs (a
+ * backward with lattice_state 1 or 2, plattice_filter, plattice_filter_backward):
+ * the front part of the full scratch.  No reference counterpart (the
+ * reference rebuilds, permutohedral.cu:615-635). */
+int plattice_reuse_scratch_size(int b, int h, int w, int pd, int vd, size_t* bytes);
+
 /* Forward filter: builds the lattice of `features` into `lattice`, splats
  * `values`, blurs along the pd+1 lattice axes in order 0..pd and slices:
  *   out[p] = sum_i w_pi L[v_pi][0:vd] / sum_i w_pi L[v_pi][vd],
@@ -75,21 +94,23 @@ int plattice_forward(float* weight_out, float* out, const float* values, const f
 /* Value gradient: grad_values_out = S^T B^T S'(grad * weight_in), the blur in
  * axis order pd..0.  lattice_state: 0 = `lattice` does not hold the lattice of
  * `features` (it is rebuilt, `scratch` and `features` required); 1 = it holds
- * the lattice built by the last plattice_forward on these features and no
- * backward has used it yet; 2 = it holds that lattice and was used by an
- * earlier backward.  `features` is read only by a rebuild and may be NULL
- * otherwise.  Replaces permuto_filter_grad (permutohedral.cu:717), which
- * always rebuilds. */
+ * the lattice built by the last plattice_forward on these features (1 and 2,
+ * "not yet used by a backward" and "used", are treated alike).  `features` is
+ * read only by a rebuild and may be NULL otherwise.  `scratch` is always
+ * required: scratch_bytes from plattice_workspace_sizes for a rebuild, at
+ * least plattice_reuse_scratch_size otherwise.  Replaces permuto_filter_grad
+ * (permutohedral.cu:717), which always rebuilds. */
 int plattice_backward(float* grad_values_out, const float* grad, const float* weight_in,
                       const float* features, void* lattice, size_t lattice_bytes,
                       int lattice_state, void* scratch, size_t scratch_bytes, int pd, int vd,
                       int w, int h, void* stream);
 
 /* Batches: B images of one shape, [B][h][w][...] contiguous (features,
- * values, outputs), in one call -- the dense-CRF use of many images.  The
- * images' lattices lie one after the other in `lattice` (kept for the
- * backward); one image-sized `scratch` serves them all, since the images run
- * one after the other on `stream`.  Sizes from plattice_batch_workspace_sizes.
+ * values, outputs), in one call -- the dense-CRF use of many images.  Each
+ * image has its own lattice vertices, but the B lattices share one buffer
+ * and one launch of every stage: the key hash mixes in the image index, so
+ * equal keys of two images never merge.  Sizes from
+ * plattice_batch_workspace_sizes (b = 1 gives plattice_workspace_sizes).
  * The reference has no batch call (its callers loop over images in Python,
  * permuto.cpp:71-158 per image).  plattice_backward_batch takes the same
  * lattice_state values as plattice_backward, for all B images at once. */
@@ -114,8 +135,9 @@ int plattice_backward_batch(float* grad_values_out, const float* grad, const flo
  * plattice_filter_backward: the value gradient of such a call, given its
  * weight_out as weight_in (same result as plattice_backward).
  * `values_ws` holds the lattice value rows of the call
- * (plattice_filter_workspace_size bytes; any allocator, reusable across
- * calls).  `lattice_bytes` may be the buffer size of a forward with any vd.
+ * (plattice_filter_workspace_size bytes, which equals
+ * plattice_reuse_scratch_size for one image; any allocator, reusable across
+ * calls).  A lattice serves every vd.
  * Both calls update bookkeeping in the lattice header, so calls on one
  * lattice must be issued one after the other (one stream). */
 int plattice_filter_workspace_size(int h, int w, int pd, int vd, size_t* bytes);
@@ -157,6 +179,21 @@ int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total
 int plattice_vertex_keys(const void* lattice, const void* scratch, int pd, int vd, int w, int h,
                          int16_t* keys_dev, int max_keys, int* m, void* stream);
 
+/* Reports device-side failures of earlier calls whose kernels have finished
+ * (see the top of this file): PLATTICE_ERR_DEVICE once per failure, with
+ * plattice_last_error_detail naming the call; PLATTICE_OK otherwise.  Does
+ * not synchronise.  No reference counterpart. */
+int plattice_poll_status(void);
+
+/* Everything the first call for (pd, vd) does in the current CUDA context
+ * apart from the filter itself: kernel attribute settings (dynamic shared
+ * memory limits), the creation of the library's side stream and its two
+ * events, and the loading of every kernel of the forward and backward filter
+ * (with lazy module loading each kernel is otherwise loaded at its first
+ * launch).  Call it before any stream capture, or before real-time work that
+ * must not pay these costs.  No reference counterpart. */
+int plattice_prepare(int pd, int vd);
+
 /* Test support: force the hash-table capacity to 2^log2 cells (0 = automatic,
  * >= twice the staged keys).  A capacity below the vertex count makes the
  * build report PLATTICE_DEV_TABLE_FULL instead of looping. */
@@ -191,16 +228,28 @@ void plattice_debug_set_blur_streaming(int on);
  * every call).  Same computation and outputs as plattice_forward, but the
  * lattice and scratch buffers live in one fixed 64 MiB array inside the
  * library (plattice_noalloc_capacity() bytes), held on every GPU that loads
- * the library until the process exits; the call allocates nothing.  An image
- * whose workspace exceeds the array returns PLATTICE_ERR_WORKSPACE
- * (plattice_noalloc_error_detail() says how much it needs).  The first call
- * on each device looks up the array's device address: make it before any
+ * the library until the process exits; the call allocates no device memory.
+ * An image whose workspace exceeds the array returns PLATTICE_ERR_WORKSPACE
+ * (plattice_noalloc_error_detail() says how much it needs).
+ * First call in a CUDA context: it looks up the array's device address in
+ * that context, sets kernel attributes, creates the library's side stream and
+ * two events, and (lazy module loading) loads the kernels it launches --
+ * plattice_prepare(pd, vd) does all of this except the address lookup, and
+ * plattice_noalloc_status does the lookup; make these first calls before any
  * stream capture.  All calls on a device share the array, so calls that
- * overlap on the GPU race: issue them one after the other. */
+ * overlap on the GPU race: issue them one after the other.  Its device
+ * failures are not reported through the status ring (whose pinned host slots
+ * would be an allocation): plattice_noalloc_status reads them. */
 int plattice_forward_noalloc(float* weight_out, float* out, const float* values, const float* features,
                              int pd, int vd, int w, int h, void* stream);
 size_t plattice_noalloc_capacity(void);
 const char* plattice_noalloc_error_detail(void);
+
+/* Synchronises `stream` and reads the header of the lattice that the last
+ * plattice_forward_noalloc in the current context left in the fixed array:
+ * device status bits and vertex count (either pointer may be NULL).  Returns
+ * PLATTICE_ERR_DEVICE when the status word is non-zero. */
+int plattice_noalloc_status(int* status, int* m, void* stream);
 
 /* Profiling (no reference counterpart): when enabled, every kernel launch is
  * bracketed by CUDA events recorded on its stream.  plattice_profile_read

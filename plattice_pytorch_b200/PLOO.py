@@ -15,8 +15,16 @@ Differences that a caller can observe only as speed:
   * kernels run on PyTorch's current stream of the tensors' device, not on the
     legacy default stream, and no call synchronises the host.
 
-Set the environment variable PLATTICE_CHECK=1 to synchronise after every call
-and raise if the device reports a failure.
+Device-side failures (a hash table too small, a bounded wait that gave up)
+raise :class:`PlatticeError` at the first call after the failed call's kernels
+have finished (or at :func:`check_device_status`).  Set the environment
+variable PLATTICE_CHECK=1 to synchronise after every call and raise at once.
+
+The hot paths (``lattice_forward``, ``lattice_backward``) do their checks with
+one combined test first and build the reference's messages only on failure,
+cache the workspace sizes per shape, and call the library directly on the
+current device, so that their host cost stays a few microseconds above the
+library call itself.
 """
 import ctypes
 import os
@@ -28,9 +36,22 @@ from . import _lib
 
 __all__ = ["forward", "backward", "Lattice", "lattice_forward", "lattice_backward",
            "lattice_filter", "lattice_filter_backward", "feature_grad", "BatchLattice", "batch_forward",
-           "batch_backward", "forward_batch", "backward_batch", "lattice_info", "vertex_keys"]
+           "batch_backward", "forward_batch", "backward_batch", "lattice_info", "vertex_keys",
+           "check_device_status", "prepare"]
 
 _CHECK = os.environ.get("PLATTICE_CHECK", "0") not in ("", "0")
+
+_F32 = torch.float32
+_cur_dev = torch._C._cuda_getDevice
+_raw_stream = torch._C._cuda_getCurrentRawStream
+_L = None
+
+
+def _lib_h():
+    global _L
+    if _L is None:
+        _L = _lib.lib()
+    return _L
 
 
 def _require(cond, msg):
@@ -51,27 +72,51 @@ def _check_dims(pd, vd):
 
 
 def _ptr(t):
-    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    return t.data_ptr() if t is not None else None
 
 
 def _stream(device):
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+    return _raw_stream(device.index)
+
+
+_SIZES = {}
+
+
+def _sizes(b, h, w, pd, vd):
+    """(lattice bytes, full scratch bytes, kept-lattice scratch bytes), cached per shape."""
+    key = (b, h, w, pd, vd)
+    s = _SIZES.get(key)
+    if s is None:
+        lb, sb = _lib.batch_workspace_sizes(b, h, w, pd, vd)
+        s = _SIZES[key] = (lb, sb, _lib.reuse_scratch_size(b, h, w, pd, vd))
+    return s
+
+
+def _call(dev_index, fn, *args):
+    """Library call with `dev_index` the current device (kernels launch on its stream)."""
+    if _cur_dev() == dev_index:
+        return fn(*args)
+    with torch.cuda.device(dev_index):
+        return fn(*args)
+
+
+def _raise(call, rc, detail):
+    raise _lib.PlatticeError(call, rc, detail)
 
 
 class Lattice:
     """A lattice built on the device for one ``features`` tensor.
 
-    Holds the lattice buffer (kept for backward calls), optionally the scratch
-    buffer of the build (needed by :func:`vertex_keys`), and whether a
-    backward pass has already used its value buffers."""
+    Holds the lattice buffer (kept for backward calls) and optionally the
+    scratch buffer of the build (needed by :func:`vertex_keys`)."""
 
     __slots__ = ("buf", "scratch", "h", "w", "pd", "vd", "device", "used", "_feat_ref",
                  "_feat_version", "_feat_ptr", "__weakref__")
 
-    def __init__(self, features, vd, buf, scratch):
+    def __init__(self, features, vd, buf, scratch, shape=None):
         self.buf = buf
         self.scratch = scratch
-        self.h, self.w, self.pd = (int(s) for s in features.shape)
+        self.h, self.w, self.pd = shape if shape is not None else (int(s) for s in features.shape)
         self.vd = int(vd)
         self.device = features.device
         self.used = False
@@ -83,10 +128,10 @@ class Lattice:
         """True when this lattice was built from ``features`` as it is now.
         ``same_object=False`` drops the identity test, for callers (autograd's
         saved tensors) that hand back a new tensor object over the same,
-        version-checked storage."""
+        version-checked storage.  A lattice serves every vd."""
         if same_object and self._feat_ref() is not features:
             return False
-        return (features.data_ptr() == self._feat_ptr and int(vd) == self.vd
+        return (features.data_ptr() == self._feat_ptr
                 and tuple(features.shape) == (self.h, self.w, self.pd)
                 and features.device == self.device
                 and (not same_object or features._version == self._feat_version))
@@ -94,14 +139,13 @@ class Lattice:
 
 def _sync_check(lat, call):
     st = ctypes.c_int(0)
-    rc = _lib.lib().plattice_lattice_info(_ptr(lat.buf), ctypes.byref(st), None, None, None,
-                                          _stream(lat.device))
+    rc = _lib_h().plattice_lattice_info(_ptr(lat.buf), ctypes.byref(st), None, None, None,
+                                        _stream(lat.device))
     if rc != _lib.OK:
-        raise _lib.PlatticeError(call, rc, f"device status bits {st.value:#x}")
+        _raise(call, rc, f"device status bits {st.value:#x}")
 
 
-def lattice_forward(features, values, keep_scratch=False):
-    """Forward filter; returns ``(weight [H,W,1], out [H,W,vd], Lattice)``."""
+def _forward_checks(features, values):
     _check_input(features, "features")
     _check_input(values, "values")
     _require(features.dim() == 3, "features must be [H, W, pd]")
@@ -110,33 +154,40 @@ def lattice_forward(features, values, keep_scratch=False):
     _require(values.dtype == torch.float32, "values must be float32")
     _require(features.shape[0] == values.shape[0] and features.shape[1] == values.shape[1],
              "features and values must have matching H, W")
-    h, w, pd = (int(s) for s in features.shape)
-    vd = int(values.shape[2])
-    _check_dims(pd, vd)
+    _check_dims(int(features.shape[2]), int(values.shape[2]))
     _require(values.device == features.device, "features and values must be on the same device")
+
+
+def lattice_forward(features, values, keep_scratch=False):
+    """Forward filter; returns ``(weight [H,W,1], out [H,W,vd], Lattice)``."""
+    if not (isinstance(features, torch.Tensor) and isinstance(values, torch.Tensor)
+            and features.is_cuda and values.is_cuda and len(fs := features.shape) == 3
+            and len(vs := values.shape) == 3
+            and features.dtype is _F32 and values.dtype is _F32
+            and fs[0] == vs[0] and fs[1] == vs[1] and 1 <= fs[2] <= 16 and 1 <= vs[2] <= 8
+            and features.is_contiguous() and values.is_contiguous()
+            and values.device == features.device):
+        _forward_checks(features, values)
+    h, w, pd = features.shape
+    vd = values.shape[2]
     dev = features.device
-    with torch.cuda.device(dev):
-        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
-        weight = torch.empty((h, w, 1), dtype=torch.float32, device=dev)
-        lb, sb = _lib.workspace_sizes(h, w, pd, vd)
-        buf = torch.empty(lb, dtype=torch.uint8, device=dev)
-        scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
-        rc = _lib.lib().plattice_forward(_ptr(weight), _ptr(out), _ptr(values), _ptr(features),
-                                         _ptr(buf), lb, _ptr(scratch), sb, pd, vd, w, h,
-                                         _stream(dev))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError("plattice_forward", rc, f"h={h} w={w} pd={pd} vd={vd}")
-        lat = Lattice(features, vd, buf, scratch if keep_scratch else None)
-        if _CHECK and h * w > 0:
-            _sync_check(lat, "plattice_forward")
+    out = torch.empty((h, w, vd), dtype=_F32, device=dev)
+    weight = torch.empty((h, w, 1), dtype=_F32, device=dev)
+    lb, sb, _ = _sizes(1, h, w, pd, vd)
+    buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+    scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+    rc = _call(dev.index, _lib_h().plattice_forward, weight.data_ptr(), out.data_ptr(), values.data_ptr(),
+               features.data_ptr(), buf.data_ptr(), lb, scratch.data_ptr(), sb, pd, vd, w, h,
+               _raw_stream(dev.index))
+    if rc:
+        _raise("plattice_forward", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    lat = Lattice(features, vd, buf, scratch if keep_scratch else None, (h, w, pd))
+    if _CHECK and h * w > 0:
+        _sync_check(lat, "plattice_forward")
     return weight, out, lat
 
 
-def lattice_backward(features, grad_values, weight_saved, lattice=None, saved=False):
-    """Value gradient; reuses ``lattice`` when it was built from ``features``
-    as they are now, else rebuilds.  ``saved=True`` when ``features`` comes
-    from autograd's saved tensors (whose version check already guarantees
-    they are unmodified).  Returns ``grad [H,W,vd]``."""
+def _backward_checks(features, grad_values, weight_saved):
     _check_input(features, "features")
     _check_input(grad_values, "grad_values")
     _check_input(weight_saved, "weight_saved")
@@ -150,34 +201,51 @@ def lattice_backward(features, grad_values, weight_saved, lattice=None, saved=Fa
              "features and grad_values must have matching H, W")
     _require(features.shape[0] == weight_saved.shape[0] and features.shape[1] == weight_saved.shape[1],
              "features and weight_saved must have matching H, W")
-    h, w, pd = (int(s) for s in features.shape)
-    vd = int(grad_values.shape[2])
-    _check_dims(pd, vd)
+    _check_dims(int(features.shape[2]), int(grad_values.shape[2]))
     _require(grad_values.device == features.device and weight_saved.device == features.device,
              "features, grad_values and weight_saved must be on the same device")
+
+
+def lattice_backward(features, grad_values, weight_saved, lattice=None, saved=False):
+    """Value gradient; reuses ``lattice`` when it was built from ``features``
+    as they are now, else rebuilds.  ``saved=True`` when ``features`` comes
+    from autograd's saved tensors (whose version check already guarantees
+    they are unmodified).  Returns ``grad [H,W,vd]``."""
+    if not (isinstance(features, torch.Tensor) and isinstance(grad_values, torch.Tensor)
+            and isinstance(weight_saved, torch.Tensor)
+            and features.is_cuda and grad_values.is_cuda and weight_saved.is_cuda
+            and len(fs := features.shape) == 3 and len(gs := grad_values.shape) == 3
+            and len(ws := weight_saved.shape) == 3 and ws[2] == 1
+            and features.dtype is _F32 and grad_values.dtype is _F32 and weight_saved.dtype is _F32
+            and fs[0] == gs[0] == ws[0] and fs[1] == gs[1] == ws[1]
+            and 1 <= fs[2] <= 16 and 1 <= gs[2] <= 8
+            and features.is_contiguous() and grad_values.is_contiguous() and weight_saved.is_contiguous()
+            and grad_values.device == features.device and weight_saved.device == features.device):
+        _backward_checks(features, grad_values, weight_saved)
+    h, w, pd = features.shape
+    vd = grad_values.shape[2]
     dev = features.device
-    with torch.cuda.device(dev):
-        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
-        lb, sb = _lib.workspace_sizes(h, w, pd, vd)
-        if lattice is not None and lattice.matches(features, vd, same_object=not saved):
-            state = 2 if lattice.used else 1
-            buf, scratch, sbytes = lattice.buf, None, 0
-        else:
-            state = 0
-            lattice = None
-            buf = torch.empty(lb, dtype=torch.uint8, device=dev)
-            scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
-            sbytes = sb
-        rc = _lib.lib().plattice_backward(_ptr(out), _ptr(grad_values), _ptr(weight_saved),
-                                          _ptr(features), _ptr(buf), lb, state, _ptr(scratch), sbytes,
-                                          pd, vd, w, h, _stream(dev))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError("plattice_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
-        if lattice is not None:
-            lattice.used = True
-        if _CHECK and h * w > 0:
-            chk = lattice if lattice is not None else Lattice(features, vd, buf, None)
-            _sync_check(chk, "plattice_backward")
+    out = torch.empty((h, w, vd), dtype=_F32, device=dev)
+    lb, sb, rb = _sizes(1, h, w, pd, vd)
+    if lattice is not None and lattice.matches(features, vd, same_object=not saved):
+        state = 2 if lattice.used else 1
+        buf, sbytes = lattice.buf, rb
+    else:
+        state = 0
+        lattice = None
+        buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+        sbytes = sb
+    scratch = torch.empty(sbytes, dtype=torch.uint8, device=dev)
+    rc = _call(dev.index, _lib_h().plattice_backward, out.data_ptr(), grad_values.data_ptr(),
+               weight_saved.data_ptr(), features.data_ptr(), buf.data_ptr(), lb, state, scratch.data_ptr(),
+               sbytes, pd, vd, w, h, _raw_stream(dev.index))
+    if rc:
+        _raise("plattice_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    if lattice is not None:
+        lattice.used = True
+    if _CHECK and h * w > 0:
+        chk = lattice if lattice is not None else Lattice(features, vd, buf, None)
+        _sync_check(chk, "plattice_backward")
     return out
 
 
@@ -202,17 +270,17 @@ def lattice_filter(lattice, values):
     on one stream (they update its header)."""
     vd = _check_kept(lattice, values, "values")
     h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
-    with torch.cuda.device(dev):
-        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
-        weight = torch.empty((h, w, 1), dtype=torch.float32, device=dev)
-        wsb = _lib.filter_workspace_size(h, w, pd, vd)
-        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        rc = _lib.lib().plattice_filter(_ptr(weight), _ptr(out), _ptr(values), _ptr(lattice.buf),
-                                        lattice.buf.numel(), _ptr(ws), wsb, pd, vd, w, h, _stream(dev))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError("plattice_filter", rc, f"h={h} w={w} pd={pd} vd={vd}")
-        if _CHECK and h * w > 0:
-            _sync_check(lattice, "plattice_filter")
+    out = torch.empty((h, w, vd), dtype=_F32, device=dev)
+    weight = torch.empty((h, w, 1), dtype=_F32, device=dev)
+    _, _, wsb = _sizes(1, h, w, pd, vd)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    rc = _call(dev.index, _lib_h().plattice_filter, weight.data_ptr(), out.data_ptr(), values.data_ptr(),
+               lattice.buf.data_ptr(), lattice.buf.numel(), ws.data_ptr(), wsb, pd, vd, w, h,
+               _raw_stream(dev.index))
+    if rc:
+        _raise("plattice_filter", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    if _CHECK and h * w > 0:
+        _sync_check(lattice, "plattice_filter")
     return weight, out
 
 
@@ -225,17 +293,16 @@ def lattice_filter_backward(lattice, grad_values, weight_saved):
              "weight_saved must be [H, W, 1]")
     _require(weight_saved.dtype == torch.float32, "weight_saved must be float32")
     h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
-    with torch.cuda.device(dev):
-        out = torch.empty((h, w, vd), dtype=torch.float32, device=dev)
-        wsb = _lib.filter_workspace_size(h, w, pd, vd)
-        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        rc = _lib.lib().plattice_filter_backward(_ptr(out), _ptr(grad_values), _ptr(weight_saved),
-                                                 _ptr(lattice.buf), lattice.buf.numel(), _ptr(ws), wsb,
-                                                 pd, vd, w, h, _stream(dev))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError("plattice_filter_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
-        if _CHECK and h * w > 0:
-            _sync_check(lattice, "plattice_filter_backward")
+    out = torch.empty((h, w, vd), dtype=_F32, device=dev)
+    _, _, wsb = _sizes(1, h, w, pd, vd)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    rc = _call(dev.index, _lib_h().plattice_filter_backward, out.data_ptr(), grad_values.data_ptr(),
+               weight_saved.data_ptr(), lattice.buf.data_ptr(), lattice.buf.numel(), ws.data_ptr(), wsb,
+               pd, vd, w, h, _raw_stream(dev.index))
+    if rc:
+        _raise("plattice_filter_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    if _CHECK and h * w > 0:
+        _sync_check(lattice, "plattice_filter_backward")
     return out
 
 
@@ -255,23 +322,23 @@ def feature_grad(lattice, features, values, grad_out, weight, out):
     _check_input(weight, "weight")
     _require(tuple(weight.shape) == (lattice.h, lattice.w, 1), "weight must be [H, W, 1]")
     h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
-    with torch.cuda.device(dev):
-        gf = torch.empty((h, w, pd), dtype=torch.float32, device=dev)
-        wsb = _lib.feature_grad_workspace_size(h, w, pd, vd)
-        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        rc = _lib.lib().plattice_feature_grad(_ptr(gf), _ptr(grad_out), _ptr(out), _ptr(weight), _ptr(values),
-                                              _ptr(features), _ptr(lattice.buf), lattice.buf.numel(), _ptr(ws),
-                                              wsb, pd, vd, w, h, _stream(dev))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError("plattice_feature_grad", rc, f"h={h} w={w} pd={pd} vd={vd}")
-        if _CHECK and h * w > 0:
-            _sync_check(lattice, "plattice_feature_grad")
+    gf = torch.empty((h, w, pd), dtype=_F32, device=dev)
+    wsb = _lib.feature_grad_workspace_size(h, w, pd, vd)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    rc = _call(dev.index, _lib_h().plattice_feature_grad, gf.data_ptr(), grad_out.data_ptr(), out.data_ptr(),
+               weight.data_ptr(), values.data_ptr(), features.data_ptr(), lattice.buf.data_ptr(),
+               lattice.buf.numel(), ws.data_ptr(), wsb, pd, vd, w, h, _raw_stream(dev.index))
+    if rc:
+        _raise("plattice_feature_grad", rc, f"h={h} w={w} pd={pd} vd={vd}")
+    if _CHECK and h * w > 0:
+        _sync_check(lattice, "plattice_feature_grad")
     return gf
 
 
 class BatchLattice:
-    """The lattices of a batch of images built by :func:`batch_forward`, kept
-    for the batch's backward (one buffer, one lattice per image)."""
+    """The lattice of a batch of images built by :func:`batch_forward`, kept
+    for the batch's backward (one buffer; the images' vertices are kept apart
+    by the image index in the key hash)."""
 
     __slots__ = ("buf", "shape", "vd", "device", "used", "_feat_ref", "_feat_version", "_feat_ptr",
                  "__weakref__")
@@ -289,7 +356,7 @@ class BatchLattice:
     def matches(self, features, vd, same_object=True):
         if same_object and self._feat_ref() is not features:
             return False
-        return (features.data_ptr() == self._feat_ptr and int(vd) == self.vd
+        return (features.data_ptr() == self._feat_ptr
                 and tuple(features.shape) == self.shape and features.device == self.device
                 and (not same_object or features._version == self._feat_version))
 
@@ -315,19 +382,19 @@ def batch_forward(features, values):
     out [B,H,W,vd], BatchLattice)``; the same per image as :func:`lattice_forward`."""
     b, h, w, pd, vd = _check_batch(features, values, "values")
     dev = features.device
-    with torch.cuda.device(dev):
-        out = torch.empty((b, h, w, vd), dtype=torch.float32, device=dev)
-        weight = torch.empty((b, h, w, 1), dtype=torch.float32, device=dev)
-        lb, sb = _lib.batch_workspace_sizes(b, h, w, pd, vd)
-        buf = torch.empty(lb, dtype=torch.uint8, device=dev)
-        scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
-        rc = _lib.lib().plattice_forward_batch(_ptr(weight), _ptr(out), _ptr(values), _ptr(features), _ptr(buf),
-                                               lb, _ptr(scratch), sb, b, pd, vd, w, h, _stream(dev))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError("plattice_forward_batch", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
-        lat = BatchLattice(features, vd, buf)
-        if _CHECK and b * h * w > 0:
-            _sync_check_batch(lat, b, h, w, pd, "plattice_forward_batch")
+    out = torch.empty((b, h, w, vd), dtype=_F32, device=dev)
+    weight = torch.empty((b, h, w, 1), dtype=_F32, device=dev)
+    lb, sb, _ = _sizes(b, h, w, pd, vd)
+    buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+    scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
+    rc = _call(dev.index, _lib_h().plattice_forward_batch, weight.data_ptr(), out.data_ptr(), values.data_ptr(),
+               features.data_ptr(), buf.data_ptr(), lb, scratch.data_ptr(), sb, b, pd, vd, w, h,
+               _raw_stream(dev.index))
+    if rc:
+        _raise("plattice_forward_batch", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
+    lat = BatchLattice(features, vd, buf)
+    if _CHECK and b * h * w > 0:
+        _sync_check(lat, "plattice_forward_batch")
     return weight, out, lat
 
 
@@ -339,42 +406,30 @@ def batch_backward(features, grad_values, weight_saved, lattice=None, saved=Fals
     _require(tuple(weight_saved.shape) == (b, h, w, 1), "weight_saved must be [B, H, W, 1]")
     _require(weight_saved.dtype == torch.float32, "weight_saved must be float32")
     dev = features.device
-    with torch.cuda.device(dev):
-        out = torch.empty((b, h, w, vd), dtype=torch.float32, device=dev)
-        lb, sb = _lib.batch_workspace_sizes(b, h, w, pd, vd)
-        if lattice is not None and lattice.matches(features, vd, same_object=not saved):
-            state = 2 if lattice.used else 1
-            buf, scratch, sbytes = lattice.buf, None, 0
-        else:
-            state = 0
-            lattice = None
-            buf = torch.empty(lb, dtype=torch.uint8, device=dev)
-            scratch = torch.empty(sb, dtype=torch.uint8, device=dev)
-            sbytes = sb
-        rc = _lib.lib().plattice_backward_batch(_ptr(out), _ptr(grad_values), _ptr(weight_saved),
-                                                _ptr(features), _ptr(buf), lb, state, _ptr(scratch), sbytes,
-                                                b, pd, vd, w, h, _stream(dev))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError("plattice_backward_batch", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
-        if lattice is not None:
-            lattice.used = True
-        if _CHECK and b * h * w > 0:
-            _sync_check_batch(BatchLattice(features, vd, buf), b, h, w, pd, "plattice_backward_batch")
+    out = torch.empty((b, h, w, vd), dtype=_F32, device=dev)
+    lb, sb, rb = _sizes(b, h, w, pd, vd)
+    if lattice is not None and lattice.matches(features, vd, same_object=not saved):
+        state = 2 if lattice.used else 1
+        buf, sbytes = lattice.buf, rb
+    else:
+        state = 0
+        lattice = None
+        buf = torch.empty(lb, dtype=torch.uint8, device=dev)
+        sbytes = sb
+    scratch = torch.empty(sbytes, dtype=torch.uint8, device=dev)
+    rc = _call(dev.index, _lib_h().plattice_backward_batch, out.data_ptr(), grad_values.data_ptr(),
+               weight_saved.data_ptr(), features.data_ptr(), buf.data_ptr(), lb, state, scratch.data_ptr(),
+               sbytes, b, pd, vd, w, h, _raw_stream(dev.index))
+    if rc:
+        _raise("plattice_backward_batch", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
+    if lattice is not None:
+        lattice.used = True
+    if _CHECK and b * h * w > 0:
+        _sync_check(BatchLattice(features, vd, buf), "plattice_backward_batch")
     return out
 
 
-def _sync_check_batch(lat, b, h, w, pd, call):
-    lb, _ = _lib.workspace_sizes(h, w, pd, lat.vd)
-    stride = (lb + 255) & ~255
-    for i in range(b):
-        st = ctypes.c_int(0)
-        rc = _lib.lib().plattice_lattice_info(ctypes.c_void_p(lat.buf.data_ptr() + i * stride),
-                                              ctypes.byref(st), None, None, None, _stream(lat.device))
-        if rc != _lib.OK:
-            raise _lib.PlatticeError(call, rc, f"image {i}: device status bits {st.value:#x}")
-
-
-# The most recent batch forward's lattices, for a standalone batch backward.
+# The most recent batch forward's lattice, for a standalone batch backward.
 _last_batch = None
 
 
@@ -387,7 +442,7 @@ def forward_batch(features, values):
 
 
 def backward_batch(features, grad_values, weight_saved):
-    """``backward`` over ``[B,H,W,...]``; reuses the last batch forward's lattices."""
+    """``backward`` over ``[B,H,W,...]``; reuses the last batch forward's lattice."""
     return batch_backward(features, grad_values, weight_saved, _last_batch)
 
 
@@ -409,13 +464,31 @@ def backward(features, grad_values, weight_saved):
     return lattice_backward(features, grad_values, weight_saved, _last)
 
 
+def check_device_status():
+    """Raise :class:`PlatticeError` if an earlier call's kernels finished with
+    a device-side failure not yet reported (does not synchronise)."""
+    rc = _lib_h().plattice_poll_status()
+    if rc:
+        _raise("plattice_poll_status", rc, "")
+
+
+def prepare(pd, vd, device=None):
+    """Do once, on ``device``'s context, what a first call for (pd, vd) would
+    do besides filtering: kernel attributes, the side stream, kernel loading."""
+    _check_dims(pd, vd)
+    idx = torch.cuda.current_device() if device is None else torch.device(device).index
+    rc = _call(idx, _lib_h().plattice_prepare, pd, vd)
+    if rc:
+        _raise("plattice_prepare", rc, f"pd={pd} vd={vd}")
+
+
 def lattice_info(lattice):
     """Synchronise and read the lattice header: dict(status, m, u_total, cap_log2)."""
     st, m, u, cap = (ctypes.c_int(0) for _ in range(4))
-    rc = _lib.lib().plattice_lattice_info(_ptr(lattice.buf), ctypes.byref(st), ctypes.byref(m),
-                                          ctypes.byref(u), ctypes.byref(cap), _stream(lattice.device))
+    rc = _lib_h().plattice_lattice_info(_ptr(lattice.buf), ctypes.byref(st), ctypes.byref(m),
+                                        ctypes.byref(u), ctypes.byref(cap), _stream(lattice.device))
     if rc not in (_lib.OK, _lib.ERR_DEVICE):
-        raise _lib.PlatticeError("plattice_lattice_info", rc)
+        _raise("plattice_lattice_info", rc, "")
     return {"status": st.value, "m": m.value, "u_total": u.value, "cap_log2": cap.value}
 
 
@@ -427,12 +500,11 @@ def vertex_keys(lattice):
     m = info["m"]
     keys = torch.empty((max(m, 1), lattice.pd), dtype=torch.int16, device=lattice.device)
     mm = ctypes.c_int(0)
-    with torch.cuda.device(lattice.device):
-        rc = _lib.lib().plattice_vertex_keys(_ptr(lattice.buf), _ptr(lattice.scratch), lattice.pd,
-                                             lattice.vd, lattice.w, lattice.h, _ptr(keys), m,
-                                             ctypes.byref(mm), _stream(lattice.device))
+    rc = _call(lattice.device.index, _lib_h().plattice_vertex_keys, _ptr(lattice.buf), _ptr(lattice.scratch),
+               lattice.pd, lattice.vd, lattice.w, lattice.h, _ptr(keys), m, ctypes.byref(mm),
+               _stream(lattice.device))
     if rc != _lib.OK:
-        raise _lib.PlatticeError("plattice_vertex_keys", rc)
+        _raise("plattice_vertex_keys", rc, "")
     return keys[:mm.value]
 
 
@@ -444,11 +516,11 @@ def set_lattice_precision(precision):
     reference, which computes in float only (permutohedral.cu:321-348)."""
     bits = {"fp32": 32, "bf16": 16}.get(precision)
     _require(bits is not None, f"lattice precision must be 'fp32' or 'bf16', got {precision!r}")
-    rc = _lib.lib().plattice_set_lattice_precision(bits)
+    rc = _lib_h().plattice_set_lattice_precision(bits)
     if rc != _lib.OK:
-        raise _lib.PlatticeError("plattice_set_lattice_precision", rc)
+        _raise("plattice_set_lattice_precision", rc, "")
 
 
 def get_lattice_precision():
     """``"fp32"`` or ``"bf16"``: the setting of set_lattice_precision."""
-    return "bf16" if _lib.lib().plattice_get_lattice_precision() == 16 else "fp32"
+    return "bf16" if _lib_h().plattice_get_lattice_precision() == 16 else "fp32"

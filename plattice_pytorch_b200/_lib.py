@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "libplattice_b200.so")
 
 OK, ERR_INVALID, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
 DEV_TABLE_FULL, DEV_WAIT_LIMIT, DEV_ROUND_LIMIT = 2, 4, 8
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _lock = threading.Lock()
 _lib = None
@@ -27,7 +27,7 @@ class PlatticeError(RuntimeError):
         msg = f"{call} failed: {error_string(status)} (status {status})"
         if detail:
             msg += f"; {detail}"
-        if status == ERR_CUDA:
+        if status in (ERR_CUDA, ERR_DEVICE):
             try:
                 msg += f"; {lib().plattice_last_error_detail().decode()}"
             except ImportError:
@@ -71,6 +71,20 @@ def lib():
         L.plattice_feature_grad_workspace_size.argtypes = [I, I, I, I, ctypes.POINTER(S)]
         L.plattice_feature_grad.restype = I
         L.plattice_feature_grad.argtypes = [P, P, P, P, P, P, P, S, P, S, I, I, I, I, P]
+        L.plattice_reuse_scratch_size.restype = I
+        L.plattice_reuse_scratch_size.argtypes = [I, I, I, I, I, ctypes.POINTER(S)]
+        L.plattice_poll_status.restype = I
+        L.plattice_poll_status.argtypes = []
+        L.plattice_prepare.restype = I
+        L.plattice_prepare.argtypes = [I, I]
+        L.plattice_forward_noalloc.restype = I
+        L.plattice_forward_noalloc.argtypes = [P, P, P, P, I, I, I, I, P]
+        L.plattice_noalloc_capacity.restype = S
+        L.plattice_noalloc_capacity.argtypes = []
+        L.plattice_noalloc_error_detail.restype = ctypes.c_char_p
+        L.plattice_noalloc_error_detail.argtypes = []
+        L.plattice_noalloc_status.restype = I
+        L.plattice_noalloc_status.argtypes = [ctypes.POINTER(I), ctypes.POINTER(I), P]
         L.plattice_filter_workspace_size.restype = I
         L.plattice_filter_workspace_size.argtypes = [I, I, I, I, ctypes.POINTER(S)]
         L.plattice_filter.restype = I
@@ -126,6 +140,16 @@ def batch_workspace_sizes(b, h, w, pd, vd):
     if rc != OK:
         raise PlatticeError("plattice_batch_workspace_sizes", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
     return lb.value, sb.value
+
+
+def reuse_scratch_size(b, h, w, pd, vd):
+    """Scratch bytes of a call on a kept lattice of b images (the front part
+    of the full scratch: the value rows of its blur)."""
+    n = ctypes.c_size_t(0)
+    rc = lib().plattice_reuse_scratch_size(b, h, w, pd, vd, ctypes.byref(n))
+    if rc != OK:
+        raise PlatticeError("plattice_reuse_scratch_size", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
+    return n.value
 
 
 def feature_grad_workspace_size(h, w, pd, vd):

@@ -60,7 +60,7 @@ def build(jobs=None, verbose_ptxas=False, force=False):
         obj = os.path.join(BUILD, f"plattice_pd{pd}.o")
         units.append((obj, [nvcc()] + NVCC_FLAGS + extra + [f"-DPL_PD={pd}", "-c",
                                                            os.path.join(CSRC, "plattice_pd.cu"), "-o", obj]))
-    for name in ("plattice_capi", "plattice_noalloc"):
+    for name in ("plattice_capi", "plattice_runtime", "plattice_noalloc"):
         obj = os.path.join(BUILD, f"{name}.o")
         units.append((obj, [nvcc()] + NVCC_FLAGS + extra + ["-c", os.path.join(CSRC, f"{name}.cu"), "-o", obj]))
     todo = [(o, c) for o, c in units if force or _stale(o, deps)]

@@ -9,6 +9,7 @@
 
 #include "../../include/plattice.h"
 #include "plattice_impl.cuh"
+#include "plattice_runtime.h"
 
 namespace pl {
 #define PL_DECLARE_PD(N)                                                                    \
@@ -16,6 +17,7 @@ namespace pl {
     extern template cudaError_t run_backward<N>(const CallArgs&);                            \
     extern template cudaError_t run_filter<N>(const CallArgs&);                              \
     extern template cudaError_t run_feature_grad<N>(const CallArgs&);                        \
+    extern template cudaError_t run_prepare<N>(const CallArgs&);                             \
     extern template cudaError_t run_export_keys<N>(const void*, const void*, const PlLayout&, \
                                                    int16_t*, int, cudaStream_t);
 PL_DECLARE_PD(1) PL_DECLARE_PD(2) PL_DECLARE_PD(3) PL_DECLARE_PD(4)
@@ -30,52 +32,6 @@ static int g_blur_half = 0;     // bfloat16 rows in the streaming blur passes
 static int g_blur_stream = 0;   // test support: streaming blur passes for every lattice
 
 static int blur_flags() { return (g_blur_half ? pl::kBlurHalf : 0) | (g_blur_stream ? pl::kBlurStream : 0); }
-
-// ---------------------------------------------------------------- side stream
-
-namespace {
-struct DeviceSide {
-    std::mutex mu;
-    cudaStream_t stream = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
-};
-DeviceSide g_side[64];
-}  // namespace
-
-namespace pl {
-cudaError_t side_fork(cudaStream_t main, SideFork* f) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    DeviceSide& d = g_side[dev];
-    d.mu.lock();
-    if (!d.stream) {
-        // the side stream's kernels (blur neighbours, latency-bound) are
-        // scheduled ahead of the caller's (the splat) when both wait for SMs
-        int least = 0, greatest = 0;
-        e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
-        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&d.stream, cudaStreamNonBlocking, greatest);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d.fork, cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d.join, cudaEventDisableTiming);
-        if (e != cudaSuccess) { d.mu.unlock(); return e; }
-    }
-    e = cudaEventRecord(d.fork, main);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(d.stream, d.fork, 0);
-    if (e != cudaSuccess) { d.mu.unlock(); return e; }
-    f->side = d.stream;
-    f->token = &d;
-    return cudaSuccess;
-}
-
-cudaError_t side_join(cudaStream_t main, SideFork* f) {
-    DeviceSide& d = *static_cast<DeviceSide*>(f->token);
-    cudaError_t e = cudaEventRecord(d.join, d.stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, d.join, 0);
-    d.mu.unlock();
-    return e;
-}
-}  // namespace pl
 
 // ---------------------------------------------------------------- profiling
 
@@ -186,17 +142,25 @@ static int sm_count_current() {
     return n;
 }
 
+static cudaError_t dispatch_prepare(const pl::CallArgs& a) {
+#define PL_PREP(N) pl::run_prepare<N>(a)
+    PL_PD_SWITCH(a.lay.pd, PL_PREP)
+#undef PL_PREP
+}
+
 // dimension checks of permuto.cpp:37-40 plus the index range of this build
-// (32-bit vertex ids and slot indices)
-static int check_dims(int h, int w, int pd, int vd) {
+// (32-bit vertex ids and slot indices) for b images
+static int check_dims_b(int b, int h, int w, int pd, int vd) {
     if (pd < 1 || pd > PL_MAX_PD || vd < 1 || vd > PL_MAX_VD) return PLATTICE_ERR_INVALID;
-    if (h < 0 || w < 0) return PLATTICE_ERR_INVALID;
-    if (h == 0 || w == 0) return PLATTICE_OK;
+    if (b < 0 || h < 0 || w < 0) return PLATTICE_ERR_INVALID;
+    if (b == 0 || h == 0 || w == 0) return PLATTICE_OK;
     PlLayout L;
-    pl_layout(&L, h, w, pd, vd);
+    pl_layout_batch(&L, b, h, w, pd, vd);
     if (L.slots > (1ll << 29)) return PLATTICE_ERR_INVALID;
     return PLATTICE_OK;
 }
+
+static int check_dims(int h, int w, int pd, int vd) { return check_dims_b(1, h, w, pd, vd); }
 
 static thread_local char g_last_error[256] = "";
 
@@ -205,6 +169,89 @@ static int cuda_status(cudaError_t e, const char* where = "") {
     snprintf(g_last_error, sizeof(g_last_error), "%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
     if (e == cudaErrorInvalidValue) return PLATTICE_ERR_INVALID;
     return PLATTICE_ERR_CUDA;
+}
+
+static const char* status_bits_text(int st) {
+    if (st & PL_ST_TABLE_FULL) return "hash table full";
+    if (st & PL_ST_SPIN) return "a bounded wait gave up";
+    if (st & PL_ST_SMEM_PROBE) return "tile table exhausted";
+    return "device failure";
+}
+
+// Device failures of earlier calls: their last kernel left the status word in
+// the host-mapped ring; the first call that finds a failure there returns
+// PLATTICE_ERR_DEVICE (without enqueueing its own work) and names it.
+static int poll_earlier(const char* call) {
+    const char* name = nullptr;
+    unsigned seq = 0;
+    const int st = pl::status_poll(&name, &seq);
+    if (st == 0) return PLATTICE_OK;
+    snprintf(g_last_error, sizeof(g_last_error),
+             "%s: an earlier call (%s, call #%u) reported device status bits %#x (%s); its outputs are invalid",
+             call, name ? name : "?", seq, st, status_bits_text(st));
+    return PLATTICE_ERR_DEVICE;
+}
+
+static void common_args(pl::CallArgs& a, void* stream, bool track, const char* call) {
+    a.stream = static_cast<cudaStream_t>(stream);
+    a.sm_count = sm_count_current();
+    a.cap_override_log2 = g_cap_override_log2;
+    a.filter_min_log2 = g_filter_min_log2;
+    a.blur_flags = blur_flags();
+    a.st = track ? pl::status_ticket(call) : pl::StatusTicket{nullptr, 0};
+}
+
+namespace pl {
+
+// Forward of b images (b = 1: plattice_forward).  track = false: no status
+// ticket (the no-allocation entry point, which allocates nothing).
+int forward_images(float* weight_out, float* out, const float* values, const float* features, void* lattice,
+                   size_t lattice_bytes, void* scratch, size_t scratch_bytes, int b, int pd, int vd, int w,
+                   int h, void* stream, bool track, const char* call) {
+    int rc = check_dims_b(b, h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (b == 0 || h == 0 || w == 0) return PLATTICE_OK;
+    if (!weight_out || !out || !values || !features || !lattice || !scratch) return PLATTICE_ERR_INVALID;
+    CallArgs a = {};
+    pl_layout_batch(&a.lay, b, h, w, pd, vd);
+    if (lattice_bytes < a.lay.lattice_bytes || scratch_bytes < a.lay.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
+    rc = poll_earlier(call);
+    if (rc != PLATTICE_OK) return rc;
+    a.features = features; a.values = values; a.weight_in = nullptr;
+    a.out = out; a.wout = weight_out;
+    a.lattice = lattice; a.scratch = scratch;
+    rows_in_scratch(a, scratch);
+    a.lattice_state = 0;
+    common_args(a, stream, track, call);
+    return cuda_status(dispatch_forward(a), call);
+}
+
+}  // namespace pl
+
+static int backward_images(float* grad_values_out, const float* grad, const float* weight_in,
+                           const float* features, void* lattice, size_t lattice_bytes, int lattice_state,
+                           void* scratch, size_t scratch_bytes, int b, int pd, int vd, int w, int h, void* stream,
+                           const char* call) {
+    int rc = check_dims_b(b, h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (b == 0 || h == 0 || w == 0) return PLATTICE_OK;
+    if (lattice_state < 0 || lattice_state > 2) return PLATTICE_ERR_INVALID;
+    if (!grad_values_out || !grad || !weight_in || !lattice || !scratch) return PLATTICE_ERR_INVALID;
+    if (lattice_state == 0 && !features) return PLATTICE_ERR_INVALID;
+    pl::CallArgs a = {};
+    pl_layout_batch(&a.lay, b, h, w, pd, vd);
+    if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
+    if (scratch_bytes < (lattice_state == 0 ? a.lay.scratch_bytes : a.lay.rows_bytes)) return PLATTICE_ERR_WORKSPACE;
+    rc = poll_earlier(call);
+    if (rc != PLATTICE_OK) return rc;
+    a.features = features; a.values = grad; a.weight_in = weight_in;
+    a.out = grad_values_out; a.wout = nullptr;
+    a.lattice = lattice;
+    a.scratch = lattice_state == 0 ? scratch : nullptr;
+    rows_in_scratch(a, scratch);
+    a.lattice_state = lattice_state;
+    common_args(a, stream, true, call);
+    return cuda_status(dispatch_backward(a), call);
 }
 
 extern "C" {
@@ -224,13 +271,14 @@ const char* plattice_error_string(int status) {
     }
 }
 
-int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes, size_t* scratch_bytes) {
-    const int rc = check_dims(h, w, pd, vd);
+int plattice_batch_workspace_sizes(int b, int h, int w, int pd, int vd, size_t* lattice_bytes,
+                                   size_t* scratch_bytes) {
+    const int rc = check_dims_b(b, h, w, pd, vd);
     if (rc != PLATTICE_OK) return rc;
     size_t lb = 256, sb = 256;
-    if (h > 0 && w > 0) {
+    if (b > 0 && h > 0 && w > 0) {
         PlLayout L;
-        pl_layout(&L, h, w, pd, vd);
+        pl_layout_batch(&L, b, h, w, pd, vd);
         lb = L.lattice_bytes;
         sb = L.scratch_bytes;
     }
@@ -239,152 +287,68 @@ int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes
     return PLATTICE_OK;
 }
 
+int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes, size_t* scratch_bytes) {
+    return plattice_batch_workspace_sizes(1, h, w, pd, vd, lattice_bytes, scratch_bytes);
+}
+
+int plattice_reuse_scratch_size(int b, int h, int w, int pd, int vd, size_t* bytes) {
+    const int rc = check_dims_b(b, h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (!bytes) return PLATTICE_ERR_INVALID;
+    *bytes = 256;
+    if (b > 0 && h > 0 && w > 0) {
+        PlLayout L;
+        pl_layout_batch(&L, b, h, w, pd, vd);
+        *bytes = L.rows_bytes;
+    }
+    return PLATTICE_OK;
+}
+
 int plattice_forward(float* weight_out, float* out, const float* values, const float* features,
                      void* lattice, size_t lattice_bytes, void* scratch, size_t scratch_bytes, int pd,
                      int vd, int w, int h, void* stream) {
-    int rc = check_dims(h, w, pd, vd);
-    if (rc != PLATTICE_OK) return rc;
-    if (h == 0 || w == 0) return PLATTICE_OK;
-    if (!weight_out || !out || !values || !features || !lattice || !scratch) return PLATTICE_ERR_INVALID;
-    pl::CallArgs a = {};
-    pl_layout(&a.lay, h, w, pd, vd);
-    if (lattice_bytes < a.lay.lattice_bytes || scratch_bytes < a.lay.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
-    a.features = features; a.values = values; a.weight_in = nullptr;
-    a.out = out; a.wout = weight_out;
-    a.lattice = lattice; a.scratch = scratch;
-    a.stream = static_cast<cudaStream_t>(stream);
-    a.sm_count = sm_count_current();
-    a.lattice_state = 0;
-    a.cap_override_log2 = g_cap_override_log2;
-    a.filter_min_log2 = g_filter_min_log2;
-    a.blur_flags = blur_flags();
-    return cuda_status(dispatch_forward(a), "plattice_forward");
+    return pl::forward_images(weight_out, out, values, features, lattice, lattice_bytes, scratch, scratch_bytes, 1,
+                              pd, vd, w, h, stream, true, "plattice_forward");
 }
 
 int plattice_backward(float* grad_values_out, const float* grad, const float* weight_in, const float* features,
                       void* lattice, size_t lattice_bytes, int lattice_state, void* scratch, size_t scratch_bytes,
                       int pd, int vd, int w, int h, void* stream) {
-    int rc = check_dims(h, w, pd, vd);
-    if (rc != PLATTICE_OK) return rc;
-    if (h == 0 || w == 0) return PLATTICE_OK;
-    if (lattice_state < 0 || lattice_state > 2) return PLATTICE_ERR_INVALID;
-    if (!grad_values_out || !grad || !weight_in || !lattice) return PLATTICE_ERR_INVALID;
-    if (lattice_state == 0 && (!scratch || !features)) return PLATTICE_ERR_INVALID;
-    pl::CallArgs a = {};
-    pl_layout(&a.lay, h, w, pd, vd);
-    if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
-    if (lattice_state == 0 && scratch_bytes < a.lay.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
-    a.features = features; a.values = grad; a.weight_in = weight_in;
-    a.out = grad_values_out; a.wout = nullptr;
-    a.lattice = lattice; a.scratch = scratch;
-    a.stream = static_cast<cudaStream_t>(stream);
-    a.sm_count = sm_count_current();
-    a.lattice_state = lattice_state;
-    a.cap_override_log2 = g_cap_override_log2;
-    a.filter_min_log2 = g_filter_min_log2;
-    a.blur_flags = blur_flags();
-    return cuda_status(dispatch_backward(a), "plattice_backward");
-}
-
-// ---------------------------------------------------------------- batches
-
-// B images of one shape: their lattices one after the other in `lattice`
-// (each lattice region padded to 256 bytes), one scratch region shared by
-// the images, which run one after the other on the caller's stream.
-static size_t batch_lattice_stride(const PlLayout& L) { return pl_align(L.lattice_bytes); }
-
-int plattice_batch_workspace_sizes(int b, int h, int w, int pd, int vd, size_t* lattice_bytes,
-                                   size_t* scratch_bytes) {
-    if (b < 0) return PLATTICE_ERR_INVALID;
-    size_t lb = 0, sb = 0;
-    const int rc = plattice_workspace_sizes(h, w, pd, vd, &lb, &sb);
-    if (rc != PLATTICE_OK) return rc;
-    if (lattice_bytes) *lattice_bytes = pl_align(lb) * (size_t)(b > 0 ? b : 1);
-    if (scratch_bytes) *scratch_bytes = sb;
-    return PLATTICE_OK;
+    return backward_images(grad_values_out, grad, weight_in, features, lattice, lattice_bytes, lattice_state,
+                           scratch, scratch_bytes, 1, pd, vd, w, h, stream, "plattice_backward");
 }
 
 int plattice_forward_batch(float* weight_out, float* out, const float* values, const float* features,
                            void* lattice, size_t lattice_bytes, void* scratch, size_t scratch_bytes, int b,
                            int pd, int vd, int w, int h, void* stream) {
-    int rc = check_dims(h, w, pd, vd);
-    if (rc != PLATTICE_OK) return rc;
-    if (b < 0) return PLATTICE_ERR_INVALID;
-    if (b == 0 || h == 0 || w == 0) return PLATTICE_OK;
-    if (!weight_out || !out || !values || !features || !lattice || !scratch) return PLATTICE_ERR_INVALID;
-    PlLayout L;
-    pl_layout(&L, h, w, pd, vd);
-    const size_t stride = batch_lattice_stride(L);
-    if (lattice_bytes < stride * (size_t)b || scratch_bytes < L.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
-    const size_t n = (size_t)h * w;
-    for (int i = 0; i < b; ++i) {
-        rc = plattice_forward(weight_out + i * n, out + i * n * vd, values + i * n * vd, features + i * n * pd,
-                              static_cast<char*>(lattice) + i * stride, stride, scratch, scratch_bytes, pd, vd, w,
-                              h, stream);
-        if (rc != PLATTICE_OK) return rc;
-    }
-    return PLATTICE_OK;
+    return pl::forward_images(weight_out, out, values, features, lattice, lattice_bytes, scratch, scratch_bytes, b,
+                              pd, vd, w, h, stream, true, "plattice_forward_batch");
 }
 
 int plattice_backward_batch(float* grad_values_out, const float* grad, const float* weight_in, const float* features,
                             void* lattice, size_t lattice_bytes, int lattice_state, void* scratch,
                             size_t scratch_bytes, int b, int pd, int vd, int w, int h, void* stream) {
-    int rc = check_dims(h, w, pd, vd);
-    if (rc != PLATTICE_OK) return rc;
-    if (b < 0 || lattice_state < 0 || lattice_state > 2) return PLATTICE_ERR_INVALID;
-    if (b == 0 || h == 0 || w == 0) return PLATTICE_OK;
-    if (!grad_values_out || !grad || !weight_in || !lattice) return PLATTICE_ERR_INVALID;
-    if (lattice_state == 0 && (!scratch || !features)) return PLATTICE_ERR_INVALID;
-    PlLayout L;
-    pl_layout(&L, h, w, pd, vd);
-    const size_t stride = batch_lattice_stride(L);
-    if (lattice_bytes < stride * (size_t)b) return PLATTICE_ERR_WORKSPACE;
-    if (lattice_state == 0 && scratch_bytes < L.scratch_bytes) return PLATTICE_ERR_WORKSPACE;
-    const size_t n = (size_t)h * w;
-    for (int i = 0; i < b; ++i) {
-        rc = plattice_backward(grad_values_out + i * n * vd, grad + i * n * vd, weight_in + i * n,
-                               features ? features + i * n * pd : nullptr, static_cast<char*>(lattice) + i * stride,
-                               stride, lattice_state, scratch, scratch_bytes, pd, vd, w, h, stream);
-        if (rc != PLATTICE_OK) return rc;
-    }
-    return PLATTICE_OK;
+    return backward_images(grad_values_out, grad, weight_in, features, lattice, lattice_bytes, lattice_state,
+                           scratch, scratch_bytes, b, pd, vd, w, h, stream, "plattice_backward_batch");
 }
 
 // ---------------------------------------------------------------- kept lattice
 
-// Value rows of a filter call: two buffers of slots x pad(vd+1) floats.
-static size_t filter_ws_half(const PlLayout& L) { return pl_align((size_t)L.slots * (size_t)L.CPf * 4); }
-
 int plattice_filter_workspace_size(int h, int w, int pd, int vd, size_t* bytes) {
-    const int rc = check_dims(h, w, pd, vd);
-    if (rc != PLATTICE_OK) return rc;
-    if (!bytes) return PLATTICE_ERR_INVALID;
-    *bytes = 256;
-    if (h > 0 && w > 0) {
-        PlLayout L;
-        pl_layout(&L, h, w, pd, vd);
-        *bytes = 2 * filter_ws_half(L);
-    }
-    return PLATTICE_OK;
+    return plattice_reuse_scratch_size(1, h, w, pd, vd, bytes);
 }
 
 // The checks shared by the two kept-lattice calls; fills the layout and the
-// value buffers.
+// value rows.
 static int kept_lattice_args(pl::CallArgs& a, size_t lattice_bytes, void* ws, size_t ws_bytes, int pd, int vd,
-                             int w, int h, void* stream) {
+                             int w, int h, void* stream, const char* call) {
     pl_layout(&a.lay, h, w, pd, vd);
-    // the arrays a filter reads precede the backward value rows, whose size
-    // is the only part of the lattice that depends on vd
-    if (lattice_bytes < a.lay.off_vb0) return PLATTICE_ERR_WORKSPACE;
-    const size_t half = filter_ws_half(a.lay);
-    if (ws_bytes < 2 * half) return PLATTICE_ERR_WORKSPACE;
-    a.vbuf0 = static_cast<float*>(ws);
-    a.vbuf1 = reinterpret_cast<float*>(static_cast<char*>(ws) + half);
-    a.stream = static_cast<cudaStream_t>(stream);
-    a.sm_count = sm_count_current();
-    a.cap_override_log2 = g_cap_override_log2;
-    a.filter_min_log2 = g_filter_min_log2;
-    a.blur_flags = blur_flags();
+    if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
+    if (ws_bytes < a.lay.rows_bytes) return PLATTICE_ERR_WORKSPACE;
+    const int rc = poll_earlier(call);
+    if (rc != PLATTICE_OK) return rc;
+    rows_in_scratch(a, ws);
+    common_args(a, stream, true, call);
     return PLATTICE_OK;
 }
 
@@ -395,7 +359,7 @@ int plattice_filter(float* weight_out, float* out, const float* values, void* la
     if (h == 0 || w == 0) return PLATTICE_OK;
     if (!weight_out || !out || !values || !lattice || !values_ws) return PLATTICE_ERR_INVALID;
     pl::CallArgs a = {};
-    rc = kept_lattice_args(a, lattice_bytes, values_ws, values_ws_bytes, pd, vd, w, h, stream);
+    rc = kept_lattice_args(a, lattice_bytes, values_ws, values_ws_bytes, pd, vd, w, h, stream, "plattice_filter");
     if (rc != PLATTICE_OK) return rc;
     a.values = values;
     a.out = out;
@@ -412,7 +376,8 @@ int plattice_filter_backward(float* grad_values_out, const float* grad, const fl
     if (h == 0 || w == 0) return PLATTICE_OK;
     if (!grad_values_out || !grad || !weight_in || !lattice || !values_ws) return PLATTICE_ERR_INVALID;
     pl::CallArgs a = {};
-    rc = kept_lattice_args(a, lattice_bytes, values_ws, values_ws_bytes, pd, vd, w, h, stream);
+    rc = kept_lattice_args(a, lattice_bytes, values_ws, values_ws_bytes, pd, vd, w, h, stream,
+                           "plattice_filter_backward");
     if (rc != PLATTICE_OK) return rc;
     a.values = grad;
     a.weight_in = weight_in;
@@ -425,9 +390,10 @@ int plattice_filter_backward(float* grad_values_out, const float* grad, const fl
 // ---------------------------------------------------------------- feature gradient
 
 // Workspace: two result flags, four lattice row buffers (R and H, ping-pong)
-// of slots x pad(vd+1) floats, and the per-pixel (G, -G.out) rows.
+// of slots x pad(vd+1) floats, the blur's bookkeeping bytes, and the
+// per-pixel (G, -G.out) rows.
 struct FgradWs {
-    size_t flags, r0, r1, h0, h1, ev, total;
+    size_t flags, r0, r1, h0, h1, bst, ev, total;
 };
 
 static FgradWs fgrad_ws(const PlLayout& L) {
@@ -438,7 +404,8 @@ static FgradWs fgrad_ws(const PlLayout& L) {
     W.r1 = W.r0 + rows;
     W.h0 = W.r1 + rows;
     W.h1 = W.h0 + rows;
-    W.ev = W.h1 + rows;
+    W.bst = W.h1 + rows;
+    W.ev = W.bst + pl_align(2 * (size_t)L.slots);
     W.total = W.ev + pl_align((size_t)L.h * L.w * (size_t)(L.vd + 1) * 4);
     return W;
 }
@@ -466,15 +433,18 @@ int plattice_feature_grad(float* grad_features_out, const float* grad, const flo
         return PLATTICE_ERR_INVALID;
     pl::CallArgs a = {};
     pl_layout(&a.lay, h, w, pd, vd);
-    if (lattice_bytes < a.lay.off_vb0) return PLATTICE_ERR_WORKSPACE;
+    if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
     const FgradWs W = fgrad_ws(a.lay);
     if (ws_bytes < W.total) return PLATTICE_ERR_WORKSPACE;
+    rc = poll_earlier("plattice_feature_grad");
+    if (rc != PLATTICE_OK) return rc;
     char* b = static_cast<char*>(ws);
     a.flags = reinterpret_cast<int*>(b + W.flags);
-    a.vbuf0 = reinterpret_cast<float*>(b + W.r0);
-    a.vbuf1 = reinterpret_cast<float*>(b + W.r1);
+    a.v0 = reinterpret_cast<float*>(b + W.r0);
+    a.v1 = reinterpret_cast<float*>(b + W.r1);
     a.hbuf0 = reinterpret_cast<float*>(b + W.h0);
     a.hbuf1 = reinterpret_cast<float*>(b + W.h1);
+    a.bstate = reinterpret_cast<uint8_t*>(b + W.bst);
     a.evec = reinterpret_cast<float*>(b + W.ev);
     a.features = features;
     a.values = values;
@@ -483,12 +453,20 @@ int plattice_feature_grad(float* grad_features_out, const float* grad, const flo
     a.out_in = out;
     a.out = grad_features_out;
     a.lattice = lattice;
-    a.stream = static_cast<cudaStream_t>(stream);
-    a.sm_count = sm_count_current();
-    a.cap_override_log2 = g_cap_override_log2;
-    a.filter_min_log2 = g_filter_min_log2;
-    a.blur_flags = blur_flags();
+    common_args(a, stream, true, "plattice_feature_grad");
     return cuda_status(dispatch_feature_grad(a), "plattice_feature_grad");
+}
+
+// ---------------------------------------------------------------- status, set-up, test support
+
+int plattice_poll_status(void) { return poll_earlier("plattice_poll_status"); }
+
+int plattice_prepare(int pd, int vd) {
+    const int rc = check_dims(1, 1, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    pl::CallArgs a = {};
+    pl_layout(&a.lay, 1, 1, pd, vd);
+    return cuda_status(dispatch_prepare(a), "plattice_prepare");
 }
 
 int plattice_lattice_info(const void* lattice, int* status, int* m, int* u_total, int* cap_log2, void* stream) {

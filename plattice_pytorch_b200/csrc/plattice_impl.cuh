@@ -8,6 +8,7 @@
 
 #include "plattice_kernels.cuh"
 #include "plattice_profile.h"
+#include "plattice_runtime.h"
 
 namespace pl {
 
@@ -18,16 +19,17 @@ struct CallArgs {
     float* out;
     float* wout;             // forward: normaliser output
     void* lattice;
-    void* scratch;
+    void* scratch;           // build part of the scratch (lattice builds only)
     PlLayout lay;
     cudaStream_t stream;
     int sm_count;
-    int lattice_state;       // backward: 0 rebuild, 1 fresh from forward, 2 reuse (re-zero)
+    int lattice_state;       // backward: 0 rebuild, 1 or 2 reuse the lattice
     int cap_override_log2;
     int filter_min_log2;     // 0: the default (tables of 2^22 cells and more)
     int blur_flags;          // kBlurHalf (bfloat16 rows of large lattices), kBlurStream (tests)
-    float* vbuf0;            // value buffers of a filter call on a kept lattice (else null:
-    float* vbuf1;            // the forward's scratch rows / the lattice's backward rows)
+    float* v0;               // lattice value rows of the call's blur (ping-pong) and
+    float* v1;               // their bookkeeping: the scratch's front part, or a
+    uint8_t* bstate;         // kept-lattice call's workspace
     // feature gradient: dL/dout, the forward's out, and lattice rows / flags in the workspace
     const float* grad_in;
     const float* out_in;
@@ -35,6 +37,7 @@ struct CallArgs {
     float* hbuf1;
     float* evec;
     int* flags;
+    StatusTicket st;         // where the call's last kernel reports the status word
 };
 
 inline LatView lat_view(void* base, const PlLayout& L) {
@@ -50,12 +53,10 @@ inline LatView lat_view(void* base, const PlLayout& L) {
     v.first_lid = reinterpret_cast<uint16_t*>(b + L.off_first_lid);
     v.staged_vid = reinterpret_cast<int*>(b + L.off_staged_vid);
     v.nbr = reinterpret_cast<int2*>(b + L.off_nbr);
-    v.vb0 = reinterpret_cast<float*>(b + L.off_vb0);
-    v.vb1 = reinterpret_cast<float*>(b + L.off_vb1);
-    v.bstate = reinterpret_cast<uint8_t*>(b + L.off_bstate);
     return v;
 }
 
+// `base`: the whole scratch buffer (front part + build part)
 inline ScrView scr_view(void* base, const PlLayout& L) {
     char* b = static_cast<char*>(base);
     ScrView v;
@@ -65,9 +66,15 @@ inline ScrView scr_view(void* base, const PlLayout& L) {
     v.owner = reinterpret_cast<int*>(b + L.off_owner);
     v.vid_of = reinterpret_cast<int*>(b + L.off_vid_of);
     v.vkeys = reinterpret_cast<uint4*>(b + L.off_vkeys);
-    v.vf0 = reinterpret_cast<float*>(b + L.off_vf0);
-    v.vf1 = reinterpret_cast<float*>(b + L.off_vf1);
     return v;
+}
+
+// The value rows of a call in the front part of a scratch buffer.
+inline void rows_in_scratch(CallArgs& a, void* scratch) {
+    char* b = static_cast<char*>(scratch);
+    a.v0 = reinterpret_cast<float*>(b + a.lay.off_v0);
+    a.v1 = reinterpret_cast<float*>(b + a.lay.off_v1);
+    a.bstate = reinterpret_cast<uint8_t*>(b + a.lay.off_bstate);
 }
 
 // Scale factors of permutohedral.cu:507-508, in float on the host as there.
@@ -85,6 +92,8 @@ inline EmbedConsts embed_consts(int pd) {
 inline Geo make_geo(const CallArgs& a) {
     Geo g;
     g.h = a.lay.h; g.w = a.lay.w; g.tiles_x = a.lay.tiles_x; g.tiles = a.lay.tiles;
+    g.tiles_img = a.lay.tiles_img;
+    g.n_img = a.lay.n_img;
     g.cap_max_log2 = a.lay.cap_max_log2;
     g.cap_override_log2 = a.cap_override_log2;
     g.filter_min_log2 = a.filter_min_log2 > 0 ? a.filter_min_log2 : 22;   // a 16 MB table and up
@@ -111,28 +120,37 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-// opt in to more than 48 KB of dynamic shared memory, once per device
+// opt in to more than 48 KB of dynamic shared memory, once per context
 template <int PD>
-cudaError_t prepare_tile_build() {
-    static bool done[64] = {};
-    constexpr int smem = tile_build_smem_bytes<PD>();
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64 || !done[dev]) {
-        e = cudaFuncSetAttribute(k_tile_build<PD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) done[dev] = true;
-    }
-    return cudaSuccess;
+cudaError_t tile_build_attr(int* v) {
+    *v = 1;
+    return cudaFuncSetAttribute(k_tile_build<PD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                tile_build_smem_bytes<PD>());
 }
 
-// Build the lattice: tile dedup (which also zeroes the lattice value rows),
-// table clear, global insert, vertex ids.  Blur neighbours follow, alongside
-// the first splat (neighbors_alongside).
 template <int PD>
-cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
-                          float* zero_f, int cpf, float* zero_b, int cpb) {
+cudaError_t prepare_tile_build() {
+    int v = 0;
+    return kernel_once(reinterpret_cast<const void*>(k_tile_build<PD>), tile_build_attr<PD>, &v);
+}
+
+// the blur kernel's dynamic shared memory and its co-resident CTAs per SM
+template <int PD, int CP>
+cudaError_t blur_attr(int* per_sm) {
+    cudaError_t e = cudaFuncSetAttribute(k_blur_all<PD, CP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kBlurQueueBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_blur_all<PD, CP>, kBlurThreads, kBlurQueueBytes);
+    if (e != cudaSuccess) return e;
+    return *per_sm < 1 ? cudaErrorLaunchOutOfResources : cudaSuccess;
+}
+
+// Build the lattice: tile dedup (which also zeroes the lattice value rows
+// `zero` of cp floats each), table clear, global insert, vertex ids.  Blur
+// neighbours follow, alongside the first splat (neighbors_alongside).
+template <int PD>
+cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv, float* zero,
+                          int cp) {
     using C = Cfg<PD>;
     const cudaStream_t s = a.stream;
     const int grid = a.sm_count * 8;
@@ -143,23 +161,13 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     const EmbedConsts ec = embed_consts(PD);
     PL_LAUNCH(STAGE_TILE_BUILD, s,
               e = launch_k(k_tile_build<PD>, dim3(a.lay.tiles), dim3(C::P), tile_build_smem_bytes<PD>(), s, false,
-                             a.features, geo, ec, Lv, Sv, zero_f, cpf, zero_b, cpb));
+                             a.features, geo, ec, Lv, Sv, zero, cp));
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_CLEAR, s, e = launch_k(k_clear, dim3(grid), dim3(256), 0, s, false, geo, Lv, Sv));
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_INSERT, s, e = launch_k(k_insert<PD>, dim3(grid * 2), dim3(256), 0, s, false, geo, Lv, Sv));
     return e;
 }
-
-// Side stream of the current device, forked from and joined back into the
-// caller's stream with events, so that independent kernels overlap (defined
-// in plattice_capi.cu; the fork is held by one host thread at a time).
-struct SideFork {
-    cudaStream_t side;
-    void* token;
-};
-cudaError_t side_fork(cudaStream_t main, SideFork* f);
-cudaError_t side_join(cudaStream_t main, SideFork* f);
 
 // Blur neighbours on the side stream while `main_work` runs on the caller's stream.
 template <int PD, typename MainWork>
@@ -183,49 +191,40 @@ template <int PD, int CP>
 cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1, int reverse,
                             int* final_flag = nullptr) {
     if (!final_flag) final_flag = &Lv.hdr->blur_final;
-    static int per_sm[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    int n = 0;
+    cudaError_t e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CP>), blur_attr<PD, CP>, &n);
     if (e != cudaSuccess) return e;
-    int n = (dev >= 0 && dev < 64) ? per_sm[dev] : 0;
-    if (n == 0) {
-        e = cudaFuncSetAttribute(k_blur_all<PD, CP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBlurQueueBytes);
-        if (e != cudaSuccess) return e;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_blur_all<PD, CP>, kBlurThreads, kBlurQueueBytes);
-        if (e != cudaSuccess) return e;
-        if (n < 1) return cudaErrorLaunchOutOfResources;
-        if (dev >= 0 && dev < 64) per_sm[dev] = n;
-    }
     const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
               e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), kBlurQueueBytes, a.stream, true, Lv,
-                           b0, b1, reverse, final_flag, a.blur_flags));
+                           b0, b1, a.bstate, reverse, final_flag, a.blur_flags));
     return e;
 }
 
 template <int PD, int V>
 cudaError_t forward_v(const CallArgs& a) {
-    constexpr int CPF = pad_ch(V + 1), CPB = pad_ch(V);
+    constexpr int CPF = pad_ch(V + 1);
     const Geo geo = make_geo(a);
     const LatView Lv = lat_view(a.lattice, a.lay);
     const ScrView Sv = scr_view(a.scratch, a.lay);
-    cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, Sv.vf0, CPF, Lv.vb0, CPB);
+    cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPF);
     if (e != cudaSuccess) return e;
     // neighbour lookups (L2-latency-bound) overlap the splat (HBM-bound)
     e = neighbors_alongside<PD>(a, geo, Lv, Sv, [&] {
         cudaError_t es;
         PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
                   es = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
-                                  a.values, (const float*)nullptr, geo, Lv, Sv, 1, Sv.vf0));
+                                  a.values, (const float*)nullptr, geo, Lv, Sv, 1, a.v0));
         return es;
     });
     if (e != cudaSuccess) return e;
     // blur in axis order 0..pd (permutohedral.cu:585)
-    e = launch_blur_all<PD, CPF>(a, Lv, Sv.vf0, Sv.vf1, 0);
+    e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
               e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
-                           false, a.out, a.wout, geo, Lv, (const float*)Sv.vf0, (const float*)Sv.vf1));
+                           false, a.out, a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot,
+                           a.st.seq));
     return e;
 }
 
@@ -233,41 +232,36 @@ template <int PD, int V>
 cudaError_t backward_v(const CallArgs& a) {
     constexpr int CPB = pad_ch(V);
     const Geo geo = make_geo(a);
-    LatView Lv = lat_view(a.lattice, a.lay);
+    const LatView Lv = lat_view(a.lattice, a.lay);
     const ScrView Sv = a.scratch ? scr_view(a.scratch, a.lay) : ScrView{};
-    if (a.vbuf0) {   // a filter on a kept lattice: the caller's value rows
-        Lv.vb0 = a.vbuf0;
-        Lv.vb1 = a.vbuf1;
-    }
     const int grid = a.sm_count * 8;
     cudaError_t e = cudaSuccess;
     auto splat = [&] {
         cudaError_t es;
         PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
                   es = launch_k(k_splat<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
-                                  a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, Lv.vb0));
+                                  a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, a.v0));
         return es;
     };
-    if (a.lattice_state == 0) {
-        e = build_lattice<PD>(a, geo, Lv, Sv, nullptr, 0, Lv.vb0, CPB);
+    if (a.lattice_state == 0) {   // rebuild (permutohedral.cu:615-635); the tile build zeroes the rows
+        e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPB);
         if (e != cudaSuccess) return e;
         e = neighbors_alongside<PD>(a, geo, Lv, Sv, splat);
     } else {
-        if (a.lattice_state == 2) {
-            PL_LAUNCH(STAGE_ZERO, a.stream,
-                      e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, Lv.vb0,
-                                     (const LatticeHeader*)Lv.hdr, CPB));
-            if (e != cudaSuccess) return e;
-        }
+        PL_LAUNCH(STAGE_ZERO, a.stream,
+                  e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.v0,
+                               (const LatticeHeader*)Lv.hdr, CPB));
+        if (e != cudaSuccess) return e;
         e = splat();
     }
     if (e != cudaSuccess) return e;
     // blur in axis order pd..0 (permutohedral.cu:647)
-    e = launch_blur_all<PD, CPB>(a, Lv, Lv.vb0, Lv.vb1, 1);
+    e = launch_blur_all<PD, CPB>(a, Lv, a.v0, a.v1, 1);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
               e = launch_k(k_slice<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
-                           false, a.out, (float*)nullptr, geo, Lv, (const float*)Lv.vb0, (const float*)Lv.vb1));
+                           false, a.out, (float*)nullptr, geo, Lv, (const float*)a.v0, (const float*)a.v1,
+                           a.st.slot, a.st.seq));
     return e;
 }
 
@@ -282,18 +276,18 @@ cudaError_t filter_v(const CallArgs& a) {
     const int grid = a.sm_count * 8;
     cudaError_t e;
     PL_LAUNCH(STAGE_ZERO, a.stream,
-              e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.vbuf0,
+              e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.v0,
                            (const LatticeHeader*)Lv.hdr, CPF));
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
               e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
-                           a.values, (const float*)nullptr, geo, Lv, Sv, 0, a.vbuf0));
+                           a.values, (const float*)nullptr, geo, Lv, Sv, 0, a.v0));
     if (e != cudaSuccess) return e;
-    e = launch_blur_all<PD, CPF>(a, Lv, a.vbuf0, a.vbuf1, 0);
+    e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
               e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.out,
-                           a.wout, geo, Lv, (const float*)a.vbuf0, (const float*)a.vbuf1));
+                           a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot, a.st.seq));
     return e;
 }
 
@@ -309,15 +303,15 @@ cudaError_t fgrad_v(const CallArgs& a) {
     const int grid = a.sm_count * 8;
     cudaError_t e;
     // R: the forward's lattice values
-    e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.vbuf0, (const LatticeHeader*)Lv.hdr, CPF);
+    e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.v0, (const LatticeHeader*)Lv.hdr, CPF);
     if (e != cudaSuccess) return e;
     e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.values,
-                 (const float*)nullptr, geo, Lv, Sv, 0, a.vbuf0);
+                 (const float*)nullptr, geo, Lv, Sv, 0, a.v0);
     if (e != cudaSuccess) return e;
-    e = launch_blur_all<PD, CPF>(a, Lv, a.vbuf0, a.vbuf1, 0, a.flags);
+    e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0, a.flags);
     if (e != cudaSuccess) return e;
     // H: the lattice gradient, V+1 channels of (G, -G.out) weighted by 1/Z
-    const size_t n = (size_t)a.lay.h * a.lay.w;
+    const size_t n = (size_t)a.lay.b * (size_t)a.lay.n_img;
     e = launch_k(k_fgrad_prep<V>, dim3(grid), dim3(256), 0, a.stream, false, a.evec, a.grad_in, a.out_in, n);
     if (e != cudaSuccess) return e;
     e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.hbuf0, (const LatticeHeader*)Lv.hdr, CPF);
@@ -328,8 +322,40 @@ cudaError_t fgrad_v(const CallArgs& a) {
     e = launch_blur_all<PD, CPF>(a, Lv, a.hbuf0, a.hbuf1, 1, a.flags + 1);
     if (e != cudaSuccess) return e;
     return launch_k(k_fgrad<PD, V>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.out, a.features,
-                    a.values, a.grad_in, a.out_in, a.weight_in, geo, embed_consts(PD), Lv, (const float*)a.vbuf0,
-                    (const float*)a.vbuf1, (const float*)a.hbuf0, (const float*)a.hbuf1, (const int*)a.flags);
+                    a.values, a.grad_in, a.out_in, a.weight_in, geo, embed_consts(PD), Lv, (const float*)a.v0,
+                    (const float*)a.v1, (const float*)a.hbuf0, (const float*)a.hbuf1, (const int*)a.flags,
+                    a.st.slot, a.st.seq);
+}
+
+// Everything the first call of (PD, V) does on a context besides the filter
+// itself: kernel attributes, the side stream, and the loading of every kernel
+// of the forward and backward (lazy module loading otherwise loads each on
+// its first launch).
+template <int PD, int V>
+cudaError_t prepare_v(const CallArgs&) {
+    constexpr int CPF = pad_ch(V + 1), CPB = pad_ch(V);
+    cudaError_t e = prepare_tile_build<PD>();
+    int n = 0;
+    if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CPF>), blur_attr<PD, CPF>, &n);
+    if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CPB>), blur_attr<PD, CPB>, &n);
+    const void* fns[] = {reinterpret_cast<const void*>(k_tile_build<PD>), reinterpret_cast<const void*>(k_clear),
+                         reinterpret_cast<const void*>(k_insert<PD>), reinterpret_cast<const void*>(k_neighbors<PD>),
+                         reinterpret_cast<const void*>(k_splat<PD, V, true>),
+                         reinterpret_cast<const void*>(k_splat<PD, V, false>),
+                         reinterpret_cast<const void*>(k_slice<PD, V, true>),
+                         reinterpret_cast<const void*>(k_slice<PD, V, false>),
+                         reinterpret_cast<const void*>(k_zero_rows)};
+    for (const void* f : fns) {
+        cudaFuncAttributes fa;
+        if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, f);
+    }
+    if (e == cudaSuccess) {
+        SideFork f;
+        cudaStream_t s = nullptr;
+        e = side_fork(s, &f);   // creates the side stream and its events (fork on the legacy stream, no work)
+        if (e == cudaSuccess) e = side_join(s, &f);
+    }
+    return e;
 }
 
 #define PL_DISPATCH_V(FN, PDV, ARGS)                      \
@@ -356,6 +382,9 @@ cudaError_t run_filter(const CallArgs& a) { PL_DISPATCH_V(filter_v, PD, a) }
 
 template <int PD>
 cudaError_t run_feature_grad(const CallArgs& a) { PL_DISPATCH_V(fgrad_v, PD, a) }
+
+template <int PD>
+cudaError_t run_prepare(const CallArgs& a) { PL_DISPATCH_V(prepare_v, PD, a) }
 
 template <int PD>
 cudaError_t run_export_keys(const void* lattice, const void* scratch, const PlLayout& lay, int16_t* out,

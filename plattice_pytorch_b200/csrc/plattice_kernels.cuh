@@ -57,11 +57,32 @@ struct EmbedConsts {
 };
 
 struct Geo {
-    int h, w, tiles_x, tiles;
+    int h, w, tiles_x, tiles;   // tiles: of all images
+    int tiles_img;              // tiles per image
+    long long n_img;            // pixels per image
     int cap_max_log2, cap_override_log2;
     int idx_bits;   // bits that hold 1 + any staged index of the call (global table cells)
     int filter_min_log2;   // table size (log2 cells) from which lookups consult the miss filter
 };
+
+// Image, tile origin and first pixel of tile `tile` (tiles numbered image by
+// image, row-major within an image).
+struct TilePos {
+    int img, x0, y0;
+    long long pix0;   // index of pixel (x0, y0) in the [b][h][w] pixel array
+};
+
+template <int TW, int TH>
+__device__ __forceinline__ TilePos tile_pos(const Geo& g, int tile) {
+    TilePos t;
+    t.img = tile / g.tiles_img;
+    const int ti = tile - t.img * g.tiles_img;
+    const int ty = ti / g.tiles_x;
+    t.x0 = (ti - ty * g.tiles_x) * TW;
+    t.y0 = ty * TH;
+    t.pix0 = (long long)t.img * g.n_img + (long long)t.y0 * g.w + t.x0;
+    return t;
+}
 
 struct LatView {
     LatticeHeader* hdr;
@@ -74,9 +95,6 @@ struct LatView {
     uint16_t* first_lid;
     int* staged_vid;
     int2* nbr;
-    float* vb0;
-    float* vb1;
-    uint8_t* bstate;   // [2][slots] blur bookkeeping of large lattices
 };
 
 struct ScrView {
@@ -86,8 +104,6 @@ struct ScrView {
     int* owner;     // [U] staged index of the owner of each staged key
     int* vid_of;    // [U] vertex id of each owner
     uint4* vkeys;
-    float* vf0;
-    float* vf1;
 };
 
 // ---------------------------------------------------------------- memory helpers
@@ -250,7 +266,38 @@ __host__ __device__ constexpr uint32_t coord_mul(int i) {
     }
 }
 
-__device__ __forceinline__ uint32_t hash_of_lin(uint32_t lin) { return fmix32(lin ^ 0x9E3779B9u); }
+// Inverse of fmix32: the xor-shifts undone in reverse order, the odd
+// multipliers replaced by their inverses mod 2^32 (Newton's iteration
+// x <- x (2 - a x), exact after five steps from x = a for odd a).
+__host__ __device__ constexpr uint32_t inv_odd(uint32_t a) {
+    uint32_t x = a;
+    for (int i = 0; i < 5; ++i) x *= 2u - a * x;
+    return x;
+}
+static_assert(0x85EBCA6Bu * inv_odd(0x85EBCA6Bu) == 1u && 0xC2B2AE35u * inv_odd(0xC2B2AE35u) == 1u,
+              "modular inverses of the avalanche multipliers");
+
+__host__ __device__ __forceinline__ uint32_t fmix32_inv(uint32_t h) {
+    h ^= h >> 16;
+    h *= inv_odd(0xC2B2AE35u);
+    h ^= (h >> 13) ^ (h >> 26);
+    h *= inv_odd(0x85EBCA6Bu);
+    h ^= h >> 16;
+    return h;
+}
+
+// The stored hash of a key: the avalanche of its linear part plus the image's
+// salt (image index times an odd constant).  Keys of different images with
+// equal coordinates therefore differ in their hash word (fmix32 is a
+// bijection and the salts differ mod 2^32), and every key comparison, which
+// includes the hash word, keeps the images of a batch apart.  The linear part
+// (with the salt) is recovered from the hash by the inverse avalanche, so a
+// neighbour's hash follows from the vertex's stored hash alone.
+constexpr uint32_t kHashSalt = 0x9E3779B9u;
+constexpr uint32_t kImageMul = 0x61C88647u;   // odd
+__device__ __forceinline__ uint32_t hash_of_lin(uint32_t lin) { return fmix32(lin ^ kHashSalt); }
+__device__ __forceinline__ uint32_t lin_of_hash(uint32_t h) { return fmix32_inv(h) ^ kHashSalt; }
+__device__ __forceinline__ uint32_t image_salt(int img) { return (uint32_t)img * kImageMul; }
 
 // coordinate i (sign-extended int16) of a packed key record
 __device__ __forceinline__ int key_coord(const uint32_t* kw, int i) {
@@ -389,7 +436,7 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
 // g[i] + c, minus K where rank[i] > PD - c, stored as int16 halfword i of
 // words 1..; word 0 receives the hash.
 template <int PD>
-__device__ __forceinline__ void make_key(const int (&g)[PD + 1], const int (&rank)[PD + 1], int c,
+__device__ __forceinline__ void make_key(const int (&g)[PD + 1], const int (&rank)[PD + 1], int c, uint32_t salt,
                                          uint32_t (&kw)[Cfg<PD>::NW]) {
     constexpr int NW = Cfg<PD>::NW;
 #pragma unroll
@@ -399,7 +446,7 @@ __device__ __forceinline__ void make_key(const int (&g)[PD + 1], const int (&ran
         const int v = g[i] + c - ((rank[i] > PD - c) ? (PD + 1) : 0);
         kw[1 + i / 2] |= ((uint32_t)(uint16_t)(int16_t)v) << (16 * (i & 1));   // int16 wrap-around
     }
-    kw[0] = hash_of_lin(key_lin_words<PD>(kw));
+    kw[0] = hash_of_lin(key_lin_words<PD>(kw) + salt);
 }
 
 // ---------------------------------------------------------------- warp helpers
@@ -477,7 +524,7 @@ __host__ __device__ constexpr int tile_build_ctas_per_sm() {
 template <int PD>
 __global__ void __launch_bounds__(Cfg<PD>::P, tile_build_ctas_per_sm<PD>())
 k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L, ScrView S,
-             float* zero_f, int cpf, float* zero_b, int cpb) {
+             float* zero_f, int cpf) {
     using C = Cfg<PD>;
     constexpr int K = C::K, P = C::P, CW = C::CW, NW = C::NW, SLOTS = C::SLOTS, SC = C::SC;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -488,10 +535,12 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
 
     const int t = threadIdx.x, lane = t & 31;
     const int tile = blockIdx.x;
-    const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
-    const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
+    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
+    const int x = tp.x0 + (t % C::TW);
+    const int y = tp.y0 + (t / C::TW);
     const bool active = x < geo.w && y < geo.h;
-    const size_t p = (size_t)y * geo.w + x;
+    const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
+    const uint32_t salt = image_salt(tp.img);
 
     if (t == 0) s_count = 0;
 
@@ -509,7 +558,7 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
 #pragma unroll
     for (int c = 0; c < K; ++c) {
         uint32_t kw[NW];
-        make_key<PD>(g, rank, c, kw);
+        make_key<PD>(g, rank, c, salt, kw);
         if (active) {
 #pragma unroll
             for (int w = 0; w < CW; ++w)
@@ -653,8 +702,7 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
         reinterpret_cast<uint4*>(gord)[i] = reinterpret_cast<const uint4*>(ord)[i];
     for (int i = t; 16 * i < 4 * total; i += P)
         reinterpret_cast<float4*>(gws)[i] = reinterpret_cast<const float4*>(wsort)[i];
-    if (zero_f) zero_rows_block<P>(zero_f + (size_t)base * cpf, U * cpf, cpf % 4 == 0);
-    zero_rows_block<P>(zero_b + (size_t)base * cpb, U * cpb, cpb % 4 == 0);
+    zero_rows_block<P>(zero_f + (size_t)base * cpf, U * cpf, cpf % 4 == 0);
 }
 
 // ---------------------------------------------------------------- K_clear
@@ -912,12 +960,13 @@ __device__ __forceinline__ void neighbour_pair(const ScrView& S, const LatView& 
         const uint32_t d = axis_lin_step<PD>(c);
         hp = hash_of_lin(lin + d);
         hm = hash_of_lin(lin - d);
-    } else {
+    } else {   // linear parts from the words, plus the vertex's image salt
+        const uint32_t salt = lin - key_lin_words<PD>(key);
         uint32_t kw[NW];
         neighbour_key<PD>(key, c, 1, 0u, kw);
-        hp = hash_of_lin(key_lin_words<PD>(kw));
+        hp = hash_of_lin(key_lin_words<PD>(kw) + salt);
         neighbour_key<PD>(key, c, -1, 0u, kw);
-        hm = hash_of_lin(key_lin_words<PD>(kw));
+        hm = hash_of_lin(key_lin_words<PD>(kw) + salt);
     }
     const uint32_t pa = hp & mask, pb = hm & mask;
     // a cell reads as empty when the key is already known to be absent or the filter rules it out
@@ -941,7 +990,7 @@ __device__ __forceinline__ void load_vertex_key(const ScrView& S, int v, uint32_
         const uint4 r = __ldcs(S.vkeys + (size_t)v * CW + w);
         key[4 * w] = r.x; key[4 * w + 1] = r.y; key[4 * w + 2] = r.z; key[4 * w + 3] = r.w;
     }
-    lin = key_lin_words<PD>(key);
+    lin = lin_of_hash(key[0]);   // linear part plus the image's salt
     edge = false;
 #pragma unroll
     for (int i = 0; i < PD; ++i) {
@@ -1100,7 +1149,8 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
     __shared__ float4 pv[P * NV4];               // per-pixel values, padded to float4
     const int t = threadIdx.x, tile = blockIdx.x;
     if (tile == 0 && t == 0) L.hdr->bar_count = 0u;   // grid barrier of the blur that follows
-    const int x0 = (tile % geo.tiles_x) * C::TW, y0 = (tile / geo.tiles_x) * C::TH;
+    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
+    const int x0 = tp.x0, y0 = tp.y0;
     const int nx = min(C::TW, geo.w - x0), ny = min(C::TH, geo.h - y0);
     const int total = nx * ny * K;
     // my K sorted positions: entries and weights straight into registers
@@ -1138,7 +1188,7 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
     {   // this pixel's values
         const int x = x0 + (t % C::TW), y = y0 + (t / C::TW);
         const bool active = x < geo.w && y < geo.h;
-        const size_t p = (size_t)y * geo.w + x;
+        const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
         float wp = 1.0f;
         if constexpr (!FWD) wp = active ? __ldg(wt + p) : 0.0f;
         float r[4 * NV4];
@@ -1474,8 +1524,8 @@ constexpr int kBlurHalf = 1;     // flags of k_blur_all: bfloat16 rows in the st
 constexpr int kBlurStream = 2;   // the streaming passes whatever the lattice's size (tests)
 
 template <int PD, int CP>
-__global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, int reverse,
-                                                             int* final_flag, int flags) {
+__global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, uint8_t* bstate,
+                                                             int reverse, int* final_flag, int flags) {
     constexpr int K = PD + 1;
     constexpr int R = CP <= 2 ? 2 : 1;        // vertices per thread kept in registers
     constexpr int W = CP < 4 ? CP : 4;         // channels per group (the stencil is per channel)
@@ -1539,9 +1589,21 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
         return;
     }
     if (flags & kBlurHalf)
-        blur_streaming<PD, CP, true>(L.nbr, L.bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
+        blur_streaming<PD, CP, true>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
     else
-        blur_streaming<PD, CP, false>(L.nbr, L.bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
+        blur_streaming<PD, CP, false>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
+}
+
+// ---------------------------------------------------------------- status
+
+// The last kernel of a call copies the lattice's status word, with the
+// call's sequence number, to the call's slot of the host-mapped status ring
+// (one thread; every earlier kernel of the call has finished, stream order).
+__device__ __forceinline__ void report_status(unsigned long long* slot, unsigned seq, const LatticeHeader* hdr) {
+    if (slot && blockIdx.x == 0 && threadIdx.x == 0) {
+        const unsigned st = (unsigned)*reinterpret_cast<const volatile int*>(&hdr->status);
+        *reinterpret_cast<volatile unsigned long long*>(slot) = ((unsigned long long)seq << 32) | st;
+    }
 }
 
 // ---------------------------------------------------------------- slice
@@ -1554,15 +1616,17 @@ constexpr int kSlicePix = 1;   // pixels per thread in k_slice
 template <int PD, int V, bool FWD>
 __global__ void __launch_bounds__(Cfg<PD>::P / kSlicePix)
 k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
-        const float* __restrict__ lat1) {
+        const float* __restrict__ lat1, unsigned long long* st_slot, unsigned st_seq) {
     using C = Cfg<PD>;
+    report_status(st_slot, st_seq, L.hdr);
     const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
     constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS, R = kSlicePix, T = P / R;
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
     __shared__ int svid[SLOTS];
     const int t = threadIdx.x, tile = blockIdx.x;
-    const int x0 = (tile % geo.tiles_x) * C::TW, y0 = (tile / geo.tiles_x) * C::TH;
+    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
+    const int x0 = tp.x0, y0 = tp.y0;
     // pixels t and t + T of the tile; all slot loads issued before any use
     bool act[R];
     int lid[R][K];
@@ -1602,7 +1666,7 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
     for (int r = 0; r < R; ++r) {
         if (!act[r]) continue;
         const int pi = t + r * T;
-        const size_t p = (size_t)(y0 + pi / C::TW) * geo.w + x0 + (pi % C::TW);
+        const size_t p = (size_t)(tp.pix0 + (long long)(pi / C::TW) * geo.w + (pi % C::TW));
         if constexpr (FWD) {
             const float inv = 1.0f / acc[r][V];
 #pragma unroll
@@ -1648,8 +1712,9 @@ __global__ void __launch_bounds__(Cfg<PD>::P)
 k_fgrad(float* __restrict__ gfeat, const float* __restrict__ feat, const float* __restrict__ vals,
         const float* __restrict__ grad, const float* __restrict__ outp, const float* __restrict__ winv, Geo geo,
         EmbedConsts ec, LatView L, const float* R0, const float* R1, const float* H0, const float* H1,
-        const int* flags) {
+        const int* flags, unsigned long long* st_slot, unsigned st_seq) {
     using C = Cfg<PD>;
+    report_status(st_slot, st_seq, L.hdr);
     constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
     constexpr int CP = pad_ch(V + 1);
     __shared__ int svid[SLOTS];
@@ -1657,10 +1722,11 @@ k_fgrad(float* __restrict__ gfeat, const float* __restrict__ feat, const float* 
     const float* __restrict__ R = flags[0] ? R1 : R0;
     const float* __restrict__ H = flags[1] ? H1 : H0;
     const int t = threadIdx.x, tile = blockIdx.x;
-    const int x = (tile % geo.tiles_x) * C::TW + (t % C::TW);
-    const int y = (tile / geo.tiles_x) * C::TH + (t / C::TW);
+    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
+    const int x = tp.x0 + (t % C::TW);
+    const int y = tp.y0 + (t / C::TW);
     const bool act = x < geo.w && y < geo.h;
-    const size_t p = (size_t)y * geo.w + x;
+    const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
     const size_t so = (size_t)tile * K * P + t;
     int lid[K];
     float w[K];

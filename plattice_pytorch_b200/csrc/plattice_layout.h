@@ -1,12 +1,17 @@
 // plattice_layout.h -- host+device description of the lattice and scratch
 // buffers used by the sm_100a permutohedral-lattice filter.
 //
-// Geometry.  The image (h x w pixels, n = h*w) is cut into tiles of P pixels
-// (32 wide, P/32 high).  One CTA owns one tile in every per-pixel kernel, so
-// each tile's distinct lattice vertices (at most P*K, K = pd+1) can be
-// deduplicated in shared memory and addressed by a 16-bit local id.
+// Geometry.  A call filters b images of h x w pixels (b = 1 for the
+// single-image entry points).  Each image is cut into tiles of P pixels (32
+// wide, P/32 high); the tiles of all images are numbered image by image.  One
+// CTA owns one tile in every per-pixel kernel, so each tile's distinct lattice
+// vertices (at most P*K, K = pd+1) can be deduplicated in shared memory and
+// addressed by a 16-bit local id.  The b images share one lattice: the key
+// hash mixes in the image index, so equal coordinates in two images are two
+// different vertices (see hash_of_key in plattice_kernels.cuh), and every
+// stage runs once over all images.
 //
-// Lattice blob (kept from forward to backward):
+// Lattice blob (kept from forward to backward; independent of vd):
 //   hdr            LatticeHeader (status word, vertex count m, staged count)
 //   tile_off/cnt   per tile: offset and length of its unique-vertex list
 //   slot_lid       [tile][K][P] uint16   local id of each (pixel, simplex corner)
@@ -19,19 +24,23 @@
 //                                        first position of splat thread t)
 //   staged_vid     [U]          int32    global vertex id of each staged key
 //   nbr            [K][m]       int2     blur neighbours (+, -) per axis, -1 absent
-//   vb0, vb1       [m][CPb]     float    backward lattice values (ping-pong)
+// Scratch blob: a front part that every call uses -- the lattice value rows
+// of its blur and their bookkeeping -- and a build part that only a call
+// which builds the lattice uses:
+//   v0, v1         [m][CPr]     float    lattice values, ping-pong (CPr = pad(vd+1)
+//                                        rows; a backward uses pad(vd) of each)
 //   bstate         [2][slots]   uint8    blur bookkeeping of large lattices: per
 //                                        vertex, the buffer holding its row and
 //                                        its pending halvings (ping-pong)
-// Scratch blob (forward build only):
+//   -- build part --
 //   staged_keys    [U][CW]      uint4    each tile's unique keys (word 0: hash)
 //   table          [cap]        uint32   open-addressed hash table: 0 empty, else
 //                                        1 + staged index of the owning key in the
 //                                        low bits, hash bits above (a tag)
+//   filter         [cap]        uint8    miss filter of large tables
 //   owner          [U]          int32    staged index of the owner of each staged key
 //   vid_of         [U]          int32    vertex id of each owner
 //   vkeys          [m][CW]      uint4    key of every vertex
-//   vf0, vf1       [m][CPf]     float    forward lattice values (ping-pong)
 // U, m <= slots = tiles*K*P: buffers are sized for that bound, but every kernel
 // reads the live counts from the header and touches only what is used.
 #pragma once
@@ -44,7 +53,7 @@
 // status bits (LatticeHeader::status)
 #define PL_ST_SMEM_PROBE 1   /* tile-local table exhausted (cannot happen: sized 2x) */
 #define PL_ST_TABLE_FULL 2   /* global hash table probe limit reached */
-#define PL_ST_SPIN 4         /* a bounded wait (tile-local insert, grid barrier) gave up */
+#define PL_ST_SPIN 4         /* a bounded wait (grid barrier) gave up */
 #define PL_ST_ROUNDS 8       /* global insert did not settle within the round limit */
 
 typedef struct {
@@ -66,22 +75,26 @@ static inline int pl_pad_ch(int c) { return c <= 2 ? c : ((c + 3) / 4) * 4; }
 static inline size_t pl_align(size_t x) { return (x + 255) & ~(size_t)255; }
 
 typedef struct {
-    int h, w, pd, vd, K, P, TH, tiles_x, tiles_y, tiles;
+    int b, h, w, pd, vd, K, P, TH, tiles_x, tiles_y, tiles_img, tiles;
     int CW, CPf, CPb;
+    long long n_img;      /* pixels per image */
     long long slots;      /* tiles*K*P: bound on staged keys and on vertices */
     int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
     size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_slot_wsort, off_first_lid,
-        off_staged_vid, off_nbr, off_vb0, off_vb1, off_bstate, lattice_bytes;
-    size_t off_skeys, off_table, off_filter, off_owner, off_vid_of, off_vkeys, off_vf0, off_vf1, scratch_bytes;
+        off_staged_vid, off_nbr, lattice_bytes;
+    size_t off_v0, off_v1, off_bstate, rows_bytes;   /* scratch front part */
+    size_t off_skeys, off_table, off_filter, off_owner, off_vid_of, off_vkeys, scratch_bytes;
 } PlLayout;
 
-static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
-    L->h = h; L->w = w; L->pd = pd; L->vd = vd; L->K = pd + 1;
+static inline void pl_layout_batch(PlLayout* L, int b, int h, int w, int pd, int vd) {
+    L->b = b; L->h = h; L->w = w; L->pd = pd; L->vd = vd; L->K = pd + 1;
     L->P = pl_tile_pixels(pd);
     L->TH = L->P / 32;
     L->tiles_x = (w + 31) / 32;
     L->tiles_y = (h + L->TH - 1) / L->TH;
-    L->tiles = L->tiles_x * L->tiles_y;
+    L->tiles_img = L->tiles_x * L->tiles_y;
+    L->tiles = L->tiles_img * b;
+    L->n_img = (long long)h * w;
     L->CW = pl_key_words(pd);
     L->CPf = pl_pad_ch(vd + 1);
     L->CPb = pl_pad_ch(vd);
@@ -100,18 +113,19 @@ static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) {
     L->off_first_lid = o;  o = pl_align(o + T * (size_t)L->P * 2);
     L->off_staged_vid = o; o = pl_align(o + S * 4);
     L->off_nbr = o;        o = pl_align(o + S * L->K * 8);
-    L->off_vb0 = o;        o = pl_align(o + S * L->CPb * 4);
-    L->off_vb1 = o;        o = pl_align(o + S * L->CPb * 4);
-    L->off_bstate = o;     o = pl_align(o + 2 * S);
     L->lattice_bytes = o;
     o = 0;
+    L->off_v0 = o;         o = pl_align(o + S * L->CPf * 4);
+    L->off_v1 = o;         o = pl_align(o + S * L->CPf * 4);
+    L->off_bstate = o;     o = pl_align(o + 2 * S);
+    L->rows_bytes = o;
     L->off_skeys = o;      o = pl_align(o + S * L->CW * 16);
     L->off_table = o;      o = pl_align(o + ((size_t)1 << lg) * 4);
     L->off_filter = o;     o = pl_align(o + ((size_t)1 << lg));
     L->off_owner = o;      o = pl_align(o + S * 4);
     L->off_vid_of = o;     o = pl_align(o + S * 4);
     L->off_vkeys = o;      o = pl_align(o + S * L->CW * 16);
-    L->off_vf0 = o;        o = pl_align(o + S * L->CPf * 4);
-    L->off_vf1 = o;        o = pl_align(o + S * L->CPf * 4);
     L->scratch_bytes = o;
 }
+
+static inline void pl_layout(PlLayout* L, int h, int w, int pd, int vd) { pl_layout_batch(L, 1, h, w, pd, vd); }

@@ -16,10 +16,10 @@
 // process exits.  An image whose workspace does not fit is rejected.
 //
 // Host code cannot use the array's name as a device address (it only names a
-// host-side shadow of the symbol), so the first call on each device, with
-// that device current, asks the runtime for the array's device address
-// (cudaGetSymbolAddress) and keeps it.  Make that first call on a device
-// before any stream capture begins.
+// host-side shadow of the symbol), so the first call in each CUDA context,
+// with that context current, asks the runtime for the array's device address
+// (cudaGetSymbolAddress) and keeps it for that context.  Make that first call
+// -- or plattice_prepare -- before any stream capture begins.
 //
 // All calls on a device share the one array and it keeps whatever the last
 // call left in it; the filter clears every part it needs to start at zero.
@@ -28,19 +28,33 @@
 #include <cuda_runtime.h>
 #include <stdio.h>
 
-#include <mutex>
-
 #include "../../include/plattice.h"
 #include "plattice_layout.h"
+#include "plattice_runtime.h"
 
 #define PL_NOALLOC_BYTES (64ull << 20)
 
 static __device__ __align__(256) unsigned char g_noalloc_arena[PL_NOALLOC_BYTES];
 
+namespace pl {
+int forward_images(float* weight_out, float* out, const float* values, const float* features, void* lattice,
+                   size_t lattice_bytes, void* scratch, size_t scratch_bytes, int b, int pd, int vd, int w,
+                   int h, void* stream, bool track, const char* call);
+}
+
 namespace {
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
 thread_local char g_noalloc_err[192] = "";
+
+// the array's device address in the current context
+int arena(void** base) {
+    const cudaError_t e = pl::symbol_address(reinterpret_cast<const void*>(&g_noalloc_arena), base);
+    if (e != cudaSuccess) {
+        snprintf(g_noalloc_err, sizeof(g_noalloc_err), "device address of the fixed array: %s",
+                 cudaGetErrorName(e));
+        return PLATTICE_ERR_CUDA;
+    }
+    return PLATTICE_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -51,6 +65,7 @@ const char* plattice_noalloc_error_detail(void) { return g_noalloc_err; }
 
 int plattice_forward_noalloc(float* weight_out, float* out, const float* values, const float* features,
                              int pd, int vd, int w, int h, void* stream) {
+    g_noalloc_err[0] = '\0';
     size_t lattice_bytes = 0, scratch_bytes = 0;
     int rc = plattice_workspace_sizes(h, w, pd, vd, &lattice_bytes, &scratch_bytes);
     if (rc != PLATTICE_OK) return rc;
@@ -61,31 +76,22 @@ int plattice_forward_noalloc(float* weight_out, float* out, const float* values,
                  h, w, pd, vd, need, (unsigned long long)PL_NOALLOC_BYTES);
         return PLATTICE_ERR_WORKSPACE;
     }
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-        snprintf(g_noalloc_err, sizeof(g_noalloc_err), "no usable current CUDA device");
-        return PLATTICE_ERR_CUDA;
-    }
+    if (h == 0 || w == 0) return PLATTICE_OK;
     void* base = nullptr;
-    {
-        std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        if (!g_noalloc_ptr[dev]) {
-            void* p = nullptr;
-            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_arena);
-            if (e != cudaSuccess || !p) {
-                snprintf(g_noalloc_err, sizeof(g_noalloc_err), "cudaGetSymbolAddress failed: %s",
-                         cudaGetErrorName(e));
-                return PLATTICE_ERR_CUDA;
-            }
-            g_noalloc_ptr[dev] = p;
-        }
-        base = g_noalloc_ptr[dev];
-    }
+    rc = arena(&base);
+    if (rc != PLATTICE_OK) return rc;
     unsigned char* lattice = static_cast<unsigned char*>(base);
     unsigned char* scratch = lattice + pl_align(lattice_bytes);
-    g_noalloc_err[0] = '\0';
-    return plattice_forward(weight_out, out, values, features, lattice, lattice_bytes, scratch, scratch_bytes,
-                            pd, vd, w, h, stream);
+    // no status ticket: the ring's pinned host memory would be an allocation
+    return pl::forward_images(weight_out, out, values, features, lattice, lattice_bytes, scratch, scratch_bytes,
+                              1, pd, vd, w, h, stream, false, "plattice_forward_noalloc");
+}
+
+int plattice_noalloc_status(int* status, int* m, void* stream) {
+    void* base = nullptr;
+    const int rc = arena(&base);
+    if (rc != PLATTICE_OK) return rc;
+    return plattice_lattice_info(base, status, m, nullptr, nullptr, stream);
 }
 
 }  // extern "C"

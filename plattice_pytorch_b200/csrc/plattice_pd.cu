@@ -12,6 +12,7 @@ template cudaError_t run_forward<PL_PD>(const CallArgs&);
 template cudaError_t run_backward<PL_PD>(const CallArgs&);
 template cudaError_t run_filter<PL_PD>(const CallArgs&);
 template cudaError_t run_feature_grad<PL_PD>(const CallArgs&);
+template cudaError_t run_prepare<PL_PD>(const CallArgs&);
 template cudaError_t run_export_keys<PL_PD>(const void*, const void*, const PlLayout&, int16_t*, int,
                                            cudaStream_t);
 }  // namespace pl

@@ -1,0 +1,58 @@
+// plattice_runtime.h -- host-side state of the library that belongs to a CUDA
+// context: the side stream of the neighbour lookups, one-time kernel
+// attribute settings, the fixed array of the no-allocation entry point, and
+// the ring of per-call device status words that reports device-side failures
+// (table full, a bounded wait that gave up) on a later call without
+// synchronising.
+//
+// Everything cached is keyed by the calling thread's current CUDA context,
+// identified by its unique id (cuCtxGetId: never reused, also not after
+// cudaDeviceReset re-creates the primary context), so that a caller running
+// in its own context (cuCtxCreate) or after a device reset gets state created
+// in that context, never another context's handles or addresses.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pl {
+
+struct CtxState;
+
+// The state of the current context (created on first use).  Returns nullptr
+// and sets *err when the context cannot be determined.
+CtxState* ctx_state(cudaError_t* err);
+
+// Side stream of the context, forked from and joined back into `main` with
+// events; the fork is held by one host thread at a time (side_fork locks,
+// side_join unlocks).
+struct SideFork {
+    cudaStream_t side;
+    void* token;
+};
+cudaError_t side_fork(cudaStream_t main, SideFork* f);
+cudaError_t side_join(cudaStream_t main, SideFork* f);
+
+// Runs set_attr once per context for the kernel `fn` (a kernel attribute
+// such as the dynamic shared-memory limit) and caches an int result (e.g. the
+// resident CTAs per SM it implies).  Returns the cached value in *value.
+cudaError_t kernel_once(const void* fn, cudaError_t (*set_attr)(int* value), int* value);
+
+// Device address of a __device__ symbol in the current context (looked up
+// with cudaGetSymbolAddress once per context and symbol).
+cudaError_t symbol_address(const void* symbol, void** addr);
+
+// Status ring.  A call that enqueues work takes a ticket: a slot of pinned,
+// mapped host memory and a sequence number.  The call's last kernel stores
+// (sequence << 32) | status word there; status_poll, run at the start of every
+// call, reads the slots of earlier calls whose kernels have finished and
+// returns the first non-zero status it finds (once), with the call's name.
+struct StatusTicket {
+    unsigned long long* slot;   // device-visible address (nullptr: not tracked)
+    unsigned seq;
+};
+StatusTicket status_ticket(const char* call);
+// 0 when no finished call reported a failure; else its status bits, with the
+// call's name and sequence number in name/seq.
+int status_poll(const char** name, unsigned* seq);
+
+}  // namespace pl

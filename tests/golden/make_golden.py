@@ -2,7 +2,7 @@
 
 Two sources, two modes:
 
-``python tests/golden/make_golden.py image``
+``python tests/golden/make_golden.py image --ref <reference tree>``
     Runs where the reference tree is mounted (CPU is enough).  Takes the
     32x32 crop [48:80, 48:80] of the reference test image
     (tests/assets/test_image.png), builds its features with the reference
@@ -129,10 +129,9 @@ def run_reference(out_dir, big):
         print(f"{name}: m={lat['m']} out[{out.min().item():.4g},{out.max().item():.4g}]", flush=True)
 
 
-def run_image(out_dir):
+def run_image(out_dir, ref_root):
     import importlib.util
     from PIL import Image
-    ref_root = "/root/reference"
     spec = importlib.util.spec_from_file_location(
         "ref_test_plattice", os.path.join(ref_root, "tests", "test_plattice.py"))
     mod = importlib.util.module_from_spec(spec)
@@ -154,9 +153,12 @@ def main():
     ap.add_argument("mode", choices=["image", "reference"])
     ap.add_argument("--out", default=HERE)
     ap.add_argument("--big", action="store_true")
+    ap.add_argument("--ref", help="the reference source tree (mode image: its test module and test image)")
     a = ap.parse_args()
     if a.mode == "image":
-        run_image(a.out)
+        if not a.ref:
+            ap.error("mode image reads the reference's test files: pass --ref <reference tree>")
+        run_image(a.out, a.ref)
     else:
         run_reference(a.out, a.big)
 

@@ -53,13 +53,14 @@ def _layout(h, w, pd, vd):
     lat, o = {}, _align(256)
     for name, sz in [("tile_off", T * 4), ("tile_cnt", T * 4), ("slot_lid", S * 2), ("slot_w", S * 4),
                      ("slot_order", S * 2), ("slot_wsort", S * 4), ("first_lid", T * P * 2), ("staged_vid", S * 4),
-                     ("nbr", S * K * 8), ("vb0", S * CPb * 4), ("vb1", S * CPb * 4), ("bstate", 2 * S)]:
+                     ("nbr", S * K * 8)]:
         lat[name] = o
         o = _align(o + sz)
     lat_bytes, scr, o = o, {}, 0
-    for name, sz in [("skeys", S * CW * 16), ("table", (1 << lg) * 4), ("filter", 1 << lg), ("owner", S * 4),
-                     ("vid_of", S * 4),
-                     ("vkeys", S * CW * 16), ("vf0", S * CPf * 4), ("vf1", S * CPf * 4)]:
+    # scratch: the value rows (front part), then the build part
+    for name, sz in [("v0", S * CPf * 4), ("v1", S * CPf * 4), ("bstate", 2 * S),
+                     ("skeys", S * CW * 16), ("table", (1 << lg) * 4), ("filter", 1 << lg), ("owner", S * 4),
+                     ("vid_of", S * 4), ("vkeys", S * CW * 16)]:
         scr[name] = o
         o = _align(o + sz)
     return lat, scr, dict(K=K, P=P, TH=TH, tx=tx, T=T, CW=CW, S=S, lat_bytes=lat_bytes, scr_bytes=o)

@@ -257,26 +257,46 @@ def test_empty_image(dev):
 def test_undersized_table_reports_error(dev):
     """A hash table forced below the vertex count ends its probes at the limit
     and reports PLATTICE_DEV_TABLE_FULL through the status word (bounded
-    loops, no hang); the next call with the automatic size is correct."""
+    loops, no hang).  Without PLATTICE_CHECK the failure raises at the first
+    call after the failed call's kernels have finished (here the next call,
+    after a synchronising read); with it, the failed call itself raises.  The
+    next call with the automatic size is correct."""
     from plattice_pytorch_b200 import PLOO, _lib
     d = np.load(os.path.join(GOLDEN, "ref_blobs64_pd5_vd3.npz"))
     ft, vt = _t(d["features"], dev), _t(d["values"], dev)
     L = _lib.lib()
     check = PLOO._CHECK
+    PLOO.check_device_status()   # nothing pending from earlier tests
     try:
         L.plattice_debug_set_table_cap_log2(6)   # 64 cells for 1225 vertices
         PLOO._CHECK = False
         _, _, lat = PLOO.lattice_forward(ft, vt)
-        info = PLOO.lattice_info(lat)
-        # with per-call checking on, the same failure raises
+        info = PLOO.lattice_info(lat)            # synchronises
+        with pytest.raises(_lib.PlatticeError) as ei:
+            PLOO.lattice_forward(ft, vt)         # refused: reports the earlier failure
+        assert ei.value.status == _lib.ERR_DEVICE
+        assert "plattice_forward" in str(ei.value) and "0x2" in str(ei.value)
+        # the same through a backward that rebuilds, reported by a call of another kind
+        gt = _t(d["grad"], dev)
+        PLOO.lattice_backward(ft, gt, _t(d["weight"], dev), None)
+        torch.cuda.synchronize()
+        with pytest.raises(_lib.PlatticeError) as ei:
+            PLOO.check_device_status()
+        assert ei.value.status == _lib.ERR_DEVICE and "plattice_backward" in str(ei.value)
+        # with per-call checking on, the failing call itself raises
         PLOO._CHECK = True
         with pytest.raises(_lib.PlatticeError) as ei:
             PLOO.lattice_forward(ft, vt)
         assert ei.value.status == _lib.ERR_DEVICE
+        with pytest.raises(_lib.PlatticeError):   # ... and the ring still holds it once
+            PLOO.check_device_status()
     finally:
         L.plattice_debug_set_table_cap_log2(0)
         PLOO._CHECK = check
     assert info["status"] & _lib.DEV_TABLE_FULL
+    PLOO.check_device_status()   # reported once: nothing left
     _, out, lat = PLOO.lattice_forward(ft, vt)
     assert PLOO.lattice_info(lat)["status"] == 0
     assert allclose_report(out.cpu().numpy(), d["out"]) <= 1.0
+    torch.cuda.synchronize()
+    PLOO.check_device_status()

@@ -84,13 +84,29 @@ def test_kept_lattice_sizes_and_argument_checks(lib):
     # a rebuild needs the features
     assert lib.plattice_backward(fake, fake, fake, None, fake, lb8, 0, fake, 1 << 30, 5, 3, 8, 8,
                                  None) == _lib.ERR_INVALID
+    # every backward needs a scratch: the full one for a rebuild, the front part otherwise
+    rb8 = _lib.reuse_scratch_size(1, 8, 8, 5, 3)
+    _, sb8 = _lib.workspace_sizes(8, 8, 5, 3)
+    assert rb8 < sb8
+    assert lib.plattice_backward(fake, fake, fake, None, fake, lb8, 1, None, 0, 5, 3, 8, 8,
+                                 None) == _lib.ERR_INVALID
+    assert lib.plattice_backward(fake, fake, fake, None, fake, lb8, 1, fake, rb8 - 1, 5, 3, 8, 8,
+                                 None) == _lib.ERR_WORKSPACE
+    assert lib.plattice_backward(fake, fake, fake, fake, fake, lb8, 0, fake, rb8, 5, 3, 8, 8,
+                                 None) == _lib.ERR_WORKSPACE
+    # the lattice does not depend on vd
+    assert _lib.workspace_sizes(8, 8, 5, 1)[0] == lb8 == _lib.workspace_sizes(8, 8, 5, 8)[0]
 
 
 def test_batch_sizes_and_argument_checks(lib):
     from plattice_pytorch_b200 import _lib
     lb, sb = _lib.workspace_sizes(512, 512, 5, 3)
     blb, bsb = _lib.batch_workspace_sizes(64, 512, 512, 5, 3)
-    assert blb == 64 * ((lb + 255) // 256 * 256) and bsb == sb   # lattices kept per image, scratch shared
+    # one lattice for the batch: every array scales with the images, only the
+    # header and the 256-byte padding of each array do not
+    assert 64 * lb - 64 * 4096 <= blb <= 64 * lb
+    assert bsb >= 64 * _lib.reuse_scratch_size(1, 512, 512, 5, 3)
+    assert _lib.reuse_scratch_size(64, 512, 512, 5, 3) < bsb
     with pytest.raises(_lib.PlatticeError):
         _lib.batch_workspace_sizes(-1, 8, 8, 5, 3)
     fake = ctypes.c_void_p(256)
