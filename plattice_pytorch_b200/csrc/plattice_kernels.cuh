@@ -1016,19 +1016,28 @@ constexpr int kNbrThreads = 256;
 // remaining (vertex, axis) pairs of the warp go to a queue in shared memory
 // (with the vertices' keys) and the warp's lanes take them one each, so that
 // the full probe and key compare run with every lane busy.
+// Per-warp shared memory of the sparse path's queue.
 template <int PD>
-__global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo geo, LatView L, ScrView S) {
+struct NbrWarpSmem {
+    uint32_t key[Cfg<PD>::NW][32];
+    uint32_t lin[32];
+    unsigned long long side[32];   // bits 2c, 2c+1: the + / - lookup of axis c may hit
+    uint16_t q[32 * (PD + 1)];     // (lane << 5) | axis
+};
+
+// The neighbour lookups of all vertices by the threads gtid = 0..nthreads-1
+// of a grid (whole warps); `wsm` is this warp's queue memory.
+template <int PD>
+__device__ __forceinline__ void neighbors_grid(const Geo& geo, const LatView& L, const ScrView& S, int gtid,
+                                               int nthreads, NbrWarpSmem<PD>* wsm) {
     constexpr int K = PD + 1, NW = Cfg<PD>::NW;
-    constexpr int WARPS = kNbrThreads / 32;
     const int M = L.hdr->m;
     if (M <= 0) return;
     const uint32_t mask = (1u << L.hdr->cap_log2) - 1u;
     const bool use_filter = L.hdr->cap_log2 >= geo.filter_min_log2;
     const TableFmt f = table_fmt(geo);
-    const int nthreads = gridDim.x * blockDim.x;
     int G = (nthreads + M - 1) / M;   // axis groups
     G = G < 1 ? 1 : (G > K ? K : G);
-    const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
     if (!(use_filter && G == 1)) {   // dense (uniform over the grid)
         const size_t total = (size_t)M * G;
         for (size_t idx = gtid; idx < total; idx += nthreads) {
@@ -1041,11 +1050,7 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
         }
         return;
     }
-    __shared__ uint32_t s_key[WARPS][NW][32];
-    __shared__ uint32_t s_lin[WARPS][32];
-    __shared__ unsigned long long s_side[WARPS][32];   // bits 2c, 2c+1: the + / - lookup of axis c may hit
-    __shared__ uint16_t s_q[WARPS][32 * K];   // (lane << 5) | axis
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int lane = gtid & 31;
     for (int wb = gtid - lane; wb < M; wb += nthreads) {   // warp-uniform
         const int v = wb + lane;
         uint32_t pend = 0u;   // my axes still to look up, one bit each
@@ -1075,9 +1080,9 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
                 }
             }
 #pragma unroll
-            for (int k = 0; k < NW; ++k) s_key[wid][k][lane] = key[k];
-            s_lin[wid][lane] = lin;
-            s_side[wid][lane] = side;
+            for (int k = 0; k < NW; ++k) wsm->key[k][lane] = key[k];
+            wsm->lin[lane] = lin;
+            wsm->side[lane] = side;
         }
         // my queue entries after those of the lanes below me
         const int cnt = __popc(pend);
@@ -1089,14 +1094,14 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
         }
         const int qtotal = __shfl_sync(kFull, pre, 31);
         pre -= cnt;
-        for (uint32_t m = pend; m != 0u; m &= m - 1u) s_q[wid][pre++] = (uint16_t)((lane << 5) | (__ffs(m) - 1));
+        for (uint32_t m = pend; m != 0u; m &= m - 1u) wsm->q[pre++] = (uint16_t)((lane << 5) | (__ffs(m) - 1));
         __syncwarp();
         for (int j = lane; j < qtotal; j += 32) {
-            const int e = s_q[wid][j];
+            const int e = wsm->q[j];
             const int src = e >> 5, c = e & 31;
             uint32_t key[NW];
 #pragma unroll
-            for (int k = 0; k < NW; ++k) key[k] = s_key[wid][k][src];
+            for (int k = 0; k < NW; ++k) key[k] = wsm->key[k][src];
             bool edge = false;
 #pragma unroll
             for (int i = 0; i < PD; ++i) {
@@ -1105,12 +1110,19 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
             }
             // a lookup the first sweep ruled out (filter bit clear or home cell
             // empty) reads nothing; the other reads its home cell again
-            const unsigned sd = (unsigned)(s_side[wid][src] >> (2 * c)) & 3u;
-            neighbour_pair<PD>(S, L, mask, f, false, key, s_lin[wid][src], edge, wb + src, M, c, (sd & 1u) != 0u,
+            const unsigned sd = (unsigned)(wsm->side[src] >> (2 * c)) & 3u;
+            neighbour_pair<PD>(S, L, mask, f, false, key, wsm->lin[src], edge, wb + src, M, c, (sd & 1u) != 0u,
                                (sd & 2u) != 0u);
         }
         __syncwarp();   // the queue is refilled by the next step
     }
+}
+
+template <int PD>
+__global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo geo, LatView L, ScrView S) {
+    __shared__ NbrWarpSmem<PD> wsm[kNbrThreads / 32];
+    neighbors_grid<PD>(geo, L, S, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x,
+                       &wsm[threadIdx.x >> 5]);
 }
 
 // ---------------------------------------------------------------- splat
@@ -1136,19 +1148,38 @@ __device__ __forceinline__ void red_run(float* lat, int vid, const float (&s)[NC
     red_add_row<CP>(lat + (size_t)vid * CP, r);
 }
 
-template <int PD, int V, bool FWD>
-__global__ void __launch_bounds__(Cfg<PD>::P)
-k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, ScrView S,
-        int resolve, float* lat) {
+// Shared memory of one tile worker of the splat: the tile's vertex ids and
+// the per-pixel value rows.
+template <int PD, int NC>
+struct SplatSmem {
+    int svid[Cfg<PD>::SLOTS];
+    float4 pv[Cfg<PD>::P * ((NC + 3) / 4)];
+};
+
+// Synchronisation of the P threads that work on one tile: the whole CTA
+// (one tile per CTA) or a named barrier of a tile worker inside a larger CTA.
+struct CtaSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+struct WorkerSync {
+    int id, n;   // barrier id (1..15) and thread count
+    __device__ __forceinline__ void operator()() const {
+        asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+    }
+};
+
+template <int PD, int V, bool FWD, typename Sync>
+__device__ __forceinline__ void splat_tile(int tile, int t, const float* __restrict__ vals,
+                                           const float* __restrict__ wt, const Geo& geo, const LatView& L,
+                                           const ScrView& S, int resolve, float* lat,
+                                           SplatSmem<PD, FWD ? V + 1 : V>& sm, Sync sync) {
     using C = Cfg<PD>;
     constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
     constexpr int NV4 = (NC + 3) / 4;            // float4 per pixel value row
-    __shared__ int svid[SLOTS];
-    __shared__ float4 pv[P * NV4];               // per-pixel values, padded to float4
-    const int t = threadIdx.x, tile = blockIdx.x;
-    if (tile == 0 && t == 0) L.hdr->bar_count = 0u;   // grid barrier of the blur that follows
+    int* svid = sm.svid;
+    float4* pv = sm.pv;
     const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
     const int x0 = tp.x0, y0 = tp.y0;
     const int nx = min(C::TW, geo.w - x0), ny = min(C::TH, geo.h - y0);
@@ -1218,7 +1249,7 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
         }
         svid[u] = vid;
     }
-    __syncthreads();
+    sync();
     // my pieces: the first (it may continue the previous lane's run), complete
     // runs in between (added at once), and the last (it may continue into the
     // next lane); the first and last are the same piece when no run starts
@@ -1275,15 +1306,26 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
 #pragma unroll
     for (int j = 0; j < NC; ++j) prev[j] = __shfl_up_sync(kFull, cur[j], 1);
     const bool next_cont = __shfl_down_sync(kFull, cont ? 1 : 0, 1) != 0;
-    if (nq == 0) return;
-    if (multi) {   // my first piece closes a run: add what the lanes before me carried
-        if (cont) {
+    if (nq > 0) {
+        if (multi) {   // my first piece closes a run: add what the lanes before me carried
+            if (cont) {
 #pragma unroll
-            for (int j = 0; j < NC; ++j) head[j] = __fadd_rn(head[j], prev[j]);
+                for (int j = 0; j < NC; ++j) head[j] = __fadd_rn(head[j], prev[j]);
+            }
+            if (svid[first] >= 0) red_run<CP, NC>(lat, svid[first], head);
         }
-        if (svid[first] >= 0) red_run<CP, NC>(lat, svid[first], head);
+        if ((lane == 31 || !next_cont) && svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
     }
-    if ((lane == 31 || !next_cont) && svid[l] >= 0) red_run<CP, NC>(lat, svid[l], cur);
+    sync();   // svid / pv are reused by the worker's next tile
+}
+
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(Cfg<PD>::P)
+k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, ScrView S,
+        int resolve, float* lat) {
+    __shared__ SplatSmem<PD, FWD ? V + 1 : V> sm;
+    if (blockIdx.x == 0 && threadIdx.x == 0) L.hdr->bar_count = 0u;   // grid barrier of the blur that follows
+    splat_tile<PD, V, FWD>(blockIdx.x, threadIdx.x, vals, wt, geo, L, S, resolve, lat, sm, CtaSync{});
 }
 
 // ---------------------------------------------------------------- blur
@@ -1318,6 +1360,27 @@ __device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase
         }
     }
     __syncthreads();
+}
+
+// At the end of a kernel with grid barriers: the last CTA to leave resets
+// the barrier counter (and this exit counter) for the next launch on the
+// lattice, and reports the status word of the call when `slot` is set.  Every
+// CTA has passed its last barrier by then.
+__device__ __forceinline__ void grid_exit(LatticeHeader* hdr, unsigned long long* slot, unsigned seq) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&hdr->bar_gen, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence();
+            if (slot) {
+                const unsigned st = (unsigned)atomicOr(&hdr->status, 0);
+                *reinterpret_cast<volatile unsigned long long*>(slot) = ((unsigned long long)seq << 32) | st;
+            }
+            atomicExch(&hdr->bar_count, 0u);
+            atomicExch(&hdr->bar_gen, 0u);
+        }
+    }
 }
 
 // r *= 2^-e (exact: a power of two, far from the float range limits here)
@@ -1367,8 +1430,9 @@ struct BlurIdx {
     int2 ta, tb;   // first-axis neighbours of t.x and of t.y
 };
 
+// (through L2: in the fused filter kernel the table was written in the same launch)
 __device__ __forceinline__ int2 nbr_at(const int2* nbr, int M, int axis, int v) {
-    return v >= 0 ? __ldg(nbr + (size_t)axis * M + v) : make_int2(-1, -1);
+    return v >= 0 ? __ldcg(nbr + (size_t)axis * M + v) : make_int2(-1, -1);
 }
 
 __device__ __forceinline__ BlurIdx blur_idx(const int2* nbr, int M, int v, int ax_s, int ax_t) {
@@ -1434,14 +1498,13 @@ constexpr int kBlurQueueBytes = kBlurThreads * kBlurVpt * 16;   // dynamic share
 
 template <int PD, int CP, bool HALF>
 __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, LatticeHeader* hdr, float* buf0,
-                                            float* buf1, int reverse, int* final_flag, int M, int tid, int stride) {
+                                            float* buf1, int reverse, int* final_flag, int M, int tid, int stride,
+                                            uint4* blur_queue, unsigned& phase) {
     constexpr int K = PD + 1;
     constexpr int VPT = kBlurVpt;
-    extern __shared__ uint4 blur_queue[];   // per warp: its step's vertices with neighbours
     const int lane = threadIdx.x & 31;
-    uint4* const q = blur_queue + (threadIdx.x >> 5) * (32 * VPT);
+    uint4* const q = blur_queue + (threadIdx.x >> 5) * (32 * VPT);   // per warp: its step's vertices with neighbours
     const int wbase = tid - lane;   // the warp's first vertex of a step: the loop below is warp-uniform
-    unsigned phase = 0;
     uint8_t* const st0 = bstate;
     uint8_t* const st1 = bstate + M;
     uint16_t* const h0 = reinterpret_cast<uint16_t*>(buf1);
@@ -1458,7 +1521,7 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
 #pragma unroll
             for (int k = 0; k < VPT; ++k) {
                 const int v = w0 + lane + k * stride;
-                n[k] = v < M ? __ldg(nb + v) : make_int2(-1, -1);
+                n[k] = v < M ? __ldcg(nb + v) : make_int2(-1, -1);
                 cv[k] = (s == 0 || v >= M) ? 0 : (int)__ldcg(sc + v);
             }
 #pragma unroll
@@ -1517,81 +1580,103 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
         scale_pow2<CP>(r, c & 63);
         store_row<CP>(buf0 + (size_t)v * CP, r);
     }
-    if (tid == 0) *final_flag = 0;
+    if (tid == 0 && final_flag) *final_flag = 0;
 }
 
 constexpr int kBlurHalf = 1;     // flags of k_blur_all: bfloat16 rows in the streaming passes
 constexpr int kBlurStream = 2;   // the streaming passes whatever the lattice's size (tests)
 
+// The resident blur: every vertex's row stays in a register of one thread
+// for the K passes, passes in fused pairs (one grid barrier per pair).  CTA b
+// of G owns the contiguous vertices [M b / G, M (b+1) / G) (balanced over the
+// SMs), R per thread.  Requires M <= G * blockDim * R.  Returns the buffer
+// that holds the result.
 template <int PD, int CP>
-__global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, uint8_t* bstate,
-                                                             int reverse, int* final_flag, int flags) {
+__device__ __forceinline__ float* blur_resident(const LatView& L, float* buf0, float* buf1, int reverse, int M,
+                                                unsigned& phase) {
     constexpr int K = PD + 1;
     constexpr int R = CP <= 2 ? 2 : 1;        // vertices per thread kept in registers
     constexpr int W = CP < 4 ? CP : 4;         // channels per group (the stencil is per channel)
+    const int G = gridDim.x;
+    const int vb = (int)((long long)M * blockIdx.x / G), ve = (int)((long long)M * (blockIdx.x + 1) / G);
+    float* x = buf0;
+    float* y = buf1;
+    auto axis = [&](int k) { return k >= K ? -1 : (reverse ? K - 1 - k : k); };
+    float me[R][CP];
+    BlurIdx idx[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int v = vb + threadIdx.x + r * blockDim.x;
+        if (v < ve) load_row_cg<CP>(x + (size_t)v * CP, me[r]);
+        idx[r] = blur_idx(L.nbr, M, v < ve ? v : -1, axis(0), axis(1));
+    }
+#pragma unroll 1
+    for (int k = 0; k < K; k += 2) {
+        const bool pair = k + 1 < K;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int v = vb + threadIdx.x + r * blockDim.x;
+            if (v >= ve) continue;
+            const BlurIdx& I = idx[r];
+#pragma unroll
+            for (int c0 = 0; c0 < CP; c0 += W) {
+                const float* xc = x + c0;
+                float mine[W], a[W], b[W], o[W];
+#pragma unroll
+                for (int j = 0; j < W; ++j) mine[j] = me[r][c0 + j];
+                if (I.s.x >= 0) load_row_cg<W>(xc + (size_t)I.s.x * CP, a);
+                if (I.s.y >= 0) load_row_cg<W>(xc + (size_t)I.s.y * CP, b);
+                blur_row<W>(mine, a, b, I.s, o);
+                if (pair) {
+                    float pa[W], pb[W], q[W];
+                    if (I.t.x >= 0) blur_at<W, CP>(xc, I.t.x, I.ta, pa);
+                    if (I.t.y >= 0) blur_at<W, CP>(xc, I.t.y, I.tb, pb);
+                    blur_row<W>(o, pa, pb, I.t, q);
+#pragma unroll
+                    for (int j = 0; j < W; ++j) o[j] = q[j];
+                }
+                store_row<W>(y + (size_t)v * CP + c0, o);
+#pragma unroll
+                for (int j = 0; j < W; ++j) me[r][c0 + j] = o[j];
+            }
+        }
+        float* t = x; x = y; y = t;
+        if (k + 2 < K) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int v = vb + threadIdx.x + r * blockDim.x;
+                idx[r] = blur_idx(L.nbr, M, v < ve ? v : -1, axis(k + 2), axis(k + 3));
+            }
+            grid_barrier(L.hdr, phase);
+        }
+    }
+    return x;
+}
+
+template <int CP>
+__device__ __forceinline__ bool blur_fits_resident(int M, int threads) {
+    return M <= threads * (CP <= 2 ? 2 : 1);
+}
+
+template <int PD, int CP>
+__global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf0, float* buf1, uint8_t* bstate,
+                                                             int reverse, int* final_flag, int flags) {
+    extern __shared__ uint4 blur_queue[];
     const int M = L.hdr->m;
     const int stride = gridDim.x * blockDim.x;
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned phase = 0;
-    float* x = buf0;
-    float* y = buf1;
-    if (M <= stride * R && !(flags & kBlurStream)) {
-        auto axis = [&](int k) { return k >= K ? -1 : (reverse ? K - 1 - k : k); };
-        float me[R][CP];
-        BlurIdx idx[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int v = tid + r * stride;
-            if (v < M) load_row_cg<CP>(x + (size_t)v * CP, me[r]);
-            idx[r] = blur_idx(L.nbr, M, v < M ? v : -1, axis(0), axis(1));
-        }
-#pragma unroll 1
-        for (int k = 0; k < K; k += 2) {
-            const bool pair = k + 1 < K;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int v = tid + r * stride;
-                if (v >= M) continue;
-                const BlurIdx& I = idx[r];
-#pragma unroll
-                for (int c0 = 0; c0 < CP; c0 += W) {
-                    const float* xc = x + c0;
-                    float mine[W], a[W], b[W], o[W];
-#pragma unroll
-                    for (int j = 0; j < W; ++j) mine[j] = me[r][c0 + j];
-                    if (I.s.x >= 0) load_row_cg<W>(xc + (size_t)I.s.x * CP, a);
-                    if (I.s.y >= 0) load_row_cg<W>(xc + (size_t)I.s.y * CP, b);
-                    blur_row<W>(mine, a, b, I.s, o);
-                    if (pair) {
-                        float pa[W], pb[W], q[W];
-                        if (I.t.x >= 0) blur_at<W, CP>(xc, I.t.x, I.ta, pa);
-                        if (I.t.y >= 0) blur_at<W, CP>(xc, I.t.y, I.tb, pb);
-                        blur_row<W>(o, pa, pb, I.t, q);
-#pragma unroll
-                        for (int j = 0; j < W; ++j) o[j] = q[j];
-                    }
-                    store_row<W>(y + (size_t)v * CP + c0, o);
-#pragma unroll
-                    for (int j = 0; j < W; ++j) me[r][c0 + j] = o[j];
-                }
-            }
-            float* t = x; x = y; y = t;
-            if (k + 2 < K) {
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int v = tid + r * stride;
-                    idx[r] = blur_idx(L.nbr, M, v < M ? v : -1, axis(k + 2), axis(k + 3));
-                }
-                grid_barrier(L.hdr, phase);
-            }
-        }
-        if (tid == 0) *final_flag = (x == buf1) ? 1 : 0;
-        return;
+    if (blur_fits_resident<CP>(M, stride) && !(flags & kBlurStream)) {
+        float* res = blur_resident<PD, CP>(L, buf0, buf1, reverse, M, phase);
+        if (tid == 0) *final_flag = (res == buf1) ? 1 : 0;
+    } else if (flags & kBlurHalf) {
+        blur_streaming<PD, CP, true>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride,
+                                     blur_queue, phase);
+    } else {
+        blur_streaming<PD, CP, false>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride,
+                                      blur_queue, phase);
     }
-    if (flags & kBlurHalf)
-        blur_streaming<PD, CP, true>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
-    else
-        blur_streaming<PD, CP, false>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride);
+    grid_exit(L.hdr, nullptr, 0u);
 }
 
 // ---------------------------------------------------------------- status
@@ -1610,73 +1695,156 @@ __device__ __forceinline__ void report_status(unsigned long long* slot, unsigned
 
 // FWD: out = sum_i w_i val_i[0:V] / sum_i w_i val_i[V], weight_out = 1/sum;
 // otherwise the unnormalised gather of V channels (permutohedral.cu:401-413,
-// 487-496).
-constexpr int kSlicePix = 1;   // pixels per thread in k_slice
+// 487-496).  One thread per pixel; the tile's vertex ids staged in shared
+// memory.
 
-template <int PD, int V, bool FWD>
-__global__ void __launch_bounds__(Cfg<PD>::P / kSlicePix)
-k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
-        const float* __restrict__ lat1, unsigned long long* st_slot, unsigned st_seq) {
+// COH: the rows and vertex ids were written earlier in the same launch (the
+// fused filter kernel), so they are read through L2, not the read-only path.
+template <int PD, int V, bool FWD, bool COH, typename Sync>
+__device__ __forceinline__ void slice_tile(int tile, int t, float* __restrict__ out, float* __restrict__ wout,
+                                           const Geo& geo, const LatView& L, const float* __restrict__ lat,
+                                           int* svid, Sync sync) {
     using C = Cfg<PD>;
-    report_status(st_slot, st_seq, L.hdr);
-    const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
-    constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS, R = kSlicePix, T = P / R;
+    constexpr int K = C::K, P = C::P;
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
-    __shared__ int svid[SLOTS];
-    const int t = threadIdx.x, tile = blockIdx.x;
     const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
-    const int x0 = tp.x0, y0 = tp.y0;
-    // pixels t and t + T of the tile; all slot loads issued before any use
-    bool act[R];
-    int lid[R][K];
-    float w[R][K];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        const int pi = t + r * T;
-        act[r] = x0 + (pi % C::TW) < geo.w && y0 + (pi / C::TW) < geo.h;
-        const size_t so = (size_t)tile * K * P + pi;
-#pragma unroll
-        for (int c = 0; c < K; ++c) {
-            lid[r][c] = act[r] ? (int)L.slot_lid[so + (size_t)c * P] : 0;
-            w[r][c] = act[r] ? L.slot_w[so + (size_t)c * P] : 0.0f;
-        }
-    }
-    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
-    for (int u = t; u < cnt; u += T) svid[u] = L.staged_vid[off + u];
-    __syncthreads();
-    float acc[R][NC];
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int j = 0; j < NC; ++j) acc[r][j] = 0.0f;
+    // all slot loads issued before any use
+    const bool act = tp.x0 + (t % C::TW) < geo.w && tp.y0 + (t / C::TW) < geo.h;
+    int lid[K];
+    float w[K];
+    const size_t so = (size_t)tile * K * P + t;
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-            const int vid = act[r] ? svid[lid[r][c]] : -1;
-            if (vid < 0) continue;   // inactive pixel, or failed insert (reported in the status word)
-            float rw[CP];
-            load_row<CP>(lat + (size_t)vid * CP, rw);
-#pragma unroll
-            for (int j = 0; j < NC; ++j) acc[r][j] = __fmaf_rn(w[r][c], rw[j], acc[r][j]);
-        }
+        lid[c] = act ? (int)L.slot_lid[so + (size_t)c * P] : 0;
+        w[c] = act ? L.slot_w[so + (size_t)c * P] : 0.0f;
     }
+    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
+    for (int u = t; u < cnt; u += P) svid[u] = COH ? __ldcg(L.staged_vid + off + u) : L.staged_vid[off + u];
+    sync();
+    float acc[NC];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-        if (!act[r]) continue;
-        const int pi = t + r * T;
-        const size_t p = (size_t)(tp.pix0 + (long long)(pi / C::TW) * geo.w + (pi % C::TW));
+    for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        const int vid = act ? svid[lid[c]] : -1;
+        if (vid < 0) continue;   // inactive pixel, or failed insert (reported in the status word)
+        float rw[CP];
+        if constexpr (COH) load_row_cg<CP>(lat + (size_t)vid * CP, rw);
+        else load_row<CP>(lat + (size_t)vid * CP, rw);
+#pragma unroll
+        for (int j = 0; j < NC; ++j) acc[j] = __fmaf_rn(w[c], rw[j], acc[j]);
+    }
+    if (act) {
+        const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
         if constexpr (FWD) {
-            const float inv = 1.0f / acc[r][V];
+            const float inv = 1.0f / acc[V];
 #pragma unroll
-            for (int j = 0; j < V; ++j) out[p * V + j] = acc[r][j] * inv;
+            for (int j = 0; j < V; ++j) out[p * V + j] = acc[j] * inv;
             wout[p] = inv;
         } else {
 #pragma unroll
-            for (int j = 0; j < V; ++j) out[p * V + j] = acc[r][j];
+            for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
         }
     }
+    sync();   // svid is reused by the worker's next tile
+}
+
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(Cfg<PD>::P)
+k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
+        const float* __restrict__ lat1, unsigned long long* st_slot, unsigned st_seq) {
+    __shared__ int svid[Cfg<PD>::SLOTS];
+    report_status(st_slot, st_seq, L.hdr);
+    const float* lat = L.hdr->blur_final ? lat1 : lat0;
+    slice_tile<PD, V, FWD, false>(blockIdx.x, threadIdx.x, out, wout, geo, L, lat, svid, CtaSync{});
+}
+
+// ---------------------------------------------------------------- fused filter
+
+// One cooperative launch for the whole filter of one direction: (zero the
+// value rows | the blur-neighbour lookups) -> splat -> grid barrier -> the
+// K blur passes -> grid barrier -> slice.  Every CTA holds FILTER_WORKERS
+// tile workers of P threads each (named barriers 1..4 inside the CTA), which
+// take the tiles in turn for the splat and the slice; the grid-wide phases
+// (neighbours, blur) use all threads.  Replaces the launch sequence
+// k_neighbors | k_splat -> k_blur_all -> k_slice, whose kernel boundaries
+// (launch gaps, ramp-up, last-wave tails) cost more than the grid barriers.
+constexpr int kFilterWorkers = 4;
+
+template <int PD>
+__host__ __device__ constexpr int filter_threads() { return kFilterWorkers * Cfg<PD>::P; }
+
+struct FilterArgs {
+    const float* vals;        // splat input: values, or the upstream gradient
+    const float* wt;          // backward: the saved normaliser
+    float* out;
+    float* wout;              // forward: normaliser output
+    float* rows0;             // lattice value rows, ping-pong; the splat accumulates into rows0
+    float* rows1;
+    uint8_t* bstate;          // bookkeeping of the streaming blur
+    int* final_flag;          // receives the buffer (0/1) that holds the blur's result
+    int resolve;              // the splat resolves the staged keys' vertex ids (right after a build)
+    int zero_rows;            // zero rows0 first (a call on a kept lattice)
+    int neighbors;            // the blur-neighbour lookups first (right after a build)
+    int reverse;              // blur axis order pd..0
+    int blur_flags;           // kBlurHalf, kBlurStream
+    unsigned long long* st_slot;
+    unsigned st_seq;
+};
+
+template <int PD, int V, bool FWD>
+__host__ __device__ constexpr size_t filter_smem_bytes() {
+    constexpr int NC = FWD ? V + 1 : V;
+    constexpr size_t workers = (size_t)kFilterWorkers * sizeof(SplatSmem<PD, NC>);
+    constexpr size_t nbr = (size_t)(filter_threads<PD>() / 32) * sizeof(NbrWarpSmem<PD>);
+    constexpr size_t queue = (size_t)filter_threads<PD>() * kBlurVpt * 16;
+    constexpr size_t m1 = workers > nbr ? workers : nbr;
+    return m1 > queue ? m1 : queue;
+}
+
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(filter_threads<PD>(), 1024 / filter_threads<PD>())
+k_filter(Geo geo, LatView L, ScrView S, FilterArgs fa) {
+    using C = Cfg<PD>;
+    constexpr int P = C::P;
+    constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
+    constexpr int NC = FWD ? V + 1 : V;
+    extern __shared__ __align__(16) unsigned char fsm[];
+    const int wk = threadIdx.x / P, t = threadIdx.x - wk * P;
+    const int nthreads = gridDim.x * blockDim.x;
+    const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+    const WorkerSync wsync{1 + wk, P};
+    unsigned phase = 0;
+    if (fa.zero_rows) {   // rows [0, m) of rows0, which the splat accumulates into
+        const size_t n = (size_t)L.hdr->m * CP;
+        for (size_t i = gtid; i < n; i += nthreads) fa.rows0[i] = 0.0f;
+        grid_barrier(L.hdr, phase);
+    }
+    if (fa.neighbors) {
+        neighbors_grid<PD>(geo, L, S, gtid, nthreads, reinterpret_cast<NbrWarpSmem<PD>*>(fsm) + (threadIdx.x >> 5));
+        __syncthreads();   // the queue memory becomes the workers'
+    }
+    SplatSmem<PD, NC>& ws = reinterpret_cast<SplatSmem<PD, NC>*>(fsm)[wk];
+    for (int tile = blockIdx.x * kFilterWorkers + wk; tile < geo.tiles; tile += gridDim.x * kFilterWorkers)
+        splat_tile<PD, V, FWD>(tile, t, fa.vals, fa.wt, geo, L, S, fa.resolve, fa.rows0, ws, wsync);
+    grid_barrier(L.hdr, phase);
+    const int M = L.hdr->m;
+    const float* res = fa.rows0;
+    if (blur_fits_resident<CP>(M, nthreads) && !(fa.blur_flags & kBlurStream)) {
+        res = blur_resident<PD, CP>(L, fa.rows0, fa.rows1, fa.reverse, M, phase);
+    } else if (fa.blur_flags & kBlurHalf) {
+        blur_streaming<PD, CP, true>(L.nbr, fa.bstate, L.hdr, fa.rows0, fa.rows1, fa.reverse, nullptr, M, gtid,
+                                     nthreads, reinterpret_cast<uint4*>(fsm), phase);
+    } else {
+        blur_streaming<PD, CP, false>(L.nbr, fa.bstate, L.hdr, fa.rows0, fa.rows1, fa.reverse, nullptr, M, gtid,
+                                      nthreads, reinterpret_cast<uint4*>(fsm), phase);
+    }
+    if (gtid == 0 && fa.final_flag) *fa.final_flag = res == fa.rows1 ? 1 : 0;
+    grid_barrier(L.hdr, phase);
+    for (int tile = blockIdx.x * kFilterWorkers + wk; tile < geo.tiles; tile += gridDim.x * kFilterWorkers)
+        slice_tile<PD, V, FWD, true>(tile, t, fa.out, fa.wout, geo, L, res, ws.svid, wsync);
+    grid_exit(L.hdr, fa.st_slot, fa.st_seq);
 }
 
 // ---------------------------------------------------------------- feature gradient
