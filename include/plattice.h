@@ -257,10 +257,8 @@ int plattice_noalloc_status(int* status, int* m, void* stream);
  * the launch count (stage order as plattice_profile_stage_name), and clears
  * the record.  Stages: 0 tile_build, 1 clear, 2 insert (and compaction),
  * 3 neighbors, 4 blur_fwd, 5 slice_fwd, 6 zero, 7 splat_bwd, 8 blur_bwd,
- * 9 slice_bwd, 10 splat_fwd, 11 filter_fwd, 12 filter_bwd (the fused filter
- * kernel: neighbour lookups or row zeroing, splat, blur and slice in one
- * launch). */
-#define PLATTICE_PROFILE_STAGES 13
+ * 9 slice_bwd, 10 splat_fwd. */
+#define PLATTICE_PROFILE_STAGES 11
 void plattice_profile_enable(int on);
 int plattice_profile_read(double* ms_total, int* launches, int n_stages);
 const char* plattice_profile_stage_name(int stage);

@@ -168,7 +168,7 @@ def filter_workspace_size(h, w, pd, vd):
     return b.value
 
 
-PROFILE_STAGES = 13
+PROFILE_STAGES = 11
 
 
 def profile_enable(on=True):

@@ -529,7 +529,7 @@ int plattice_profile_read(double* ms_total, int* launches, int n_stages) {
 const char* plattice_profile_stage_name(int stage) {
     static const char* names[pl::STAGE_COUNT] = {
         "tile_build", "clear", "insert", "neighbors", "blur_fwd", "slice_fwd",
-        "zero", "splat_bwd", "blur_bwd", "slice_bwd", "splat_fwd", "filter_fwd", "filter_bwd"};
+        "zero", "splat_bwd", "blur_bwd", "slice_bwd", "splat_fwd"};
     return (stage >= 0 && stage < pl::STAGE_COUNT) ? names[stage] : "";
 }
 

@@ -201,33 +201,13 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     return e;
 }
 
-// the fused filter kernel's dynamic shared memory and its co-resident CTAs per SM
-template <int PD, int V, bool FWD>
-cudaError_t filter_attr(int* per_sm) {
-    constexpr size_t smem = filter_smem_bytes<PD, V, FWD>();
-    cudaError_t e = cudaFuncSetAttribute(k_filter<PD, V, FWD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_filter<PD, V, FWD>, filter_threads<PD>(), smem);
-    if (e != cudaSuccess) return e;
-    return *per_sm < 1 ? cudaErrorLaunchOutOfResources : cudaSuccess;
-}
-
-// Cooperative launch of the fused filter on every co-resident CTA (grid
-// barriers inside).  `fa` is completed here with the call's blur settings and
-// status ticket.
-template <int PD, int V, bool FWD>
-cudaError_t launch_filter(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv, FilterArgs fa) {
-    int per_sm = 0;
-    cudaError_t e = kernel_once(reinterpret_cast<const void*>(k_filter<PD, V, FWD>), filter_attr<PD, V, FWD>, &per_sm);
-    if (e != cudaSuccess) return e;
-    fa.bstate = a.bstate;
-    fa.blur_flags = a.blur_flags;
-    if (!fa.final_flag) fa.final_flag = &Lv.hdr->blur_final;
-    fa.st_slot = a.st.slot;
-    fa.st_seq = a.st.seq;
-    PL_LAUNCH(FWD ? STAGE_FILTER_FWD : STAGE_FILTER_BWD, a.stream,
-              e = launch_k(k_filter<PD, V, FWD>, dim3(a.sm_count * per_sm), dim3(filter_threads<PD>()),
-                           filter_smem_bytes<PD, V, FWD>(), a.stream, true, geo, Lv, Sv, fa));
+// Zero the first m rows (of cp floats) of a lattice value buffer: float4
+// stores over a grid sized to the rows (at most two CTAs per SM), so that the
+// launch costs no more than the stores.
+inline cudaError_t zero_rows(const CallArgs& a, float* buf, const LatticeHeader* hdr, int cp, int stage) {
+    cudaError_t e;
+    PL_LAUNCH(stage, a.stream,
+              e = launch_k(k_zero_rows, dim3(a.sm_count * 2), dim3(256), 0, a.stream, false, buf, hdr, cp));
     return e;
 }
 
@@ -239,16 +219,23 @@ cudaError_t forward_v(const CallArgs& a) {
     const ScrView Sv = scr_view(a.scratch, a.lay);
     cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPF);
     if (e != cudaSuccess) return e;
-    // neighbour lookups + splat, blur in axis order 0..pd (permutohedral.cu:585), slice
-    FilterArgs fa = {};
-    fa.vals = a.values;
-    fa.out = a.out;
-    fa.wout = a.wout;
-    fa.rows0 = a.v0;
-    fa.rows1 = a.v1;
-    fa.resolve = 1;
-    fa.neighbors = 1;
-    return launch_filter<PD, V, true>(a, geo, Lv, Sv, fa);
+    // neighbour lookups (L2-latency-bound) overlap the splat (HBM-bound)
+    e = neighbors_alongside<PD>(a, geo, Lv, Sv, [&] {
+        cudaError_t es;
+        PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
+                  es = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                                  a.values, (const float*)nullptr, geo, Lv, Sv, 1, a.v0));
+        return es;
+    });
+    if (e != cudaSuccess) return e;
+    // blur in axis order 0..pd (permutohedral.cu:585)
+    e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
+              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
+                           false, a.out, a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot,
+                           a.st.seq));
+    return e;
 }
 
 template <int PD, int V>
@@ -257,38 +244,54 @@ cudaError_t backward_v(const CallArgs& a) {
     const Geo geo = make_geo(a);
     const LatView Lv = lat_view(a.lattice, a.lay);
     const ScrView Sv = a.scratch ? scr_view(a.scratch, a.lay) : ScrView{};
-    FilterArgs fa = {};
-    fa.vals = a.values;
-    fa.wt = a.weight_in;
-    fa.out = a.out;
-    fa.rows0 = a.v0;
-    fa.rows1 = a.v1;
-    fa.reverse = 1;   // blur in axis order pd..0 (permutohedral.cu:647)
+    cudaError_t e = cudaSuccess;
+    auto splat = [&] {
+        cudaError_t es;
+        PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
+                  es = launch_k(k_splat<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                                  a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, a.v0));
+        return es;
+    };
     if (a.lattice_state == 0) {   // rebuild (permutohedral.cu:615-635); the tile build zeroes the rows
-        cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPB);
+        e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPB);
         if (e != cudaSuccess) return e;
-        fa.resolve = 1;
-        fa.neighbors = 1;
+        e = neighbors_alongside<PD>(a, geo, Lv, Sv, splat);
     } else {
-        fa.zero_rows = 1;
+        e = zero_rows(a, a.v0, Lv.hdr, CPB, STAGE_ZERO);
+        if (e != cudaSuccess) return e;
+        e = splat();
     }
-    return launch_filter<PD, V, false>(a, geo, Lv, Sv, fa);
+    if (e != cudaSuccess) return e;
+    // blur in axis order pd..0 (permutohedral.cu:647)
+    e = launch_blur_all<PD, CPB>(a, Lv, a.v0, a.v1, 1);
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
+              e = launch_k(k_slice<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
+                           false, a.out, (float*)nullptr, geo, Lv, (const float*)a.v0, (const float*)a.v1,
+                           a.st.slot, a.st.seq));
+    return e;
 }
 
 // Forward filter of new values on a kept lattice (built by a forward call on
 // the same image): zero the value rows, splat, blur, slice.  No rebuild.
 template <int PD, int V>
 cudaError_t filter_v(const CallArgs& a) {
+    constexpr int CPF = pad_ch(V + 1);
     const Geo geo = make_geo(a);
     const LatView Lv = lat_view(a.lattice, a.lay);
-    FilterArgs fa = {};
-    fa.vals = a.values;
-    fa.out = a.out;
-    fa.wout = a.wout;
-    fa.rows0 = a.v0;
-    fa.rows1 = a.v1;
-    fa.zero_rows = 1;
-    return launch_filter<PD, V, true>(a, geo, Lv, ScrView{}, fa);
+    const ScrView Sv = {};
+    cudaError_t e = zero_rows(a, a.v0, Lv.hdr, CPF, STAGE_ZERO);
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
+              e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                           a.values, (const float*)nullptr, geo, Lv, Sv, 0, a.v0));
+    if (e != cudaSuccess) return e;
+    e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
+              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.out,
+                           a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot, a.st.seq));
+    return e;
 }
 
 // Gradient of the forward filter with respect to the features, on a kept
@@ -303,7 +306,7 @@ cudaError_t fgrad_v(const CallArgs& a) {
     const int grid = a.sm_count * 8;
     cudaError_t e;
     // R: the forward's lattice values
-    e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.v0, (const LatticeHeader*)Lv.hdr, CPF);
+    e = zero_rows(a, a.v0, Lv.hdr, CPF, STAGE_ZERO);
     if (e != cudaSuccess) return e;
     e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.values,
                  (const float*)nullptr, geo, Lv, Sv, 0, a.v0);
@@ -314,7 +317,7 @@ cudaError_t fgrad_v(const CallArgs& a) {
     const size_t n = (size_t)a.lay.b * (size_t)a.lay.n_img;
     e = launch_k(k_fgrad_prep<V>, dim3(grid), dim3(256), 0, a.stream, false, a.evec, a.grad_in, a.out_in, n);
     if (e != cudaSuccess) return e;
-    e = launch_k(k_zero_rows, dim3(grid), dim3(256), 0, a.stream, false, a.hbuf0, (const LatticeHeader*)Lv.hdr, CPF);
+    e = zero_rows(a, a.hbuf0, Lv.hdr, CPF, STAGE_ZERO);
     if (e != cudaSuccess) return e;
     e = launch_k(k_splat<PD, V + 1, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
                  (const float*)a.evec, a.weight_in, geo, Lv, Sv, 0, a.hbuf0);

@@ -728,11 +728,16 @@ static __global__ void k_clear(Geo geo, LatView L, ScrView S) {
     }
 }
 
-// zero the first m rows of a lattice value buffer (a repeated backward)
+// zero the first m rows of a lattice value buffer (a call on a kept lattice);
+// rows of cp floats, cp in {1, 2} or a multiple of 4, the buffer 16-byte aligned
 static __global__ void k_zero_rows(float* buf, const LatticeHeader* hdr, int cp) {
     const size_t n = (size_t)hdr->m * cp;
     const size_t stride = (size_t)gridDim.x * blockDim.x;
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) buf[i] = 0.0f;
+    const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    float4* b4 = reinterpret_cast<float4*>(buf);
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (size_t i = i0; i < n / 4; i += stride) b4[i] = z;
+    for (size_t i = (n & ~(size_t)3) + i0; i < n; i += stride) buf[i] = 0.0f;
 }
 
 // ---------------------------------------------------------------- global table
@@ -1653,6 +1658,73 @@ __device__ __forceinline__ float* blur_resident(const LatView& L, float* buf0, f
     return x;
 }
 
+// The resident blur for rows of 4 channels and K <= 8: every neighbour
+// index the K passes need -- the vertex's own along each axis and, per pair
+// of passes, the first axis's neighbours of the second axis's neighbours --
+// is loaded at the start, so that each pair of passes costs one round of row
+// loads and one grid barrier.  Same vertex ranges, pairs and float operations
+// as blur_resident.
+template <int PD, int CP>
+__device__ __forceinline__ float* blur_resident_pf(const LatView& L, float* buf0, float* buf1, int reverse, int M,
+                                                   unsigned& phase) {
+    constexpr int K = PD + 1;
+    constexpr int NP = (K + 1) / 2;            // pairs (the last one may be a single pass)
+    constexpr int W = CP < 4 ? CP : 4;
+    const int G = gridDim.x;
+    const int vb = (int)((long long)M * blockIdx.x / G), ve = (int)((long long)M * (blockIdx.x + 1) / G);
+    const int v = vb + threadIdx.x;
+    const bool mine = v < ve;
+    float* x = buf0;
+    float* y = buf1;
+    int2 nb[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) nb[k] = nbr_at(L.nbr, M, reverse ? K - 1 - k : k, mine ? v : -1);
+    float me[CP];
+    if (mine) load_row_cg<CP>(x + (size_t)v * CP, me);
+    int2 ha[NP], hb[NP];   // pair p: neighbours along axis 2p of the axis-(2p+1) neighbours
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        if (2 * p + 1 < K) {
+            const int ax = reverse ? K - 1 - 2 * p : 2 * p;
+            ha[p] = nbr_at(L.nbr, M, ax, nb[2 * p + 1].x);
+            hb[p] = nbr_at(L.nbr, M, ax, nb[2 * p + 1].y);
+        } else {
+            ha[p] = hb[p] = make_int2(-1, -1);
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        const int k = 2 * p;
+        const bool pair = k + 1 < K;
+        if (mine) {
+#pragma unroll
+            for (int c0 = 0; c0 < CP; c0 += W) {
+                const float* xc = x + c0;
+                float mi[W], a[W], b[W], o[W];
+#pragma unroll
+                for (int j = 0; j < W; ++j) mi[j] = me[c0 + j];
+                if (nb[k].x >= 0) load_row_cg<W>(xc + (size_t)nb[k].x * CP, a);
+                if (nb[k].y >= 0) load_row_cg<W>(xc + (size_t)nb[k].y * CP, b);
+                blur_row<W>(mi, a, b, nb[k], o);
+                if (pair) {
+                    float pa[W], pb[W], q[W];
+                    if (nb[k + 1].x >= 0) blur_at<W, CP>(xc, nb[k + 1].x, ha[p], pa);
+                    if (nb[k + 1].y >= 0) blur_at<W, CP>(xc, nb[k + 1].y, hb[p], pb);
+                    blur_row<W>(o, pa, pb, nb[k + 1], q);
+#pragma unroll
+                    for (int j = 0; j < W; ++j) o[j] = q[j];
+                }
+                store_row<W>(y + (size_t)v * CP + c0, o);
+#pragma unroll
+                for (int j = 0; j < W; ++j) me[c0 + j] = o[j];
+            }
+        }
+        float* t = x; x = y; y = t;
+        if (p + 1 < NP) grid_barrier(L.hdr, phase);
+    }
+    return x;
+}
+
 template <int CP>
 __device__ __forceinline__ bool blur_fits_resident(int M, int threads) {
     return M <= threads * (CP <= 2 ? 2 : 1);
@@ -1667,7 +1739,9 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned phase = 0;
     if (blur_fits_resident<CP>(M, stride) && !(flags & kBlurStream)) {
-        float* res = blur_resident<PD, CP>(L, buf0, buf1, reverse, M, phase);
+        float* res;
+        if constexpr (CP == 4 && PD + 1 <= 8) res = blur_resident_pf<PD, CP>(L, buf0, buf1, reverse, M, phase);
+        else res = blur_resident<PD, CP>(L, buf0, buf1, reverse, M, phase);
         if (tid == 0) *final_flag = (res == buf1) ? 1 : 0;
     } else if (flags & kBlurHalf) {
         blur_streaming<PD, CP, true>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride,
@@ -1698,153 +1772,56 @@ __device__ __forceinline__ void report_status(unsigned long long* slot, unsigned
 // 487-496).  One thread per pixel; the tile's vertex ids staged in shared
 // memory.
 
-// COH: the rows and vertex ids were written earlier in the same launch (the
-// fused filter kernel), so they are read through L2, not the read-only path.
-template <int PD, int V, bool FWD, bool COH, typename Sync>
-__device__ __forceinline__ void slice_tile(int tile, int t, float* __restrict__ out, float* __restrict__ wout,
-                                           const Geo& geo, const LatView& L, const float* __restrict__ lat,
-                                           int* svid, Sync sync) {
+// One thread per pixel.  The K slot records are loaded first, then the K
+// vertex ids through L1 (the tile's few hundred staged ids are shared by its
+// 256 pixels), then the K rows: no shared-memory stage and no barrier, so
+// every warp proceeds on its own.
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(Cfg<PD>::P)
+k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
+        const float* __restrict__ lat1, unsigned long long* st_slot, unsigned st_seq) {
     using C = Cfg<PD>;
     constexpr int K = C::K, P = C::P;
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
+    report_status(st_slot, st_seq, L.hdr);
+    const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
+    const int t = threadIdx.x, tile = blockIdx.x;
     const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
-    // all slot loads issued before any use
     const bool act = tp.x0 + (t % C::TW) < geo.w && tp.y0 + (t / C::TW) < geo.h;
-    int lid[K];
+    int vid[K];
     float w[K];
     const size_t so = (size_t)tile * K * P + t;
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        lid[c] = act ? (int)L.slot_lid[so + (size_t)c * P] : 0;
+        vid[c] = act ? (int)L.slot_lid[so + (size_t)c * P] : 0;
         w[c] = act ? L.slot_w[so + (size_t)c * P] : 0.0f;
     }
-    const int cnt = L.tile_cnt[tile], off = L.tile_off[tile];
-    for (int u = t; u < cnt; u += P) svid[u] = COH ? __ldcg(L.staged_vid + off + u) : L.staged_vid[off + u];
-    sync();
+    const int* __restrict__ sv = L.staged_vid + L.tile_off[tile];
+#pragma unroll
+    for (int c = 0; c < K; ++c) vid[c] = act ? __ldg(sv + vid[c]) : -1;
     float acc[NC];
 #pragma unroll
     for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        const int vid = act ? svid[lid[c]] : -1;
-        if (vid < 0) continue;   // inactive pixel, or failed insert (reported in the status word)
+        if (vid[c] < 0) continue;   // inactive pixel, or failed insert (reported in the status word)
         float rw[CP];
-        if constexpr (COH) load_row_cg<CP>(lat + (size_t)vid * CP, rw);
-        else load_row<CP>(lat + (size_t)vid * CP, rw);
+        load_row<CP>(lat + (size_t)vid[c] * CP, rw);
 #pragma unroll
         for (int j = 0; j < NC; ++j) acc[j] = __fmaf_rn(w[c], rw[j], acc[j]);
     }
-    if (act) {
-        const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
-        if constexpr (FWD) {
-            const float inv = 1.0f / acc[V];
+    if (!act) return;
+    const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
+    if constexpr (FWD) {
+        const float inv = 1.0f / acc[V];
 #pragma unroll
-            for (int j = 0; j < V; ++j) out[p * V + j] = acc[j] * inv;
-            wout[p] = inv;
-        } else {
-#pragma unroll
-            for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
-        }
-    }
-    sync();   // svid is reused by the worker's next tile
-}
-
-template <int PD, int V, bool FWD>
-__global__ void __launch_bounds__(Cfg<PD>::P)
-k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
-        const float* __restrict__ lat1, unsigned long long* st_slot, unsigned st_seq) {
-    __shared__ int svid[Cfg<PD>::SLOTS];
-    report_status(st_slot, st_seq, L.hdr);
-    const float* lat = L.hdr->blur_final ? lat1 : lat0;
-    slice_tile<PD, V, FWD, false>(blockIdx.x, threadIdx.x, out, wout, geo, L, lat, svid, CtaSync{});
-}
-
-// ---------------------------------------------------------------- fused filter
-
-// One cooperative launch for the whole filter of one direction: (zero the
-// value rows | the blur-neighbour lookups) -> splat -> grid barrier -> the
-// K blur passes -> grid barrier -> slice.  Every CTA holds FILTER_WORKERS
-// tile workers of P threads each (named barriers 1..4 inside the CTA), which
-// take the tiles in turn for the splat and the slice; the grid-wide phases
-// (neighbours, blur) use all threads.  Replaces the launch sequence
-// k_neighbors | k_splat -> k_blur_all -> k_slice, whose kernel boundaries
-// (launch gaps, ramp-up, last-wave tails) cost more than the grid barriers.
-constexpr int kFilterWorkers = 4;
-
-template <int PD>
-__host__ __device__ constexpr int filter_threads() { return kFilterWorkers * Cfg<PD>::P; }
-
-struct FilterArgs {
-    const float* vals;        // splat input: values, or the upstream gradient
-    const float* wt;          // backward: the saved normaliser
-    float* out;
-    float* wout;              // forward: normaliser output
-    float* rows0;             // lattice value rows, ping-pong; the splat accumulates into rows0
-    float* rows1;
-    uint8_t* bstate;          // bookkeeping of the streaming blur
-    int* final_flag;          // receives the buffer (0/1) that holds the blur's result
-    int resolve;              // the splat resolves the staged keys' vertex ids (right after a build)
-    int zero_rows;            // zero rows0 first (a call on a kept lattice)
-    int neighbors;            // the blur-neighbour lookups first (right after a build)
-    int reverse;              // blur axis order pd..0
-    int blur_flags;           // kBlurHalf, kBlurStream
-    unsigned long long* st_slot;
-    unsigned st_seq;
-};
-
-template <int PD, int V, bool FWD>
-__host__ __device__ constexpr size_t filter_smem_bytes() {
-    constexpr int NC = FWD ? V + 1 : V;
-    constexpr size_t workers = (size_t)kFilterWorkers * sizeof(SplatSmem<PD, NC>);
-    constexpr size_t nbr = (size_t)(filter_threads<PD>() / 32) * sizeof(NbrWarpSmem<PD>);
-    constexpr size_t queue = (size_t)filter_threads<PD>() * kBlurVpt * 16;
-    constexpr size_t m1 = workers > nbr ? workers : nbr;
-    return m1 > queue ? m1 : queue;
-}
-
-template <int PD, int V, bool FWD>
-__global__ void __launch_bounds__(filter_threads<PD>(), 1024 / filter_threads<PD>())
-k_filter(Geo geo, LatView L, ScrView S, FilterArgs fa) {
-    using C = Cfg<PD>;
-    constexpr int P = C::P;
-    constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
-    constexpr int NC = FWD ? V + 1 : V;
-    extern __shared__ __align__(16) unsigned char fsm[];
-    const int wk = threadIdx.x / P, t = threadIdx.x - wk * P;
-    const int nthreads = gridDim.x * blockDim.x;
-    const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
-    const WorkerSync wsync{1 + wk, P};
-    unsigned phase = 0;
-    if (fa.zero_rows) {   // rows [0, m) of rows0, which the splat accumulates into
-        const size_t n = (size_t)L.hdr->m * CP;
-        for (size_t i = gtid; i < n; i += nthreads) fa.rows0[i] = 0.0f;
-        grid_barrier(L.hdr, phase);
-    }
-    if (fa.neighbors) {
-        neighbors_grid<PD>(geo, L, S, gtid, nthreads, reinterpret_cast<NbrWarpSmem<PD>*>(fsm) + (threadIdx.x >> 5));
-        __syncthreads();   // the queue memory becomes the workers'
-    }
-    SplatSmem<PD, NC>& ws = reinterpret_cast<SplatSmem<PD, NC>*>(fsm)[wk];
-    for (int tile = blockIdx.x * kFilterWorkers + wk; tile < geo.tiles; tile += gridDim.x * kFilterWorkers)
-        splat_tile<PD, V, FWD>(tile, t, fa.vals, fa.wt, geo, L, S, fa.resolve, fa.rows0, ws, wsync);
-    grid_barrier(L.hdr, phase);
-    const int M = L.hdr->m;
-    const float* res = fa.rows0;
-    if (blur_fits_resident<CP>(M, nthreads) && !(fa.blur_flags & kBlurStream)) {
-        res = blur_resident<PD, CP>(L, fa.rows0, fa.rows1, fa.reverse, M, phase);
-    } else if (fa.blur_flags & kBlurHalf) {
-        blur_streaming<PD, CP, true>(L.nbr, fa.bstate, L.hdr, fa.rows0, fa.rows1, fa.reverse, nullptr, M, gtid,
-                                     nthreads, reinterpret_cast<uint4*>(fsm), phase);
+        for (int j = 0; j < V; ++j) out[p * V + j] = acc[j] * inv;
+        wout[p] = inv;
     } else {
-        blur_streaming<PD, CP, false>(L.nbr, fa.bstate, L.hdr, fa.rows0, fa.rows1, fa.reverse, nullptr, M, gtid,
-                                      nthreads, reinterpret_cast<uint4*>(fsm), phase);
+#pragma unroll
+        for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
     }
-    if (gtid == 0 && fa.final_flag) *fa.final_flag = res == fa.rows1 ? 1 : 0;
-    grid_barrier(L.hdr, phase);
-    for (int tile = blockIdx.x * kFilterWorkers + wk; tile < geo.tiles; tile += gridDim.x * kFilterWorkers)
-        slice_tile<PD, V, FWD, true>(tile, t, fa.out, fa.wout, geo, L, res, ws.svid, wsync);
-    grid_exit(L.hdr, fa.st_slot, fa.st_seq);
 }
 
 // ---------------------------------------------------------------- feature gradient

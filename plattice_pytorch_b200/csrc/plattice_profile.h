@@ -18,8 +18,6 @@ enum Stage {
     STAGE_BLUR_BWD,        // bwd: the blur passes
     STAGE_SLICE_BWD,       // bwd: slice
     STAGE_SPLAT_FWD,       // fwd: splat of [v*w, w]
-    STAGE_FILTER_FWD,      // fwd: the fused filter (neighbours + splat, blur, slice)
-    STAGE_FILTER_BWD,      // bwd: the fused filter (zero or neighbours + splat, blur, slice)
     STAGE_COUNT
 };
 
