@@ -187,10 +187,9 @@ int plattice_poll_status(void);
 
 /* Everything the first call for (pd, vd) does in the current CUDA context
  * apart from the filter itself: kernel attribute settings (dynamic shared
- * memory limits), the creation of the library's side stream and its two
- * events, and the loading of every kernel of the forward and backward filter
- * (with lazy module loading each kernel is otherwise loaded at its first
- * launch).  Call it before any stream capture, or before real-time work that
+ * memory limits), occupancy queries of the cooperative kernels, and the
+ * loading of every kernel of the forward and backward filter (with lazy
+ * module loading each kernel is otherwise loaded at its first launch).  Call it before any stream capture, or before real-time work that
  * must not pay these costs.  No reference counterpart. */
 int plattice_prepare(int pd, int vd);
 
@@ -232,11 +231,10 @@ void plattice_debug_set_blur_streaming(int on);
  * An image whose workspace exceeds the array returns PLATTICE_ERR_WORKSPACE
  * (plattice_noalloc_error_detail() says how much it needs).
  * First call in a CUDA context: it looks up the array's device address in
- * that context, sets kernel attributes, creates the library's side stream and
- * two events, and (lazy module loading) loads the kernels it launches --
- * plattice_prepare(pd, vd) does all of this except the address lookup, and
- * plattice_noalloc_status does the lookup; make these first calls before any
- * stream capture.  All calls on a device share the array, so calls that
+ * that context, sets kernel attributes, queries occupancies, and (lazy module
+ * loading) loads the kernels it launches -- plattice_prepare(pd, vd) does all
+ * of this except the address lookup, and plattice_noalloc_status does the
+ * lookup; make these first calls before any stream capture.  All calls on a device share the array, so calls that
  * overlap on the GPU race: issue them one after the other.  Its device
  * failures are not reported through the status ring (whose pinned host slots
  * would be an allocation): plattice_noalloc_status reads them. */

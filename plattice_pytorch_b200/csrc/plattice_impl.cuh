@@ -169,18 +169,18 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     return e;
 }
 
-// Blur neighbours on the side stream while `main_work` runs on the caller's stream.
-template <int PD, typename MainWork>
-cudaError_t neighbors_alongside(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
-                                MainWork main_work) {
-    SideFork f;
-    cudaError_t e = side_fork(a.stream, &f);
-    if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_NEIGHBORS, f.side,
-              e = launch_k(k_neighbors<PD>, dim3(a.sm_count * 8), dim3(kNbrThreads), 0, f.side, false, geo, Lv, Sv));
-    const cudaError_t e1 = e == cudaSuccess ? main_work() : e;
-    e = side_join(a.stream, &f);
-    return e1 != cudaSuccess ? e1 : e;
+// The splat right after a build, with the blur-neighbour lookups in the same
+// launch (as many lookup threads as a k_neighbors grid of 8 x 256 threads
+// per SM).
+template <int PD, int V, bool FWD>
+cudaError_t splat_with_neighbors(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
+                                 const float* vals, const float* wt, float* rows, int stage) {
+    const int nbr_blocks = a.sm_count * 8 * kNbrThreads / Cfg<PD>::P;
+    cudaError_t e;
+    PL_LAUNCH(stage, a.stream,
+              e = launch_k(k_splat_nbr<PD, V, FWD>, dim3(nbr_blocks + a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
+                           false, vals, wt, geo, Lv, Sv, rows, nbr_blocks));
+    return e;
 }
 
 // Cooperative launch of the blur kernel on as many CTAs as are co-resident
@@ -201,13 +201,28 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     return e;
 }
 
-// Zero the first m rows (of cp floats) of a lattice value buffer: float4
-// stores over a grid sized to the rows (at most two CTAs per SM), so that the
-// launch costs no more than the stores.
-inline cudaError_t zero_rows(const CallArgs& a, float* buf, const LatticeHeader* hdr, int cp, int stage) {
-    cudaError_t e;
+// co-resident CTAs per SM of the zero-then-splat kernel
+template <int PD, int V, bool FWD>
+cudaError_t splat_zeroed_attr(int* per_sm) {
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_splat_zeroed<PD, V, FWD>, Cfg<PD>::P, 0);
+    if (e != cudaSuccess) return e;
+    return *per_sm < 1 ? cudaErrorLaunchOutOfResources : cudaSuccess;
+}
+
+// Splat into rows that must first be zeroed (a call on a kept lattice): one
+// cooperative launch (zeroing, a grid barrier, the splat).
+template <int PD, int V, bool FWD>
+cudaError_t splat_zeroed(const CallArgs& a, const Geo& geo, const LatView& Lv, const float* vals, const float* wt,
+                         float* rows, int stage) {
+    constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
+    int per_sm = 0;
+    cudaError_t e = kernel_once(reinterpret_cast<const void*>(k_splat_zeroed<PD, V, FWD>), splat_zeroed_attr<PD, V, FWD>,
+                                &per_sm);
+    if (e != cudaSuccess) return e;
+    const int grid = a.sm_count * per_sm;
     PL_LAUNCH(stage, a.stream,
-              e = launch_k(k_zero_rows, dim3(a.sm_count * 2), dim3(256), 0, a.stream, false, buf, hdr, cp));
+              e = launch_k(k_splat_zeroed<PD, V, FWD>, dim3(grid < a.lay.tiles ? grid : a.lay.tiles),
+                           dim3(Cfg<PD>::P), 0, a.stream, true, vals, wt, geo, Lv, rows, CP));
     return e;
 }
 
@@ -219,14 +234,8 @@ cudaError_t forward_v(const CallArgs& a) {
     const ScrView Sv = scr_view(a.scratch, a.lay);
     cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPF);
     if (e != cudaSuccess) return e;
-    // neighbour lookups (L2-latency-bound) overlap the splat (HBM-bound)
-    e = neighbors_alongside<PD>(a, geo, Lv, Sv, [&] {
-        cudaError_t es;
-        PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
-                  es = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
-                                  a.values, (const float*)nullptr, geo, Lv, Sv, 1, a.v0));
-        return es;
-    });
+    // neighbour lookups (L2-latency-bound) alongside the splat (HBM-bound)
+    e = splat_with_neighbors<PD, V, true>(a, geo, Lv, Sv, a.values, nullptr, a.v0, STAGE_SPLAT_FWD);
     if (e != cudaSuccess) return e;
     // blur in axis order 0..pd (permutohedral.cu:585)
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
@@ -245,21 +254,12 @@ cudaError_t backward_v(const CallArgs& a) {
     const LatView Lv = lat_view(a.lattice, a.lay);
     const ScrView Sv = a.scratch ? scr_view(a.scratch, a.lay) : ScrView{};
     cudaError_t e = cudaSuccess;
-    auto splat = [&] {
-        cudaError_t es;
-        PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
-                  es = launch_k(k_splat<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
-                                  a.values, a.weight_in, geo, Lv, Sv, a.lattice_state == 0 ? 1 : 0, a.v0));
-        return es;
-    };
     if (a.lattice_state == 0) {   // rebuild (permutohedral.cu:615-635); the tile build zeroes the rows
         e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPB);
         if (e != cudaSuccess) return e;
-        e = neighbors_alongside<PD>(a, geo, Lv, Sv, splat);
-    } else {
-        e = zero_rows(a, a.v0, Lv.hdr, CPB, STAGE_ZERO);
-        if (e != cudaSuccess) return e;
-        e = splat();
+        e = splat_with_neighbors<PD, V, false>(a, geo, Lv, Sv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
+    } else {   // zero the rows and splat in one launch
+        e = splat_zeroed<PD, V, false>(a, geo, Lv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
     }
     if (e != cudaSuccess) return e;
     // blur in axis order pd..0 (permutohedral.cu:647)
@@ -279,12 +279,7 @@ cudaError_t filter_v(const CallArgs& a) {
     constexpr int CPF = pad_ch(V + 1);
     const Geo geo = make_geo(a);
     const LatView Lv = lat_view(a.lattice, a.lay);
-    const ScrView Sv = {};
-    cudaError_t e = zero_rows(a, a.v0, Lv.hdr, CPF, STAGE_ZERO);
-    if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_SPLAT_FWD, a.stream,
-              e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
-                           a.values, (const float*)nullptr, geo, Lv, Sv, 0, a.v0));
+    cudaError_t e = splat_zeroed<PD, V, true>(a, geo, Lv, a.values, nullptr, a.v0, STAGE_SPLAT_FWD);
     if (e != cudaSuccess) return e;
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
@@ -302,14 +297,10 @@ cudaError_t fgrad_v(const CallArgs& a) {
     constexpr int CPF = pad_ch(V + 1);
     const Geo geo = make_geo(a);
     const LatView Lv = lat_view(a.lattice, a.lay);
-    const ScrView Sv = {};
     const int grid = a.sm_count * 8;
     cudaError_t e;
     // R: the forward's lattice values
-    e = zero_rows(a, a.v0, Lv.hdr, CPF, STAGE_ZERO);
-    if (e != cudaSuccess) return e;
-    e = launch_k(k_splat<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.values,
-                 (const float*)nullptr, geo, Lv, Sv, 0, a.v0);
+    e = splat_zeroed<PD, V, true>(a, geo, Lv, a.values, nullptr, a.v0, STAGE_SPLAT_FWD);
     if (e != cudaSuccess) return e;
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0, a.flags);
     if (e != cudaSuccess) return e;
@@ -317,10 +308,7 @@ cudaError_t fgrad_v(const CallArgs& a) {
     const size_t n = (size_t)a.lay.b * (size_t)a.lay.n_img;
     e = launch_k(k_fgrad_prep<V>, dim3(grid), dim3(256), 0, a.stream, false, a.evec, a.grad_in, a.out_in, n);
     if (e != cudaSuccess) return e;
-    e = zero_rows(a, a.hbuf0, Lv.hdr, CPF, STAGE_ZERO);
-    if (e != cudaSuccess) return e;
-    e = launch_k(k_splat<PD, V + 1, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
-                 (const float*)a.evec, a.weight_in, geo, Lv, Sv, 0, a.hbuf0);
+    e = splat_zeroed<PD, V + 1, false>(a, geo, Lv, a.evec, a.weight_in, a.hbuf0, STAGE_SPLAT_BWD);
     if (e != cudaSuccess) return e;
     e = launch_blur_all<PD, CPF>(a, Lv, a.hbuf0, a.hbuf1, 1, a.flags + 1);
     if (e != cudaSuccess) return e;
@@ -331,9 +319,9 @@ cudaError_t fgrad_v(const CallArgs& a) {
 }
 
 // Everything the first call of (PD, V) does on a context besides the filter
-// itself: kernel attributes, the side stream, and the loading of every kernel
-// of the forward and backward (lazy module loading otherwise loads each on
-// its first launch).
+// itself: kernel attributes, occupancy queries, and the loading of every
+// kernel of the forward and backward (lazy module loading otherwise loads
+// each on its first launch).
 template <int PD, int V>
 cudaError_t prepare_v(const CallArgs&) {
     constexpr int CPF = pad_ch(V + 1), CPB = pad_ch(V);
@@ -342,22 +330,23 @@ cudaError_t prepare_v(const CallArgs&) {
     if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CPF>), blur_attr<PD, CPF>, &n);
     if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CPB>), blur_attr<PD, CPB>, &n);
     const void* fns[] = {reinterpret_cast<const void*>(k_tile_build<PD>), reinterpret_cast<const void*>(k_clear),
-                         reinterpret_cast<const void*>(k_insert<PD>), reinterpret_cast<const void*>(k_neighbors<PD>),
-                         reinterpret_cast<const void*>(k_splat<PD, V, true>),
-                         reinterpret_cast<const void*>(k_splat<PD, V, false>),
+                         reinterpret_cast<const void*>(k_insert<PD>),
+                         reinterpret_cast<const void*>(k_splat_nbr<PD, V, true>),
+                         reinterpret_cast<const void*>(k_splat_nbr<PD, V, false>),
                          reinterpret_cast<const void*>(k_slice<PD, V, true>),
                          reinterpret_cast<const void*>(k_slice<PD, V, false>),
-                         reinterpret_cast<const void*>(k_zero_rows)};
+                         reinterpret_cast<const void*>(k_splat_zeroed<PD, V, true>),
+                         reinterpret_cast<const void*>(k_splat_zeroed<PD, V, false>)};
     for (const void* f : fns) {
         cudaFuncAttributes fa;
         if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, f);
     }
-    if (e == cudaSuccess) {
-        SideFork f;
-        cudaStream_t s = nullptr;
-        e = side_fork(s, &f);   // creates the side stream and its events (fork on the legacy stream, no work)
-        if (e == cudaSuccess) e = side_join(s, &f);
-    }
+    int n2 = 0;
+    if (e == cudaSuccess)
+        e = kernel_once(reinterpret_cast<const void*>(k_splat_zeroed<PD, V, true>), splat_zeroed_attr<PD, V, true>, &n2);
+    if (e == cudaSuccess)
+        e = kernel_once(reinterpret_cast<const void*>(k_splat_zeroed<PD, V, false>), splat_zeroed_attr<PD, V, false>,
+                        &n2);
     return e;
 }
 

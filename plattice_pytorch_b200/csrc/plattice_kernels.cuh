@@ -728,18 +728,6 @@ static __global__ void k_clear(Geo geo, LatView L, ScrView S) {
     }
 }
 
-// zero the first m rows of a lattice value buffer (a call on a kept lattice);
-// rows of cp floats, cp in {1, 2} or a multiple of 4, the buffer 16-byte aligned
-static __global__ void k_zero_rows(float* buf, const LatticeHeader* hdr, int cp) {
-    const size_t n = (size_t)hdr->m * cp;
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
-    const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    float4* b4 = reinterpret_cast<float4*>(buf);
-    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (size_t i = i0; i < n / 4; i += stride) b4[i] = z;
-    for (size_t i = (n & ~(size_t)3) + i0; i < n; i += stride) buf[i] = 0.0f;
-}
-
 // ---------------------------------------------------------------- global table
 
 template <int CW>
@@ -1130,6 +1118,61 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
                        &wsm[threadIdx.x >> 5]);
 }
 
+// ---------------------------------------------------------------- grid barrier
+
+// Grid barrier over the CTAs of a cooperative launch (all co-resident): one
+// release-add per CTA on a counter that only grows during the launch (it is
+// zeroed by the kernel before), then acquire polls until all CTAs of this
+// phase have arrived.  The wait is bounded: a CTA that polls kBarrierSpin
+// times records PL_ST_SPIN and continues, so a failure shows in the status
+// word instead of a hang.
+constexpr int kBarrierSpin = 1 << 22;
+
+__device__ __forceinline__ unsigned atom_add_release(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase) {
+    __syncthreads();
+    ++phase;
+    if (threadIdx.x == 0) {
+        const unsigned target = phase * gridDim.x;
+        atom_add_release(&hdr->bar_count, 1u);
+        int spins = 0;
+        while (ld_acquire(&hdr->bar_count) < target) {
+            if (++spins > kBarrierSpin) {
+                atomicOr(&hdr->status, PL_ST_SPIN);
+                break;
+            }
+            if (spins > 4096) __nanosleep(32);
+        }
+    }
+    __syncthreads();
+}
+
+// At the end of a kernel with grid barriers: the last CTA to leave resets
+// the barrier counter (and this exit counter) for the next launch on the
+// lattice, and reports the status word of the call when `slot` is set.  Every
+// CTA has passed its last barrier by then.
+__device__ __forceinline__ void grid_exit(LatticeHeader* hdr, unsigned long long* slot, unsigned seq) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&hdr->bar_gen, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence();
+            if (slot) {
+                const unsigned st = (unsigned)atomicOr(&hdr->status, 0);
+                *reinterpret_cast<volatile unsigned long long*>(slot) = ((unsigned long long)seq << 32) | st;
+            }
+            atomicExch(&hdr->bar_count, 0u);
+            atomicExch(&hdr->bar_gen, 0u);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- splat
 
 // FWD: [v*w, w] per slot (permutohedral.cu:286-293); otherwise
@@ -1329,64 +1372,56 @@ __global__ void __launch_bounds__(Cfg<PD>::P)
 k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, ScrView S,
         int resolve, float* lat) {
     __shared__ SplatSmem<PD, FWD ? V + 1 : V> sm;
-    if (blockIdx.x == 0 && threadIdx.x == 0) L.hdr->bar_count = 0u;   // grid barrier of the blur that follows
     splat_tile<PD, V, FWD>(blockIdx.x, threadIdx.x, vals, wt, geo, L, S, resolve, lat, sm, CtaSync{});
 }
 
+// The splat right after a lattice build, together with the blur-neighbour
+// lookups of the new lattice in the same launch: the first `nbr_blocks` blocks
+// look up neighbours (grid-stride over the vertices), the others splat one
+// tile each and resolve the tile's vertex ids.  Blocks are dispatched in index
+// order, so the latency-bound lookups start first and the bandwidth-bound
+// tiles fill the SMs around them.
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(Cfg<PD>::P)
+k_splat_nbr(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, ScrView S, float* lat,
+            int nbr_blocks) {
+    __shared__ union {
+        SplatSmem<PD, FWD ? V + 1 : V> sp;
+        NbrWarpSmem<PD> nb[Cfg<PD>::P / 32];
+    } sm;
+    if ((int)blockIdx.x < nbr_blocks)
+        neighbors_grid<PD>(geo, L, S, blockIdx.x * blockDim.x + threadIdx.x, nbr_blocks * blockDim.x,
+                           &sm.nb[threadIdx.x >> 5]);
+    else
+        splat_tile<PD, V, FWD>(blockIdx.x - nbr_blocks, threadIdx.x, vals, wt, geo, L, S, 1, lat, sm.sp, CtaSync{});
+}
+
+// The splat of a call on a kept lattice, whose value rows must start at zero:
+// one cooperative launch that zeroes the first m rows (cp floats each, float4
+// stores), waits at one grid barrier, then takes the tiles in turn -- in place
+// of a separate zeroing kernel, whose launch costs more than its stores.
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(Cfg<PD>::P)
+k_splat_zeroed(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, float* lat,
+               int cp) {
+    __shared__ SplatSmem<PD, FWD ? V + 1 : V> sm;
+    unsigned phase = 0;
+    {
+        const size_t n = (size_t)L.hdr->m * cp;
+        const size_t stride = (size_t)gridDim.x * blockDim.x;
+        const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+        float4* b4 = reinterpret_cast<float4*>(lat);
+        const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (size_t i = i0; i < n / 4; i += stride) b4[i] = z;
+        for (size_t i = (n & ~(size_t)3) + i0; i < n; i += stride) lat[i] = 0.0f;
+    }
+    grid_barrier(L.hdr, phase);
+    for (int tile = blockIdx.x; tile < geo.tiles; tile += gridDim.x)
+        splat_tile<PD, V, FWD>(tile, threadIdx.x, vals, wt, geo, L, ScrView{}, 0, lat, sm, CtaSync{});
+    grid_exit(L.hdr, nullptr, 0u);
+}
+
 // ---------------------------------------------------------------- blur
-
-// Grid barrier over the CTAs of a cooperative launch (all co-resident): one
-// release-add per CTA on a counter that only grows during the launch (it is
-// zeroed by the kernel before), then acquire polls until all CTAs of this
-// phase have arrived.  The wait is bounded: a CTA that polls kBarrierSpin
-// times records PL_ST_SPIN and continues, so a failure shows in the status
-// word instead of a hang.
-constexpr int kBarrierSpin = 1 << 22;
-
-__device__ __forceinline__ unsigned atom_add_release(unsigned* p, unsigned v) {
-    unsigned old;
-    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-
-__device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase) {
-    __syncthreads();
-    ++phase;
-    if (threadIdx.x == 0) {
-        const unsigned target = phase * gridDim.x;
-        atom_add_release(&hdr->bar_count, 1u);
-        int spins = 0;
-        while (ld_acquire(&hdr->bar_count) < target) {
-            if (++spins > kBarrierSpin) {
-                atomicOr(&hdr->status, PL_ST_SPIN);
-                break;
-            }
-            if (spins > 4096) __nanosleep(32);
-        }
-    }
-    __syncthreads();
-}
-
-// At the end of a kernel with grid barriers: the last CTA to leave resets
-// the barrier counter (and this exit counter) for the next launch on the
-// lattice, and reports the status word of the call when `slot` is set.  Every
-// CTA has passed its last barrier by then.
-__device__ __forceinline__ void grid_exit(LatticeHeader* hdr, unsigned long long* slot, unsigned seq) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&hdr->bar_gen, 1u);
-        if (prev == gridDim.x - 1) {
-            __threadfence();
-            if (slot) {
-                const unsigned st = (unsigned)atomicOr(&hdr->status, 0);
-                *reinterpret_cast<volatile unsigned long long*>(slot) = ((unsigned long long)seq << 32) | st;
-            }
-            atomicExch(&hdr->bar_count, 0u);
-            atomicExch(&hdr->bar_gen, 0u);
-        }
-    }
-}
 
 // r *= 2^-e (exact: a power of two, far from the float range limits here)
 template <int CP>
@@ -1776,8 +1811,12 @@ __device__ __forceinline__ void report_status(unsigned long long* slot, unsigned
 // vertex ids through L1 (the tile's few hundred staged ids are shared by its
 // 256 pixels), then the K rows: no shared-memory stage and no barrier, so
 // every warp proceeds on its own.
+// full occupancy (32 registers) where the slice fits in them without spilling much
+template <int PD, int V>
+__host__ __device__ constexpr int slice_min_blocks() { return (PD <= 7 && V <= 4) ? 2048 / Cfg<PD>::P : 1; }
+
 template <int PD, int V, bool FWD>
-__global__ void __launch_bounds__(Cfg<PD>::P)
+__global__ void __launch_bounds__(Cfg<PD>::P, slice_min_blocks<PD, V>())
 k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
         const float* __restrict__ lat1, unsigned long long* st_slot, unsigned st_seq) {
     using C = Cfg<PD>;
@@ -1789,6 +1828,7 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
     const int t = threadIdx.x, tile = blockIdx.x;
     const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
     const bool act = tp.x0 + (t % C::TW) < geo.w && tp.y0 + (t / C::TW) < geo.h;
+    const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
     int vid[K];
     float w[K];
     const size_t so = (size_t)tile * K * P + t;
@@ -1797,9 +1837,9 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
         vid[c] = act ? (int)L.slot_lid[so + (size_t)c * P] : 0;
         w[c] = act ? L.slot_w[so + (size_t)c * P] : 0.0f;
     }
-    const int* __restrict__ sv = L.staged_vid + L.tile_off[tile];
+    const int off = act ? L.tile_off[tile] : 0;
 #pragma unroll
-    for (int c = 0; c < K; ++c) vid[c] = act ? __ldg(sv + vid[c]) : -1;
+    for (int c = 0; c < K; ++c) vid[c] = act ? __ldg(L.staged_vid + off + vid[c]) : -1;
     float acc[NC];
 #pragma unroll
     for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
@@ -1811,16 +1851,16 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
 #pragma unroll
         for (int j = 0; j < NC; ++j) acc[j] = __fmaf_rn(w[c], rw[j], acc[j]);
     }
-    if (!act) return;
-    const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
-    if constexpr (FWD) {
-        const float inv = 1.0f / acc[V];
+    if (act) {
+        if constexpr (FWD) {
+            const float inv = 1.0f / acc[V];
 #pragma unroll
-        for (int j = 0; j < V; ++j) out[p * V + j] = acc[j] * inv;
-        wout[p] = inv;
-    } else {
+            for (int j = 0; j < V; ++j) out[p * V + j] = acc[j] * inv;
+            wout[p] = inv;
+        } else {
 #pragma unroll
-        for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
+            for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
+        }
     }
 }
 

@@ -46,9 +46,6 @@ const DriverFns& driver_fns() {
 
 struct CtxState {
     unsigned long long id = 0;
-    std::mutex side_mu;   // held from side_fork to side_join
-    cudaStream_t side = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
     std::mutex mu;        // guards the maps
     std::unordered_map<const void*, int> once;
     std::unordered_map<const void*, void*> symbols;
@@ -99,43 +96,6 @@ CtxState* ctx_state(cudaError_t* err) {
     g_ctx.back()->id = id;
     t_last = g_ctx.back().get();
     return t_last;
-}
-
-cudaError_t side_fork(cudaStream_t main, SideFork* f) {
-    cudaError_t e;
-    CtxState* c = ctx_state(&e);
-    if (!c) return e;
-    c->side_mu.lock();
-    if (!c->side) {
-        // the side stream's kernels (blur neighbours, latency-bound) are
-        // scheduled ahead of the caller's when both wait for SMs
-        int least = 0, greatest = 0;
-        e = cudaDeviceGetStreamPriorityRange(&least, &greatest);
-        if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&c->side, cudaStreamNonBlocking, greatest);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->fork, cudaEventDisableTiming);
-        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->join, cudaEventDisableTiming);
-        if (e != cudaSuccess) {
-            c->side_mu.unlock();
-            return e;
-        }
-    }
-    e = cudaEventRecord(c->fork, main);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(c->side, c->fork, 0);
-    if (e != cudaSuccess) {
-        c->side_mu.unlock();
-        return e;
-    }
-    f->side = c->side;
-    f->token = c;
-    return cudaSuccess;
-}
-
-cudaError_t side_join(cudaStream_t main, SideFork* f) {
-    CtxState* c = static_cast<CtxState*>(f->token);
-    cudaError_t e = cudaEventRecord(c->join, c->side);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(main, c->join, 0);
-    c->side_mu.unlock();
-    return e;
 }
 
 cudaError_t kernel_once(const void* fn, cudaError_t (*set_attr)(int*), int* value) {

@@ -1,7 +1,7 @@
 // plattice_runtime.h -- host-side state of the library that belongs to a CUDA
-// context: the side stream of the neighbour lookups, one-time kernel
-// attribute settings, the fixed array of the no-allocation entry point, and
-// the ring of per-call device status words that reports device-side failures
+// context: one-time kernel attribute settings and occupancy figures, the
+// device address of the no-allocation entry point's fixed array; and the
+// ring of per-call device status words that reports device-side failures
 // (table full, a bounded wait that gave up) on a later call without
 // synchronising.
 //
@@ -21,16 +21,6 @@ struct CtxState;
 // The state of the current context (created on first use).  Returns nullptr
 // and sets *err when the context cannot be determined.
 CtxState* ctx_state(cudaError_t* err);
-
-// Side stream of the context, forked from and joined back into `main` with
-// events; the fork is held by one host thread at a time (side_fork locks,
-// side_join unlocks).
-struct SideFork {
-    cudaStream_t side;
-    void* token;
-};
-cudaError_t side_fork(cudaStream_t main, SideFork* f);
-cudaError_t side_join(cudaStream_t main, SideFork* f);
 
 // Runs set_attr once per context for the kernel `fn` (a kernel attribute
 // such as the dynamic shared-memory limit) and caches an int result (e.g. the
