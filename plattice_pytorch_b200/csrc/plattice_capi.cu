@@ -249,6 +249,7 @@ static int backward_images(float* grad_values_out, const float* grad, const floa
     a.lattice = lattice;
     a.scratch = lattice_state == 0 ? scratch : nullptr;
     rows_in_scratch(a, scratch);
+    a.v0 = pl::lattice_vb0(a);   // the splat target; the scratch's v1 is its ping-pong partner
     a.lattice_state = lattice_state;
     common_args(a, stream, true, call);
     return cuda_status(dispatch_backward(a), call);
@@ -343,7 +344,9 @@ int plattice_filter_workspace_size(int h, int w, int pd, int vd, size_t* bytes) 
 static int kept_lattice_args(pl::CallArgs& a, size_t lattice_bytes, void* ws, size_t ws_bytes, int pd, int vd,
                              int w, int h, void* stream, const char* call) {
     pl_layout(&a.lay, h, w, pd, vd);
-    if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
+    // a filter reads the arrays before vb0, whose size is the only part of the
+    // lattice that depends on vd: a lattice built with any vd serves
+    if (lattice_bytes < a.lay.off_vb0) return PLATTICE_ERR_WORKSPACE;
     if (ws_bytes < a.lay.rows_bytes) return PLATTICE_ERR_WORKSPACE;
     const int rc = poll_earlier(call);
     if (rc != PLATTICE_OK) return rc;
@@ -433,7 +436,7 @@ int plattice_feature_grad(float* grad_features_out, const float* grad, const flo
         return PLATTICE_ERR_INVALID;
     pl::CallArgs a = {};
     pl_layout(&a.lay, h, w, pd, vd);
-    if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
+    if (lattice_bytes < a.lay.off_vb0) return PLATTICE_ERR_WORKSPACE;
     const FgradWs W = fgrad_ws(a.lay);
     if (ws_bytes < W.total) return PLATTICE_ERR_WORKSPACE;
     rc = poll_earlier("plattice_feature_grad");

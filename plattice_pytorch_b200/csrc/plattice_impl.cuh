@@ -23,13 +23,14 @@ struct CallArgs {
     PlLayout lay;
     cudaStream_t stream;
     int sm_count;
-    int lattice_state;       // backward: 0 rebuild, 1 or 2 reuse the lattice
+    int lattice_state;       // backward: 0 rebuild, 1 reuse (rows zeroed by the forward), 2 reuse (re-zero)
     int cap_override_log2;
     int filter_min_log2;     // 0: the default (tables of 2^22 cells and more)
     int blur_flags;          // kBlurHalf (bfloat16 rows of large lattices), kBlurStream (tests)
-    float* v0;               // lattice value rows of the call's blur (ping-pong) and
-    float* v1;               // their bookkeeping: the scratch's front part, or a
-    uint8_t* bstate;         // kept-lattice call's workspace
+    float* v0;               // lattice value rows of the call's blur (ping-pong; the splat
+    float* v1;               // accumulates into v0) and their bookkeeping: the scratch's
+    uint8_t* bstate;         // front part (a backward's v0: the lattice's vb0), or a
+                             // kept-lattice call's workspace
     // feature gradient: dL/dout, the forward's out, and lattice rows / flags in the workspace
     const float* grad_in;
     const float* out_in;
@@ -68,6 +69,9 @@ inline ScrView scr_view(void* base, const PlLayout& L) {
     v.vkeys = reinterpret_cast<uint4*>(b + L.off_vkeys);
     return v;
 }
+
+// The lattice's rows for the first backward.
+inline float* lattice_vb0(const CallArgs& a) { return reinterpret_cast<float*>(static_cast<char*>(a.lattice) + a.lay.off_vb0); }
 
 // The value rows of a call in the front part of a scratch buffer.
 inline void rows_in_scratch(CallArgs& a, void* scratch) {
@@ -146,11 +150,12 @@ cudaError_t blur_attr(int* per_sm) {
 }
 
 // Build the lattice: tile dedup (which also zeroes the lattice value rows
-// `zero` of cp floats each), table clear, global insert, vertex ids.  Blur
-// neighbours follow, alongside the first splat (neighbors_alongside).
+// `zero` of cp floats each, and `zero_b` of cpb floats when set), table clear,
+// global insert, vertex ids.  Blur neighbours follow, alongside the first
+// splat.
 template <int PD>
 cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv, float* zero,
-                          int cp) {
+                          int cp, float* zero_b = nullptr, int cpb = 0) {
     using C = Cfg<PD>;
     const cudaStream_t s = a.stream;
     const int grid = a.sm_count * 8;
@@ -161,7 +166,7 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     const EmbedConsts ec = embed_consts(PD);
     PL_LAUNCH(STAGE_TILE_BUILD, s,
               e = launch_k(k_tile_build<PD>, dim3(a.lay.tiles), dim3(C::P), tile_build_smem_bytes<PD>(), s, false,
-                             a.features, geo, ec, Lv, Sv, zero, cp));
+                             a.features, geo, ec, Lv, Sv, zero, cp, zero_b, cpb));
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_CLEAR, s, e = launch_k(k_clear, dim3(grid), dim3(256), 0, s, false, geo, Lv, Sv));
     if (e != cudaSuccess) return e;
@@ -228,11 +233,12 @@ cudaError_t splat_zeroed(const CallArgs& a, const Geo& geo, const LatView& Lv, c
 
 template <int PD, int V>
 cudaError_t forward_v(const CallArgs& a) {
-    constexpr int CPF = pad_ch(V + 1);
+    constexpr int CPF = pad_ch(V + 1), CPB = pad_ch(V);
     const Geo geo = make_geo(a);
     const LatView Lv = lat_view(a.lattice, a.lay);
     const ScrView Sv = scr_view(a.scratch, a.lay);
-    cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPF);
+    // zeroes the forward's rows and the lattice's rows for the first backward
+    cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPF, lattice_vb0(a), CPB);
     if (e != cudaSuccess) return e;
     // neighbour lookups (L2-latency-bound) alongside the splat (HBM-bound)
     e = splat_with_neighbors<PD, V, true>(a, geo, Lv, Sv, a.values, nullptr, a.v0, STAGE_SPLAT_FWD);
@@ -258,7 +264,11 @@ cudaError_t backward_v(const CallArgs& a) {
         e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPB);
         if (e != cudaSuccess) return e;
         e = splat_with_neighbors<PD, V, false>(a, geo, Lv, Sv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
-    } else {   // zero the rows and splat in one launch
+    } else if (a.lattice_state == 1) {   // rows zeroed by the forward's tile build
+        PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
+                  e = launch_k(k_splat<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                               a.values, a.weight_in, geo, Lv, Sv, 0, a.v0));
+    } else {   // used by an earlier backward: zero the rows and splat in one launch
         e = splat_zeroed<PD, V, false>(a, geo, Lv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
     }
     if (e != cudaSuccess) return e;

@@ -524,7 +524,7 @@ __host__ __device__ constexpr int tile_build_ctas_per_sm() {
 template <int PD>
 __global__ void __launch_bounds__(Cfg<PD>::P, tile_build_ctas_per_sm<PD>())
 k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L, ScrView S,
-             float* zero_f, int cpf) {
+             float* zero_f, int cpf, float* zero_b, int cpb) {
     using C = Cfg<PD>;
     constexpr int K = C::K, P = C::P, CW = C::CW, NW = C::NW, SLOTS = C::SLOTS, SC = C::SC;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -703,6 +703,7 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     for (int i = t; 16 * i < 4 * total; i += P)
         reinterpret_cast<float4*>(gws)[i] = reinterpret_cast<const float4*>(wsort)[i];
     zero_rows_block<P>(zero_f + (size_t)base * cpf, U * cpf, cpf % 4 == 0);
+    if (zero_b) zero_rows_block<P>(zero_b + (size_t)base * cpb, U * cpb, cpb % 4 == 0);
 }
 
 // ---------------------------------------------------------------- K_clear

@@ -11,7 +11,8 @@
 // different vertices (see hash_of_key in plattice_kernels.cuh), and every
 // stage runs once over all images.
 //
-// Lattice blob (kept from forward to backward; independent of vd):
+// Lattice blob (kept from forward to backward; everything before vb0 is
+// independent of vd):
 //   hdr            LatticeHeader (status word, vertex count m, staged count)
 //   tile_off/cnt   per tile: offset and length of its unique-vertex list
 //   slot_lid       [tile][K][P] uint16   local id of each (pixel, simplex corner)
@@ -24,11 +25,15 @@
 //                                        first position of splat thread t)
 //   staged_vid     [U]          int32    global vertex id of each staged key
 //   nbr            [K][m]       int2     blur neighbours (+, -) per axis, -1 absent
+//   vb0            [m][CPb]     float    the first backward's splat target: zeroed
+//                                        by the forward's tile build, so that a
+//                                        backward right after its forward needs
+//                                        no zeroing pass (CPb = pad(vd))
 // Scratch blob: a front part that every call uses -- the lattice value rows
 // of its blur and their bookkeeping -- and a build part that only a call
 // which builds the lattice uses:
-//   v0, v1         [m][CPr]     float    lattice values, ping-pong (CPr = pad(vd+1)
-//                                        rows; a backward uses pad(vd) of each)
+//   v0, v1         [m][CPf]     float    lattice values, ping-pong (CPf = pad(vd+1));
+//                                        a backward uses v1 as vb0's partner
 //   bstate         [2][slots]   uint8    blur bookkeeping of large lattices: per
 //                                        vertex, the buffer holding its row and
 //                                        its pending halvings (ping-pong)
@@ -81,7 +86,7 @@ typedef struct {
     long long slots;      /* tiles*K*P: bound on staged keys and on vertices */
     int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
     size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_slot_wsort, off_first_lid,
-        off_staged_vid, off_nbr, lattice_bytes;
+        off_staged_vid, off_nbr, off_vb0, lattice_bytes;
     size_t off_v0, off_v1, off_bstate, rows_bytes;   /* scratch front part */
     size_t off_skeys, off_table, off_filter, off_owner, off_vid_of, off_vkeys, scratch_bytes;
 } PlLayout;
@@ -113,6 +118,7 @@ static inline void pl_layout_batch(PlLayout* L, int b, int h, int w, int pd, int
     L->off_first_lid = o;  o = pl_align(o + T * (size_t)L->P * 2);
     L->off_staged_vid = o; o = pl_align(o + S * 4);
     L->off_nbr = o;        o = pl_align(o + S * L->K * 8);
+    L->off_vb0 = o;        o = pl_align(o + S * L->CPb * 4);
     L->lattice_bytes = o;
     o = 0;
     L->off_v0 = o;         o = pl_align(o + S * L->CPf * 4);

@@ -53,7 +53,7 @@ def _layout(h, w, pd, vd):
     lat, o = {}, _align(256)
     for name, sz in [("tile_off", T * 4), ("tile_cnt", T * 4), ("slot_lid", S * 2), ("slot_w", S * 4),
                      ("slot_order", S * 2), ("slot_wsort", S * 4), ("first_lid", T * P * 2), ("staged_vid", S * 4),
-                     ("nbr", S * K * 8)]:
+                     ("nbr", S * K * 8), ("vb0", S * CPb * 4)]:
         lat[name] = o
         o = _align(o + sz)
     lat_bytes, scr, o = o, {}, 0
