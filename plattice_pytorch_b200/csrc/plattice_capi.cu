@@ -157,6 +157,7 @@ static int check_dims_b(int b, int h, int w, int pd, int vd) {
     PlLayout L;
     pl_layout_batch(&L, b, h, w, pd, vd);
     if (L.slots > (1ll << 29)) return PLATTICE_ERR_INVALID;
+    if (L.tiles_y > 65535 || b > 65535) return PLATTICE_ERR_INVALID;   // per-tile grids (x, y, image)
     return PLATTICE_OK;
 }
 

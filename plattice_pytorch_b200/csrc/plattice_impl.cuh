@@ -93,6 +93,11 @@ inline EmbedConsts embed_consts(int pd) {
     return ec;
 }
 
+// Grid of the per-tile kernels: one CTA per tile, (tiles_x, tiles_y, images).
+inline dim3 tile_grid(const CallArgs& a) {
+    return dim3((unsigned)a.lay.tiles_x, (unsigned)a.lay.tiles_y, (unsigned)a.lay.b);
+}
+
 inline Geo make_geo(const CallArgs& a) {
     Geo g;
     g.h = a.lay.h; g.w = a.lay.w; g.tiles_x = a.lay.tiles_x; g.tiles = a.lay.tiles;
@@ -165,7 +170,7 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     if (e != cudaSuccess) return e;
     const EmbedConsts ec = embed_consts(PD);
     PL_LAUNCH(STAGE_TILE_BUILD, s,
-              e = launch_k(k_tile_build<PD>, dim3(a.lay.tiles), dim3(C::P), tile_build_smem_bytes<PD>(), s, false,
+              e = launch_k(k_tile_build<PD>, tile_grid(a), dim3(C::P), tile_build_smem_bytes<PD>(), s, false,
                              a.features, geo, ec, Lv, Sv, zero, cp, zero_b, cpb));
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_CLEAR, s, e = launch_k(k_clear, dim3(grid), dim3(256), 0, s, false, geo, Lv, Sv));
@@ -247,7 +252,7 @@ cudaError_t forward_v(const CallArgs& a) {
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
-              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
+              e = launch_k(k_slice<PD, V, true>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream,
                            false, a.out, a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot,
                            a.st.seq));
     return e;
@@ -266,7 +271,7 @@ cudaError_t backward_v(const CallArgs& a) {
         e = splat_with_neighbors<PD, V, false>(a, geo, Lv, Sv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
     } else if (a.lattice_state == 1) {   // rows zeroed by the forward's tile build
         PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
-                  e = launch_k(k_splat<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false,
+                  e = launch_k(k_splat<PD, V, false>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false,
                                a.values, a.weight_in, geo, Lv, Sv, 0, a.v0));
     } else {   // used by an earlier backward: zero the rows and splat in one launch
         e = splat_zeroed<PD, V, false>(a, geo, Lv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
@@ -276,7 +281,7 @@ cudaError_t backward_v(const CallArgs& a) {
     e = launch_blur_all<PD, CPB>(a, Lv, a.v0, a.v1, 1);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
-              e = launch_k(k_slice<PD, V, false>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
+              e = launch_k(k_slice<PD, V, false>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream,
                            false, a.out, (float*)nullptr, geo, Lv, (const float*)a.v0, (const float*)a.v1,
                            a.st.slot, a.st.seq));
     return e;
@@ -294,7 +299,7 @@ cudaError_t filter_v(const CallArgs& a) {
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
-              e = launch_k(k_slice<PD, V, true>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.out,
+              e = launch_k(k_slice<PD, V, true>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false, a.out,
                            a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot, a.st.seq));
     return e;
 }
@@ -322,7 +327,7 @@ cudaError_t fgrad_v(const CallArgs& a) {
     if (e != cudaSuccess) return e;
     e = launch_blur_all<PD, CPF>(a, Lv, a.hbuf0, a.hbuf1, 1, a.flags + 1);
     if (e != cudaSuccess) return e;
-    return launch_k(k_fgrad<PD, V>, dim3(a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream, false, a.out, a.features,
+    return launch_k(k_fgrad<PD, V>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false, a.out, a.features,
                     a.values, a.grad_in, a.out_in, a.weight_in, geo, embed_consts(PD), Lv, (const float*)a.v0,
                     (const float*)a.v1, (const float*)a.hbuf0, (const float*)a.hbuf1, (const int*)a.flags,
                     a.st.slot, a.st.seq);

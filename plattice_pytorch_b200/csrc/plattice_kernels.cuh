@@ -72,6 +72,19 @@ struct TilePos {
     long long pix0;   // index of pixel (x0, y0) in the [b][h][w] pixel array
 };
 
+// The tile of a CTA in a grid of (tiles_x, tiles_y, images) blocks: no
+// divisions; *tile receives the linear tile index.
+template <int TW, int TH>
+__device__ __forceinline__ TilePos tile_pos_grid(const Geo& g, int* tile) {
+    TilePos t;
+    t.img = blockIdx.z;
+    t.x0 = blockIdx.x * TW;
+    t.y0 = blockIdx.y * TH;
+    t.pix0 = (long long)t.img * g.n_img + (long long)t.y0 * g.w + t.x0;
+    *tile = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+    return t;
+}
+
 template <int TW, int TH>
 __device__ __forceinline__ TilePos tile_pos(const Geo& g, int tile) {
     TilePos t;
@@ -343,7 +356,7 @@ __device__ __forceinline__ int f2s16(float x) {
 // thread's column (stride P) of 2K ints of shared scratch.
 template <int PD>
 __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& ec, int (&g)[PD + 1],
-                                      int (&rank)[PD + 1], float (&bary)[PD + 1], int* col) {
+                                      int (&rank)[PD + 1], float (&bary)[PD + 1], int* col, int (&ir)[PD + 1]) {
     constexpr int P = Cfg<PD>::P;
     constexpr int K = PD + 1;
     float e[K];
@@ -369,17 +382,26 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
         sum += g[i];
     }
     sum = (int16_t)((int16_t)sum / K);
+    // |sum| <= K/2 for finite features within the int16 key range; the clamp
+    // only keeps NaN or saturated coordinates (no defined result) from moving
+    // ranks outside [0, K)
+    sum = sum > PD ? PD : (sum < -PD ? -PD : sum);
 
-    // rank by counting, ties to the lower index
+    // rank by counting, ties to the lower index: of each pair i < j, i
+    // outranks j when d[i] < d[j], else j outranks i (one comparison per pair)
     float d[K];
 #pragma unroll
     for (int i = 0; i < K; ++i) d[i] = __fsub_rn(e[i], (float)g[i]);
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
-        int r = 0;
+    for (int i = 0; i < K; ++i) rank[i] = 0;
 #pragma unroll
-        for (int j = 0; j < K; ++j) r += (d[i] < d[j] || (d[i] == d[j] && i > j)) ? 1 : 0;
-        rank[i] = r;
+    for (int i = 0; i < K; ++i) {
+#pragma unroll
+        for (int j = i + 1; j < K; ++j) {
+            const int lt = d[i] < d[j] ? 1 : 0;
+            rank[i] += lt;
+            rank[j] += 1 - lt;
+        }
     }
 
     // move the greedy point onto the hyperplane, without branches: for sum > 0
@@ -410,7 +432,6 @@ __device__ __forceinline__ void embed(const float (&f)[PD], const EmbedConsts& e
         col[(K + rank[i]) * P] = i;
     }
     float dr[K];
-    int ir[K];
 #pragma unroll
     for (int r = 0; r < K; ++r) {
         dr[r] = __int_as_float(col[r * P]);
@@ -534,8 +555,8 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     __shared__ int s_count, s_base;
 
     const int t = threadIdx.x, lane = t & 31;
-    const int tile = blockIdx.x;
-    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
+    int tile;
+    const TilePos tp = tile_pos_grid<C::TW, C::TH>(geo, &tile);
     const int x = tp.x0 + (t % C::TW);
     const int y = tp.y0 + (t / C::TW);
     const bool active = x < geo.w && y < geo.h;
@@ -547,18 +568,50 @@ k_tile_build(const float* __restrict__ feat, Geo geo, EmbedConsts ec, LatView L,
     float f[PD];
 #pragma unroll
     for (int i = 0; i < PD; ++i) f[i] = active ? __ldg(feat + p * PD + i) : 0.0f;
-    int g[K], rank[K];
+    int g[K], rank[K], ir[K];
     float bary[K];
     static_assert(2 * K * P <= SC, "embed scratch must fit in the tile table");
-    embed<PD>(f, ec, g, rank, bary, stab + t);
+    embed<PD>(f, ec, g, rank, bary, stab + t, ir);
     // the tile table: entries t + j*P are this thread's own scratch column
     for (int i = t; i < SC; i += P) stab[i] = -1;
 
-    // 2a. candidate key records (visible to other lanes' CAS winners after the fence)
+    // 2a. candidate key records (visible to other lanes' CAS winners after the
+    // barrier).  Corner 0 is the remainder-0 point g; corner c is corner c-1
+    // plus one on every coordinate and minus K on the coordinate of rank
+    // PD-c+1 (the corners of permutohedral.cu:238-244), so its words and the
+    // linear part of its hash are updated, not rebuilt.  A point within 2K of
+    // the int16 limits may wrap a coordinate: its keys are built from scratch.
+    bool near_edge = false;
+#pragma unroll
+    for (int i = 0; i < PD; ++i) near_edge = near_edge || g[i] > 32767 - 2 * K || g[i] < -32768 + 2 * K;
+    uint32_t kw[NW];
+    uint32_t lin = salt;
+#pragma unroll
+    for (int k = 0; k < NW; ++k) kw[k] = 0u;
+#pragma unroll
+    for (int i = 0; i < PD; ++i) {
+        kw[1 + i / 2] |= ((uint32_t)(uint16_t)(int16_t)g[i]) << (16 * (i & 1));
+        lin += (uint32_t)g[i] * coord_mul(i);
+    }
 #pragma unroll
     for (int c = 0; c < K; ++c) {
-        uint32_t kw[NW];
-        make_key<PD>(g, rank, c, salt, kw);
+        if (near_edge) {
+            make_key<PD>(g, rank, c, salt, kw);
+        } else {
+            if (c > 0) {
+                const int j = ir[PD + 1 - c];
+#pragma unroll
+                for (int k = 1; k <= 1 + (PD - 1) / 2; ++k) {   // the words that hold coordinates
+                    const int lo = 2 * (k - 1), hi = lo + 1;
+                    const int dlo = 1 - (j == lo ? K : 0);
+                    const int dhi = hi < PD ? 1 - (j == hi ? K : 0) : 0;
+                    kw[k] = hw_add(kw[k], pack_hw(dlo, dhi));
+                }
+                // (coordinate PD is implied by the others and not part of the key)
+                lin += coord_mul_sum(PD) - (j < PD ? (uint32_t)K * c_coord_mul[j] : 0u);
+            }
+            kw[0] = hash_of_lin(lin);
+        }
         if (active) {
 #pragma unroll
             for (int w = 0; w < CW; ++w)
@@ -1218,7 +1271,7 @@ struct WorkerSync {
 };
 
 template <int PD, int V, bool FWD, typename Sync>
-__device__ __forceinline__ void splat_tile(int tile, int t, const float* __restrict__ vals,
+__device__ __forceinline__ void splat_tile(int tile, const TilePos& tp, int t, const float* __restrict__ vals,
                                            const float* __restrict__ wt, const Geo& geo, const LatView& L,
                                            const ScrView& S, int resolve, float* lat,
                                            SplatSmem<PD, FWD ? V + 1 : V>& sm, Sync sync) {
@@ -1229,7 +1282,6 @@ __device__ __forceinline__ void splat_tile(int tile, int t, const float* __restr
     constexpr int NV4 = (NC + 3) / 4;            // float4 per pixel value row
     int* svid = sm.svid;
     float4* pv = sm.pv;
-    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
     const int x0 = tp.x0, y0 = tp.y0;
     const int nx = min(C::TW, geo.w - x0), ny = min(C::TH, geo.h - y0);
     const int total = nx * ny * K;
@@ -1373,7 +1425,9 @@ __global__ void __launch_bounds__(Cfg<PD>::P)
 k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, ScrView S,
         int resolve, float* lat) {
     __shared__ SplatSmem<PD, FWD ? V + 1 : V> sm;
-    splat_tile<PD, V, FWD>(blockIdx.x, threadIdx.x, vals, wt, geo, L, S, resolve, lat, sm, CtaSync{});
+    int tile;
+    const TilePos tp = tile_pos_grid<Cfg<PD>::TW, Cfg<PD>::TH>(geo, &tile);
+    splat_tile<PD, V, FWD>(tile, tp, threadIdx.x, vals, wt, geo, L, S, resolve, lat, sm, CtaSync{});
 }
 
 // The splat right after a lattice build, together with the blur-neighbour
@@ -1393,8 +1447,11 @@ k_splat_nbr(const float* __restrict__ vals, const float* __restrict__ wt, Geo ge
     if ((int)blockIdx.x < nbr_blocks)
         neighbors_grid<PD>(geo, L, S, blockIdx.x * blockDim.x + threadIdx.x, nbr_blocks * blockDim.x,
                            &sm.nb[threadIdx.x >> 5]);
-    else
-        splat_tile<PD, V, FWD>(blockIdx.x - nbr_blocks, threadIdx.x, vals, wt, geo, L, S, 1, lat, sm.sp, CtaSync{});
+    else {
+        const int tile = blockIdx.x - nbr_blocks;
+        splat_tile<PD, V, FWD>(tile, tile_pos<Cfg<PD>::TW, Cfg<PD>::TH>(geo, tile), threadIdx.x, vals, wt, geo, L, S,
+                               1, lat, sm.sp, CtaSync{});
+    }
 }
 
 // The splat of a call on a kept lattice, whose value rows must start at zero:
@@ -1418,7 +1475,8 @@ k_splat_zeroed(const float* __restrict__ vals, const float* __restrict__ wt, Geo
     }
     grid_barrier(L.hdr, phase);
     for (int tile = blockIdx.x; tile < geo.tiles; tile += gridDim.x)
-        splat_tile<PD, V, FWD>(tile, threadIdx.x, vals, wt, geo, L, ScrView{}, 0, lat, sm, CtaSync{});
+        splat_tile<PD, V, FWD>(tile, tile_pos<Cfg<PD>::TW, Cfg<PD>::TH>(geo, tile), threadIdx.x, vals, wt, geo, L,
+                               ScrView{}, 0, lat, sm, CtaSync{});
     grid_exit(L.hdr, nullptr, 0u);
 }
 
@@ -1826,8 +1884,9 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
     constexpr int NC = FWD ? V + 1 : V;
     report_status(st_slot, st_seq, L.hdr);
     const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
-    const int t = threadIdx.x, tile = blockIdx.x;
-    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
+    const int t = threadIdx.x;
+    int tile;
+    const TilePos tp = tile_pos_grid<C::TW, C::TH>(geo, &tile);
     const bool act = tp.x0 + (t % C::TW) < geo.w && tp.y0 + (t / C::TW) < geo.h;
     const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
     int vid[K];
@@ -1907,8 +1966,9 @@ k_fgrad(float* __restrict__ gfeat, const float* __restrict__ feat, const float* 
     __shared__ int scol[2 * K * P];   // embed scratch, then dL/dw by corner; column t per thread
     const float* __restrict__ R = flags[0] ? R1 : R0;
     const float* __restrict__ H = flags[1] ? H1 : H0;
-    const int t = threadIdx.x, tile = blockIdx.x;
-    const TilePos tp = tile_pos<C::TW, C::TH>(geo, tile);
+    const int t = threadIdx.x;
+    int tile;
+    const TilePos tp = tile_pos_grid<C::TW, C::TH>(geo, &tile);
     const int x = tp.x0 + (t % C::TW);
     const int y = tp.y0 + (t / C::TW);
     const bool act = x < geo.w && y < geo.h;
@@ -1928,7 +1988,8 @@ k_fgrad(float* __restrict__ gfeat, const float* __restrict__ feat, const float* 
     for (int i = 0; i < PD; ++i) f[i] = act ? __ldg(feat + p * PD + i) : 0.0f;
     int g[K], rank[K];
     float bary[K];
-    embed<PD>(f, ec, g, rank, bary, scol + t);
+    int ir[K];
+    embed<PD>(f, ec, g, rank, bary, scol + t, ir);
     __syncthreads();
     if (!act) return;
     float G[V], vv[V];
