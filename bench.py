@@ -478,6 +478,21 @@ def traffic_from_profiles(kernel):
     return None
 
 
+def atomics_from_profiles():
+    """ncu reduction / CAS request counts per launch recorded in profiles/atomics.txt."""
+    path = os.path.join(ROOT, "profiles", "atomics.txt")
+    out = {}
+    try:
+        with open(path) as fh:
+            for line in fh:
+                parts = line.split()
+                if len(parts) >= 2 and not line.startswith("#"):
+                    out[parts[0]] = int(parts[1])
+    except OSError:
+        pass
+    return out
+
+
 def cpu_baseline(f_np, v_np, g_np, sample):
     """The brute-force dense Gaussian (oracle port of the reference test's
     brute_force_bilateral, generalised) on `sample` output pixels forward and
@@ -703,6 +718,12 @@ def main():
             "frac_all_kernels": (b_fwd + b_bwd) / (all_ms * 1e-3) / 1e9 / peak}
         res["stages"] = per_stage
         res["lattice"] = {"m": m, "u_total": u, "cap_log2": cap}
+        K = pd + 1
+        res["atomics"] = {
+            "reference_scalar_atomics_fwd": n * K * (vd + 1),   # permutohedral.cu:316-318, one per slot and channel
+            "reference_scalar_atomics_bwd": n * K * vd,
+            "measured": atomics_from_profiles() if args.workload == "voronoi1024_pd5_vd3" else {},
+            "measured_source": "profiles/atomics.txt (ncu, one launch each, this workload)"}
         res["gpu_launches"] = int(round(launches_per_step * args.steps * launch_mult))
 
     if rank == 0 and world_eff == 1 and not args.no_cpu_baseline:

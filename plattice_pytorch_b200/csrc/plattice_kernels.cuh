@@ -50,6 +50,12 @@ template <int PD> struct Cfg {
 
 __host__ __device__ constexpr int pad_ch(int c) { return c <= 2 ? c : ((c + 3) / 4) * 4; }
 
+// Blocks per SM a per-tile kernel asks the compiler for: full occupancy (32
+// registers) for the small feature and value dimensions, where the kernels
+// fit in them without spilling; the compiler's choice otherwise.
+template <int PD, int V>
+__host__ __device__ constexpr int slice_min_blocks() { return (PD <= 7 && V <= 4) ? 2048 / Cfg<PD>::P : 1; }
+
 struct EmbedConsts {
     float sf[PL_MAX_PD];   // scale factors, permutohedral.cu:507-508 (computed on the host)
     float rk;              // 1/K rounded to float
@@ -1437,7 +1443,7 @@ k_splat(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, L
 // order, so the latency-bound lookups start first and the bandwidth-bound
 // tiles fill the SMs around them.
 template <int PD, int V, bool FWD>
-__global__ void __launch_bounds__(Cfg<PD>::P)
+__global__ void __launch_bounds__(Cfg<PD>::P, slice_min_blocks<PD, V>())
 k_splat_nbr(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, ScrView S, float* lat,
             int nbr_blocks) {
     __shared__ union {
@@ -1870,10 +1876,6 @@ __device__ __forceinline__ void report_status(unsigned long long* slot, unsigned
 // vertex ids through L1 (the tile's few hundred staged ids are shared by its
 // 256 pixels), then the K rows: no shared-memory stage and no barrier, so
 // every warp proceeds on its own.
-// full occupancy (32 registers) where the slice fits in them without spilling much
-template <int PD, int V>
-__host__ __device__ constexpr int slice_min_blocks() { return (PD <= 7 && V <= 4) ? 2048 / Cfg<PD>::P : 1; }
-
 template <int PD, int V, bool FWD>
 __global__ void __launch_bounds__(Cfg<PD>::P, slice_min_blocks<PD, V>())
 k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
