@@ -29,10 +29,10 @@
  * plattice_workspace_sizes:
  *   lattice  -- the built lattice; kept from a forward call to the backward
  *               calls that reuse it (its size does not depend on vd).
- *   scratch  -- transient; only needed during a call.  A call on a kept
- *               lattice (a backward that reuses it, plattice_filter*) needs
- *               only its front part, plattice_reuse_scratch_size bytes: the
- *               lattice value rows of the call's blur.
+ *   scratch  -- transient; only needed during a call.  A backward that
+ *               reuses a kept lattice needs only its first
+ *               plattice_reuse_scratch_size bytes (one value-row buffer of its
+ *               blur and the blur's bookkeeping).
  * Calls that overlap in time must not share either buffer.
  */
 #ifndef PLATTICE_H
@@ -75,10 +75,9 @@ const char* plattice_last_error_detail(void);
 int plattice_workspace_sizes(int h, int w, int pd, int vd, size_t* lattice_bytes,
                              size_t* scratch_bytes);
 
-/* Bytes of scratch that a call on a kept lattice of b images needs (a
- * backward with lattice_state 1 or 2, plattice_filter, plattice_filter_backward):
- * the front part of the full scratch.  No reference counterpart (the
- * reference rebuilds, permutohedral.cu:615-635). */
+/* Bytes of scratch that a backward reusing a kept lattice of b images needs
+ * (lattice_state 1 or 2): the front part of the full scratch.  No reference
+ * counterpart (the reference rebuilds, permutohedral.cu:615-635). */
 int plattice_reuse_scratch_size(int b, int h, int w, int pd, int vd, size_t* bytes);
 
 /* Forward filter: builds the lattice of `features` into `lattice`, splats
@@ -135,9 +134,8 @@ int plattice_backward_batch(float* grad_values_out, const float* grad, const flo
  * plattice_filter_backward: the value gradient of such a call, given its
  * weight_out as weight_in (same result as plattice_backward).
  * `values_ws` holds the lattice value rows of the call
- * (plattice_filter_workspace_size bytes, which equals
- * plattice_reuse_scratch_size for one image; any allocator, reusable across
- * calls).  A lattice serves every vd.
+ * (plattice_filter_workspace_size bytes; any allocator, reusable across
+ * calls).  A lattice built with any vd serves every vd.
  * Both calls update bookkeeping in the lattice header, so calls on one
  * lattice must be issued one after the other (one stream). */
 int plattice_filter_workspace_size(int h, int w, int pd, int vd, size_t* bytes);

@@ -92,6 +92,17 @@ def _sizes(b, h, w, pd, vd):
     return s
 
 
+_FILTER_WS = {}
+
+
+def _filter_ws(h, w, pd, vd):
+    key = (h, w, pd, vd)
+    b = _FILTER_WS.get(key)
+    if b is None:
+        b = _FILTER_WS[key] = _lib.filter_workspace_size(h, w, pd, vd)
+    return b
+
+
 def _call(dev_index, fn, *args):
     """Library call with `dev_index` the current device (kernels launch on its stream)."""
     if _cur_dev() == dev_index:
@@ -272,7 +283,7 @@ def lattice_filter(lattice, values):
     h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
     out = torch.empty((h, w, vd), dtype=_F32, device=dev)
     weight = torch.empty((h, w, 1), dtype=_F32, device=dev)
-    _, _, wsb = _sizes(1, h, w, pd, vd)
+    wsb = _filter_ws(h, w, pd, vd)
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     rc = _call(dev.index, _lib_h().plattice_filter, weight.data_ptr(), out.data_ptr(), values.data_ptr(),
                lattice.buf.data_ptr(), lattice.buf.numel(), ws.data_ptr(), wsb, pd, vd, w, h,
@@ -294,7 +305,7 @@ def lattice_filter_backward(lattice, grad_values, weight_saved):
     _require(weight_saved.dtype == torch.float32, "weight_saved must be float32")
     h, w, pd, dev = lattice.h, lattice.w, lattice.pd, lattice.device
     out = torch.empty((h, w, vd), dtype=_F32, device=dev)
-    _, _, wsb = _sizes(1, h, w, pd, vd)
+    wsb = _filter_ws(h, w, pd, vd)
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     rc = _call(dev.index, _lib_h().plattice_filter_backward, out.data_ptr(), grad_values.data_ptr(),
                weight_saved.data_ptr(), lattice.buf.data_ptr(), lattice.buf.numel(), ws.data_ptr(), wsb,

@@ -242,7 +242,7 @@ static int backward_images(float* grad_values_out, const float* grad, const floa
     pl::CallArgs a = {};
     pl_layout_batch(&a.lay, b, h, w, pd, vd);
     if (lattice_bytes < a.lay.lattice_bytes) return PLATTICE_ERR_WORKSPACE;
-    if (scratch_bytes < (lattice_state == 0 ? a.lay.scratch_bytes : a.lay.rows_bytes)) return PLATTICE_ERR_WORKSPACE;
+    if (scratch_bytes < (lattice_state == 0 ? a.lay.scratch_bytes : a.lay.reuse_bytes)) return PLATTICE_ERR_WORKSPACE;
     rc = poll_earlier(call);
     if (rc != PLATTICE_OK) return rc;
     a.features = features; a.values = grad; a.weight_in = weight_in;
@@ -301,7 +301,7 @@ int plattice_reuse_scratch_size(int b, int h, int w, int pd, int vd, size_t* byt
     if (b > 0 && h > 0 && w > 0) {
         PlLayout L;
         pl_layout_batch(&L, b, h, w, pd, vd);
-        *bytes = L.rows_bytes;
+        *bytes = L.reuse_bytes;
     }
     return PLATTICE_OK;
 }
@@ -337,7 +337,16 @@ int plattice_backward_batch(float* grad_values_out, const float* grad, const flo
 // ---------------------------------------------------------------- kept lattice
 
 int plattice_filter_workspace_size(int h, int w, int pd, int vd, size_t* bytes) {
-    return plattice_reuse_scratch_size(1, h, w, pd, vd, bytes);
+    const int rc = check_dims(h, w, pd, vd);
+    if (rc != PLATTICE_OK) return rc;
+    if (!bytes) return PLATTICE_ERR_INVALID;
+    *bytes = 256;
+    if (h > 0 && w > 0) {
+        PlLayout L;
+        pl_layout(&L, h, w, pd, vd);
+        *bytes = L.rows_bytes;   // both value-row buffers and the blur's bookkeeping
+    }
+    return PLATTICE_OK;
 }
 
 // The checks shared by the two kept-lattice calls; fills the layout and the

@@ -1758,73 +1758,6 @@ __device__ __forceinline__ float* blur_resident(const LatView& L, float* buf0, f
     return x;
 }
 
-// The resident blur for rows of 4 channels and K <= 8: every neighbour
-// index the K passes need -- the vertex's own along each axis and, per pair
-// of passes, the first axis's neighbours of the second axis's neighbours --
-// is loaded at the start, so that each pair of passes costs one round of row
-// loads and one grid barrier.  Same vertex ranges, pairs and float operations
-// as blur_resident.
-template <int PD, int CP>
-__device__ __forceinline__ float* blur_resident_pf(const LatView& L, float* buf0, float* buf1, int reverse, int M,
-                                                   unsigned& phase) {
-    constexpr int K = PD + 1;
-    constexpr int NP = (K + 1) / 2;            // pairs (the last one may be a single pass)
-    constexpr int W = CP < 4 ? CP : 4;
-    const int G = gridDim.x;
-    const int vb = (int)((long long)M * blockIdx.x / G), ve = (int)((long long)M * (blockIdx.x + 1) / G);
-    const int v = vb + threadIdx.x;
-    const bool mine = v < ve;
-    float* x = buf0;
-    float* y = buf1;
-    int2 nb[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k) nb[k] = nbr_at(L.nbr, M, reverse ? K - 1 - k : k, mine ? v : -1);
-    float me[CP];
-    if (mine) load_row_cg<CP>(x + (size_t)v * CP, me);
-    int2 ha[NP], hb[NP];   // pair p: neighbours along axis 2p of the axis-(2p+1) neighbours
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-        if (2 * p + 1 < K) {
-            const int ax = reverse ? K - 1 - 2 * p : 2 * p;
-            ha[p] = nbr_at(L.nbr, M, ax, nb[2 * p + 1].x);
-            hb[p] = nbr_at(L.nbr, M, ax, nb[2 * p + 1].y);
-        } else {
-            ha[p] = hb[p] = make_int2(-1, -1);
-        }
-    }
-#pragma unroll
-    for (int p = 0; p < NP; ++p) {
-        const int k = 2 * p;
-        const bool pair = k + 1 < K;
-        if (mine) {
-#pragma unroll
-            for (int c0 = 0; c0 < CP; c0 += W) {
-                const float* xc = x + c0;
-                float mi[W], a[W], b[W], o[W];
-#pragma unroll
-                for (int j = 0; j < W; ++j) mi[j] = me[c0 + j];
-                if (nb[k].x >= 0) load_row_cg<W>(xc + (size_t)nb[k].x * CP, a);
-                if (nb[k].y >= 0) load_row_cg<W>(xc + (size_t)nb[k].y * CP, b);
-                blur_row<W>(mi, a, b, nb[k], o);
-                if (pair) {
-                    float pa[W], pb[W], q[W];
-                    if (nb[k + 1].x >= 0) blur_at<W, CP>(xc, nb[k + 1].x, ha[p], pa);
-                    if (nb[k + 1].y >= 0) blur_at<W, CP>(xc, nb[k + 1].y, hb[p], pb);
-                    blur_row<W>(o, pa, pb, nb[k + 1], q);
-#pragma unroll
-                    for (int j = 0; j < W; ++j) o[j] = q[j];
-                }
-                store_row<W>(y + (size_t)v * CP + c0, o);
-#pragma unroll
-                for (int j = 0; j < W; ++j) me[c0 + j] = o[j];
-            }
-        }
-        float* t = x; x = y; y = t;
-        if (p + 1 < NP) grid_barrier(L.hdr, phase);
-    }
-    return x;
-}
-
 template <int CP>
 __device__ __forceinline__ bool blur_fits_resident(int M, int threads) {
     return M <= threads * (CP <= 2 ? 2 : 1);
@@ -1839,9 +1772,7 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
     unsigned phase = 0;
     if (blur_fits_resident<CP>(M, stride) && !(flags & kBlurStream)) {
-        float* res;
-        if constexpr (CP == 4 && PD + 1 <= 8) res = blur_resident_pf<PD, CP>(L, buf0, buf1, reverse, M, phase);
-        else res = blur_resident<PD, CP>(L, buf0, buf1, reverse, M, phase);
+        float* res = blur_resident<PD, CP>(L, buf0, buf1, reverse, M, phase);
         if (tid == 0) *final_flag = (res == buf1) ? 1 : 0;
     } else if (flags & kBlurHalf) {
         blur_streaming<PD, CP, true>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride,

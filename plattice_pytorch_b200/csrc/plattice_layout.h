@@ -32,11 +32,13 @@
 // Scratch blob: a front part that every call uses -- the lattice value rows
 // of its blur and their bookkeeping -- and a build part that only a call
 // which builds the lattice uses:
-//   v0, v1         [m][CPf]     float    lattice values, ping-pong (CPf = pad(vd+1));
-//                                        a backward uses v1 as vb0's partner
+//   v1             [m][CPf]     float    lattice values, the ping-pong partner of
+//                                        v0 (forward) or of vb0 (backward)
 //   bstate         [2][slots]   uint8    blur bookkeeping of large lattices: per
 //                                        vertex, the buffer holding its row and
 //                                        its pending halvings (ping-pong)
+//   v0             [m][CPf]     float    the forward's splat target (CPf = pad(vd+1))
+// (a backward on a kept lattice needs only v1 and bstate: reuse_bytes)
 //   -- build part --
 //   staged_keys    [U][CW]      uint4    each tile's unique keys (word 0: hash)
 //   table          [cap]        uint32   open-addressed hash table: 0 empty, else
@@ -87,7 +89,7 @@ typedef struct {
     int cap_max_log2;     /* table cells allocated = 2^cap_max_log2 >= 2*slots */
     size_t off_tile_off, off_tile_cnt, off_slot_lid, off_slot_w, off_slot_order, off_slot_wsort, off_first_lid,
         off_staged_vid, off_nbr, off_vb0, lattice_bytes;
-    size_t off_v0, off_v1, off_bstate, rows_bytes;   /* scratch front part */
+    size_t off_v0, off_v1, off_bstate, reuse_bytes, rows_bytes;   /* scratch front part */
     size_t off_skeys, off_table, off_filter, off_owner, off_vid_of, off_vkeys, scratch_bytes;
 } PlLayout;
 
@@ -121,9 +123,10 @@ static inline void pl_layout_batch(PlLayout* L, int b, int h, int w, int pd, int
     L->off_vb0 = o;        o = pl_align(o + S * L->CPb * 4);
     L->lattice_bytes = o;
     o = 0;
-    L->off_v0 = o;         o = pl_align(o + S * L->CPf * 4);
     L->off_v1 = o;         o = pl_align(o + S * L->CPf * 4);
     L->off_bstate = o;     o = pl_align(o + 2 * S);
+    L->reuse_bytes = o;
+    L->off_v0 = o;         o = pl_align(o + S * L->CPf * 4);
     L->rows_bytes = o;
     L->off_skeys = o;      o = pl_align(o + S * L->CW * 16);
     L->off_table = o;      o = pl_align(o + ((size_t)1 << lg) * 4);

@@ -57,8 +57,8 @@ def _layout(h, w, pd, vd):
         lat[name] = o
         o = _align(o + sz)
     lat_bytes, scr, o = o, {}, 0
-    # scratch: the value rows (front part), then the build part
-    for name, sz in [("v0", S * CPf * 4), ("v1", S * CPf * 4), ("bstate", 2 * S),
+    # scratch: the value rows and the blur's bookkeeping (front part), then the build part
+    for name, sz in [("v1", S * CPf * 4), ("bstate", 2 * S), ("v0", S * CPf * 4),
                      ("skeys", S * CW * 16), ("table", (1 << lg) * 4), ("filter", 1 << lg), ("owner", S * 4),
                      ("vid_of", S * 4), ("vkeys", S * CW * 16)]:
         scr[name] = o
