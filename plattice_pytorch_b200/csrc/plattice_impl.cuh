@@ -236,6 +236,43 @@ cudaError_t splat_zeroed(const CallArgs& a, const Geo& geo, const LatView& Lv, c
     return e;
 }
 
+// the streamed slice's dynamic shared memory and its co-resident CTAs per SM
+template <int PD, int V, bool FWD>
+cudaError_t slice_attr(int* per_sm) {
+    cudaError_t e = cudaFuncSetAttribute(k_slice_pipe<PD, V, FWD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         slice_pipe_smem_bytes<PD>());
+    if (e != cudaSuccess) return e;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_slice_pipe<PD, V, FWD>, Cfg<PD>::P,
+                                                      slice_pipe_smem_bytes<PD>());
+    if (e != cudaSuccess) return e;
+    return *per_sm < 1 ? cudaErrorLaunchOutOfResources : cudaSuccess;
+}
+
+// The slice (the call's last kernel: it reports the status word).  Tiles of
+// 256 pixels (pd <= 6): persistent CTAs that stream the slot records, as many
+// as are co-resident, at most one per tile; smaller tiles (whose CTAs would be
+// too small to keep an SM busy that way): one CTA per tile.
+template <int PD, int V, bool FWD>
+cudaError_t launch_slice(const CallArgs& a, const Geo& geo, const LatView& Lv, float* out, float* wout,
+                         const float* r0, const float* r1) {
+    cudaError_t e;
+    if constexpr (kSlicePiped<PD>) {
+        int per_sm = 0;
+        e = kernel_once(reinterpret_cast<const void*>(k_slice_pipe<PD, V, FWD>), slice_attr<PD, V, FWD>, &per_sm);
+        if (e != cudaSuccess) return e;
+        const int want = a.sm_count * per_sm;
+        const int grid = want < a.lay.tiles ? want : a.lay.tiles;
+        PL_LAUNCH(FWD ? STAGE_SLICE_FWD : STAGE_SLICE_BWD, a.stream,
+                  e = launch_k(k_slice_pipe<PD, V, FWD>, dim3(grid), dim3(Cfg<PD>::P), slice_pipe_smem_bytes<PD>(),
+                               a.stream, false, out, wout, geo, Lv, r0, r1, a.st.slot, a.st.seq));
+    } else {
+        PL_LAUNCH(FWD ? STAGE_SLICE_FWD : STAGE_SLICE_BWD, a.stream,
+                  e = launch_k(k_slice<PD, V, FWD>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false, out, wout,
+                               geo, Lv, r0, r1, a.st.slot, a.st.seq));
+    }
+    return e;
+}
+
 template <int PD, int V>
 cudaError_t forward_v(const CallArgs& a) {
     constexpr int CPF = pad_ch(V + 1), CPB = pad_ch(V);
@@ -251,11 +288,7 @@ cudaError_t forward_v(const CallArgs& a) {
     // blur in axis order 0..pd (permutohedral.cu:585)
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
-              e = launch_k(k_slice<PD, V, true>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream,
-                           false, a.out, a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot,
-                           a.st.seq));
-    return e;
+    return launch_slice<PD, V, true>(a, geo, Lv, a.out, a.wout, a.v0, a.v1);
 }
 
 template <int PD, int V>
@@ -280,11 +313,7 @@ cudaError_t backward_v(const CallArgs& a) {
     // blur in axis order pd..0 (permutohedral.cu:647)
     e = launch_blur_all<PD, CPB>(a, Lv, a.v0, a.v1, 1);
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_SLICE_BWD, a.stream,
-              e = launch_k(k_slice<PD, V, false>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream,
-                           false, a.out, (float*)nullptr, geo, Lv, (const float*)a.v0, (const float*)a.v1,
-                           a.st.slot, a.st.seq));
-    return e;
+    return launch_slice<PD, V, false>(a, geo, Lv, a.out, nullptr, a.v0, a.v1);
 }
 
 // Forward filter of new values on a kept lattice (built by a forward call on
@@ -298,10 +327,7 @@ cudaError_t filter_v(const CallArgs& a) {
     if (e != cudaSuccess) return e;
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_SLICE_FWD, a.stream,
-              e = launch_k(k_slice<PD, V, true>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false, a.out,
-                           a.wout, geo, Lv, (const float*)a.v0, (const float*)a.v1, a.st.slot, a.st.seq));
-    return e;
+    return launch_slice<PD, V, true>(a, geo, Lv, a.out, a.wout, a.v0, a.v1);
 }
 
 // Gradient of the forward filter with respect to the features, on a kept
@@ -348,8 +374,10 @@ cudaError_t prepare_v(const CallArgs&) {
                          reinterpret_cast<const void*>(k_insert<PD>),
                          reinterpret_cast<const void*>(k_splat_nbr<PD, V, true>),
                          reinterpret_cast<const void*>(k_splat_nbr<PD, V, false>),
-                         reinterpret_cast<const void*>(k_slice<PD, V, true>),
-                         reinterpret_cast<const void*>(k_slice<PD, V, false>),
+                         kSlicePiped<PD> ? reinterpret_cast<const void*>(k_slice_pipe<PD, V, true>)
+                                         : reinterpret_cast<const void*>(k_slice<PD, V, true>),
+                         kSlicePiped<PD> ? reinterpret_cast<const void*>(k_slice_pipe<PD, V, false>)
+                                         : reinterpret_cast<const void*>(k_slice<PD, V, false>),
                          reinterpret_cast<const void*>(k_splat_zeroed<PD, V, true>),
                          reinterpret_cast<const void*>(k_splat_zeroed<PD, V, false>)};
     for (const void* f : fns) {
@@ -357,6 +385,10 @@ cudaError_t prepare_v(const CallArgs&) {
         if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, f);
     }
     int n2 = 0;
+    if (e == cudaSuccess && kSlicePiped<PD>)
+        e = kernel_once(reinterpret_cast<const void*>(k_slice_pipe<PD, V, true>), slice_attr<PD, V, true>, &n2);
+    if (e == cudaSuccess && kSlicePiped<PD>)
+        e = kernel_once(reinterpret_cast<const void*>(k_slice_pipe<PD, V, false>), slice_attr<PD, V, false>, &n2);
     if (e == cudaSuccess)
         e = kernel_once(reinterpret_cast<const void*>(k_splat_zeroed<PD, V, true>), splat_zeroed_attr<PD, V, true>, &n2);
     if (e == cudaSuccess)

@@ -103,6 +103,43 @@ __device__ __forceinline__ TilePos tile_pos(const Geo& g, int tile) {
     return t;
 }
 
+// The tiles first, first + stride, first + 2 stride, ... of a persistent
+// CTA: (image, tile row, tile column) advanced by mixed-radix addition, one
+// division per CTA instead of two per tile.
+struct TileWalk {
+    int tx, ty, img;      // position of the current tile
+    int dx, dy, dimg;     // the stride in the same radix
+    int tiles_x, tiles_y;
+    __device__ __forceinline__ TileWalk(const Geo& g, int first, int stride) {
+        tiles_x = g.tiles_x;
+        tiles_y = g.tiles_img / g.tiles_x;
+        img = first / g.tiles_img;
+        int r = first - img * g.tiles_img;
+        ty = r / tiles_x;
+        tx = r - ty * tiles_x;
+        dimg = stride / g.tiles_img;
+        r = stride - dimg * g.tiles_img;
+        dy = r / tiles_x;
+        dx = r - dy * tiles_x;
+    }
+    __device__ __forceinline__ void advance() {
+        tx += dx;
+        ty += dy;
+        img += dimg;
+        if (tx >= tiles_x) { tx -= tiles_x; ++ty; }
+        if (ty >= tiles_y) { ty -= tiles_y; ++img; }
+    }
+    template <int TW, int TH>
+    __device__ __forceinline__ TilePos pos(const Geo& g) const {
+        TilePos t;
+        t.img = img;
+        t.x0 = tx * TW;
+        t.y0 = ty * TH;
+        t.pix0 = (long long)img * g.n_img + (long long)t.y0 * g.w + t.x0;
+        return t;
+    }
+};
+
 struct LatView {
     LatticeHeader* hdr;
     int* tile_off;
@@ -1486,6 +1523,46 @@ k_splat_zeroed(const float* __restrict__ vals, const float* __restrict__ wt, Geo
     grid_exit(L.hdr, nullptr, 0u);
 }
 
+// ---------------------------------------------------------------- bulk copies
+
+// Bulk asynchronous copies global -> shared memory (cp.async.bulk, no
+// multicast), completed on an mbarrier of the CTA with a transaction count.
+// Addresses 16-byte aligned, sizes multiples of 16 bytes.
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase of `parity` to complete: false (and the status
+// bit PL_ST_SPIN recorded) when it has not completed after kMbarSpin tries.
+constexpr int kMbarSpin = 1 << 20;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, LatticeHeader* hdr) {
+    for (int i = 0; i < kMbarSpin; ++i)
+        if (mbar_test(bar, parity)) return true;
+    atomicOr(&hdr->status, PL_ST_SPIN);
+    return false;
+}
+
 // ---------------------------------------------------------------- blur
 
 // r *= 2^-e (exact: a power of two, far from the float range limits here)
@@ -1854,6 +1931,151 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
 #pragma unroll
             for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
         }
+    }
+}
+
+// ---------------------------------------------------------------- slice, streamed
+
+// The slice as persistent CTAs that stream the per-slot records of their
+// tiles into shared memory ahead of use.  Each CTA takes tiles blockIdx.x,
+// blockIdx.x + gridDim.x, ...; kSliceStages tiles ahead, thread 0 issues
+// bulk copies of the tile's local ids, weights and the tile's vertex ids
+// (staged_vid[tile_off .. tile_off + tile_cnt), widened to 16-byte bounds)
+// into a ring of stages.  The HBM stream of the records thus overlaps the
+// L2 gathers of the rows, and no thread holds registers for loads in flight.
+// Same arithmetic as k_slice (permutohedral.cu:401-413, 487-496).
+constexpr int kSliceStages = 3;
+template <int PD>
+constexpr bool kSlicePiped = Cfg<PD>::P == 256;
+
+template <int PD>
+struct SliceStage {
+    static constexpr int SLOTS = Cfg<PD>::SLOTS;
+    static constexpr int LID_B = SLOTS * 2;            // multiple of 128 (P >= 64)
+    static constexpr int W_B = SLOTS * 4;
+    static constexpr int VID_N = SLOTS + 32;           // room for the 16-byte widening
+    static constexpr int BYTES = LID_B + W_B + VID_N * 4;
+};
+
+template <int PD>
+__host__ __device__ constexpr int slice_pipe_smem_bytes() {
+    return kSliceStages * SliceStage<PD>::BYTES;
+}
+
+template <int PD, int V, bool FWD>
+__global__ void __launch_bounds__(Cfg<PD>::P, 1024 / Cfg<PD>::P)
+k_slice_pipe(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, const float* __restrict__ lat0,
+             const float* __restrict__ lat1, unsigned long long* st_slot, unsigned st_seq) {
+    using C = Cfg<PD>;
+    using SS = SliceStage<PD>;
+    constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS, ST = kSliceStages;
+    constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
+    constexpr int NC = FWD ? V + 1 : V;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ uint64_t full[ST];
+    __shared__ int vshift[ST];
+    report_status(st_slot, st_seq, L.hdr);
+    const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
+    const int t = threadIdx.x;
+    const int first = blockIdx.x, stride = gridDim.x;
+    const int mine = first < geo.tiles ? (geo.tiles - 1 - first) / stride + 1 : 0;
+
+    // thread 0: copy tile i of this CTA (tile_off `off`, tile_cnt `cnt`) into stage i % ST
+    auto issue = [&](int i, int off, int cnt) {
+        const int s = i % ST;
+        const int tile = first + i * stride;
+        unsigned char* st = smem_raw + s * SS::BYTES;
+        const int v0 = off & ~3, v1 = (off + cnt + 3) & ~3;   // staged_vid widened to 16-byte bounds
+        const unsigned vbytes = (unsigned)(v1 - v0) * 4u;
+        vshift[s] = off - v0;
+        mbar_expect_tx(&full[s], (unsigned)(SS::LID_B + SS::W_B) + vbytes);
+        bulk_g2s(st, L.slot_lid + (size_t)tile * SLOTS, SS::LID_B, &full[s]);
+        bulk_g2s(st + SS::LID_B, L.slot_w + (size_t)tile * SLOTS, SS::W_B, &full[s]);
+        if (vbytes) bulk_g2s(st + SS::LID_B + SS::W_B, L.staged_vid + v0, vbytes, &full[s]);
+    };
+    int nx_off = 0, nx_cnt = 0;   // thread 0: tile_off / tile_cnt of the next tile to issue
+    if (t == 0) {
+        for (int s = 0; s < ST; ++s) mbar_init(&full[s], 1);
+        mbar_init_fence();
+        int offs[ST], cnts[ST];
+#pragma unroll
+        for (int i = 0; i < ST; ++i) {
+            offs[i] = i < mine ? L.tile_off[first + i * stride] : 0;
+            cnts[i] = i < mine ? L.tile_cnt[first + i * stride] : 0;
+        }
+        if (ST < mine) {
+            nx_off = L.tile_off[first + ST * stride];
+            nx_cnt = L.tile_cnt[first + ST * stride];
+        }
+#pragma unroll
+        for (int i = 0; i < ST; ++i)
+            if (i < mine) issue(i, offs[i], cnts[i]);
+    }
+    __syncthreads();   // barriers initialised, first stages issued
+
+    TileWalk walk(geo, first, stride);
+    int i = 0;
+    for (; i < mine; ++i) {
+        const int s = i % ST;
+        const bool got = mbar_wait(&full[s], (unsigned)((i / ST) & 1), L.hdr);
+        // every thread has its stage, and every thread is done with tile i-1
+        if (!__syncthreads_and(got)) break;
+        if (t == 0 && i >= 1 && i - 1 + ST < mine) {   // refill the stage of tile i-1
+            issue(i - 1 + ST, nx_off, nx_cnt);
+            if (i + ST < mine) {
+                nx_off = L.tile_off[first + (i + ST) * stride];
+                nx_cnt = L.tile_cnt[first + (i + ST) * stride];
+            }
+        }
+        const unsigned char* st = smem_raw + s * SS::BYTES;
+        const uint16_t* slid = reinterpret_cast<const uint16_t*>(st);
+        const float* sw = reinterpret_cast<const float*>(st + SS::LID_B);
+        const int* svid = reinterpret_cast<const int*>(st + SS::LID_B + SS::W_B) + vshift[s];
+        const TilePos tp = walk.pos<C::TW, C::TH>(geo);
+        walk.advance();
+        const bool act = tp.x0 + (t % C::TW) < geo.w && tp.y0 + (t / C::TW) < geo.h;
+        const size_t p = (size_t)(tp.pix0 + (long long)(t / C::TW) * geo.w + (t % C::TW));
+        // an inactive pixel, or a corner whose insert failed (reported in the
+        // status word), reads row 0 with weight 0
+        int vid[K];
+        float w[K];
+#pragma unroll
+        for (int c = 0; c < K; ++c) {
+            const int v = act ? svid[slid[c * P + t]] : -1;
+            w[c] = v >= 0 ? sw[c * P + t] : 0.0f;
+            vid[c] = v >= 0 ? v : 0;
+        }
+        // all K rows requested before the first is used (one L2 round trip per tile)
+        float rw[K][CP];
+#pragma unroll
+        for (int c = 0; c < K; ++c) load_row<CP>(lat + (size_t)vid[c] * CP, rw[c]);
+        float acc[NC];
+#pragma unroll
+        for (int j = 0; j < NC; ++j) acc[j] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < K; ++c) {
+#pragma unroll
+            for (int j = 0; j < NC; ++j) acc[j] = __fmaf_rn(w[c], rw[c][j], acc[j]);
+        }
+        if (act) {
+            if constexpr (FWD) {
+                const float inv = 1.0f / acc[V];
+#pragma unroll
+                for (int j = 0; j < V; ++j) out[p * V + j] = acc[j] * inv;
+                wout[p] = inv;
+            } else {
+#pragma unroll
+                for (int j = 0; j < V; ++j) out[p * V + j] = acc[j];
+            }
+        }
+    }
+    // A wait that gave up (recorded as PL_ST_SPIN): the copies still in
+    // flight -- tiles i up to the last one issued -- land before the CTA exits (bounded).
+    if (i < mine && t == 0) {
+        const int last = i == 0 ? ST - 1 : i + ST - 2;   // the last tile issued
+        for (int j = i; j < mine && j <= last; ++j)
+            for (int r = 0; r < kMbarSpin && !mbar_test(&full[j % ST], (unsigned)((j / ST) & 1)); ++r) {
+            }
     }
 }
 
