@@ -423,10 +423,6 @@ def kernel_bytes(stage, n, pd, vd, m, u, cap_log2):
         "blur_bwd": K * m * (8 * CPB + 8),
         "slice_bwd": slot + m * 4 * CPB + n * 4 * vd,
     }
-    # the fused filter kernels: neighbour lookups + splat + blur + slice (forward),
-    # row zeroing + splat + blur + slice (backward)
-    per["filter_fwd"] = per["neighbors"] + per["splat_fwd"] + per["blur_fwd"] + per["slice_fwd"]
-    per["filter_bwd"] = per["zero"] + per["splat_bwd"] + per["blur_bwd"] + per["slice_bwd"]
     return per[stage]
 
 
@@ -703,14 +699,12 @@ def main():
                            "launches_per_step": d["launches_per_step"]}
         b_fwd, b_bwd = stage_bytes(n, pd, vd, m)
         stage_ms = sum(per_stage[s]["ms_per_step"] for s in per_stage
-                       if s in ("splat_fwd", "blur_fwd", "slice_fwd", "zero", "splat_bwd", "blur_bwd", "slice_bwd",
-                                "filter_fwd", "filter_bwd"))
+                       if s in ("splat_fwd", "blur_fwd", "slice_fwd", "zero", "splat_bwd", "blur_bwd", "slice_bwd"))
         all_ms = sum(per_stage[s]["ms_per_step"] for s in per_stage)
         res["roofline_stages"] = {
             "definition": "(B_fwd + B_bwd) of splat+blur+slice / summed device time of the kernels that do "
-                          "them: the fused filter kernels filter_fwd (which also does the blur-neighbour "
-                          "lookups) and filter_bwd (which also zeroes the value rows); B per the lattice byte "
-                          "formula",
+                          "them (splat_fwd is the launch that also runs the blur-neighbour lookups); B per "
+                          "the lattice byte formula",
             "bytes": b_fwd + b_bwd, "kernel_ms": stage_ms,
             "achieved": (b_fwd + b_bwd) / (stage_ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
             "frac": (b_fwd + b_bwd) / (stage_ms * 1e-3) / 1e9 / peak,

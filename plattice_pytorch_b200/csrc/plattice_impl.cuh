@@ -185,11 +185,23 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
 template <int PD, int V, bool FWD>
 cudaError_t splat_with_neighbors(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
                                  const float* vals, const float* wt, float* rows, int stage) {
-    const int nbr_blocks = a.sm_count * 8 * kNbrThreads / Cfg<PD>::P;
     cudaError_t e;
-    PL_LAUNCH(stage, a.stream,
-              e = launch_k(k_splat_nbr<PD, V, FWD>, dim3(nbr_blocks + a.lay.tiles), dim3(Cfg<PD>::P), 0, a.stream,
-                           false, vals, wt, geo, Lv, Sv, rows, nbr_blocks));
+    if constexpr (Cfg<PD>::P == 256) {
+        const int nbr_blocks = a.sm_count * 8 * kNbrThreads / Cfg<PD>::P;
+        PL_LAUNCH(stage, a.stream,
+                  e = launch_k(k_splat_nbr<PD, V, FWD>, dim3(nbr_blocks + a.lay.tiles), dim3(Cfg<PD>::P), 0,
+                               a.stream, false, vals, wt, geo, Lv, Sv, rows, nbr_blocks));
+    } else {
+        // large feature dimensions: the lookups (most of the work) in their own
+        // launch of 256-thread CTAs, then the splat, which resolves the vertex ids
+        PL_LAUNCH(STAGE_NEIGHBORS, a.stream,
+                  e = launch_k(k_neighbors<PD>, dim3(a.sm_count * 8), dim3(kNbrThreads), 0, a.stream, false, geo, Lv,
+                               Sv));
+        if (e != cudaSuccess) return e;
+        PL_LAUNCH(stage, a.stream,
+                  e = launch_k(k_splat<PD, V, FWD>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false, vals, wt, geo,
+                               Lv, Sv, 1, rows));
+    }
     return e;
 }
 
@@ -372,8 +384,11 @@ cudaError_t prepare_v(const CallArgs&) {
     if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CPB>), blur_attr<PD, CPB>, &n);
     const void* fns[] = {reinterpret_cast<const void*>(k_tile_build<PD>), reinterpret_cast<const void*>(k_clear),
                          reinterpret_cast<const void*>(k_insert<PD>),
-                         reinterpret_cast<const void*>(k_splat_nbr<PD, V, true>),
-                         reinterpret_cast<const void*>(k_splat_nbr<PD, V, false>),
+                         Cfg<PD>::P == 256 ? reinterpret_cast<const void*>(k_splat_nbr<PD, V, true>)
+                                           : reinterpret_cast<const void*>(k_neighbors<PD>),
+                         Cfg<PD>::P == 256 ? reinterpret_cast<const void*>(k_splat_nbr<PD, V, false>)
+                                           : reinterpret_cast<const void*>(k_splat<PD, V, true>),
+                         reinterpret_cast<const void*>(k_splat<PD, V, false>),
                          kSlicePiped<PD> ? reinterpret_cast<const void*>(k_slice_pipe<PD, V, true>)
                                          : reinterpret_cast<const void*>(k_slice<PD, V, true>),
                          kSlicePiped<PD> ? reinterpret_cast<const void*>(k_slice_pipe<PD, V, false>)
