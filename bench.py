@@ -117,20 +117,27 @@ def max_over_ranks(x, world):
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi sampling of this GPU's clocks and throttle reasons."""
+    """nvidia-smi sampling of the clocks and throttle reasons of the given GPUs
+    (one sampler process per node: local rank 0 samples every rank's GPU, so
+    that N ranks do not start N nvidia-smi processes on the host cores that
+    enqueue their launches)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device):
+    def __init__(self, devices):
         self.proc = None
         self.path = None
         sel = []
         try:
-            p = torch.cuda.get_device_properties(device)
-            sel = ["-i", f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"]
+            ids = []
+            for d in devices:
+                p = torch.cuda.get_device_properties(d)
+                ids.append(f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0")
+            sel = ["-i", ",".join(ids)]
         except Exception:
             sel = []
+        self.gpus = len(devices)
         self.cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                     "-lms", "100"] + sel
 
@@ -177,7 +184,8 @@ class ClockSampler:
         top = max(mx) if mx else None
         loaded = [s for s in sm if top and s >= 0.5 * top] or sm
         return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": top,
-                "power_w_max": max(pw) if pw else None, "samples": len(rows), "reasons": reasons}
+                "power_w_max": max(pw) if pw else None, "samples": len(rows), "gpus": self.gpus,
+                "reasons": reasons}
 
 
 # ---------------------------------------------------------------- implementations
@@ -595,8 +603,10 @@ def main():
                               "ms_per_step": t / args.steps}))
         return
 
-    clocks = ClockSampler(dev)
-    clocks.start()
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world_eff)))
+    clocks = ClockSampler([torch.device("cuda", i) for i in range(max(1, local_world if world_eff > 1 else 1))])
+    if local == 0:
+        clocks.start()
     # soak: untimed steps until clocks settle under load
     t_end = time.perf_counter() + args.soak_seconds
     while time.perf_counter() < t_end:
