@@ -156,8 +156,7 @@ cudaError_t blur_attr(int* per_sm) {
 
 // Build the lattice: tile dedup (which also zeroes the lattice value rows
 // `zero` of cp floats each, and `zero_b` of cpb floats when set), table clear,
-// global insert, vertex ids.  Blur neighbours follow, alongside the first
-// splat.
+// global insert, vertex ids.  Blur neighbours follow, with the first splat.
 template <int PD>
 cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv, float* zero,
                           int cp, float* zero_b = nullptr, int cpb = 0) {

@@ -9,16 +9,19 @@
 //   k_insert       global open-addressed insert of the staged keys (tagged
 //                  cells); compact vertex ids for the owners, one atomic per
 //                  CTA chunk
-//   k_neighbors    blur neighbours of every vertex by table lookup; runs on a
-//                  side stream, overlapped with the splat
-//   k_splat        per tile: [v*w, w] summed over the sorted segments of equal
-//                  vertex, one vector red.global.add per segment
+//   k_splat_nbr    blur neighbours of every vertex by table lookup (the first
+//                  CTAs) and the splat (the others): per tile, [v*w, w] summed
+//                  over the sorted runs of equal vertex, one vector
+//                  red.global.add per run piece.  Large pd: k_neighbors, then
+//                  k_splat
 //   k_blur_all     the pd+1 passes of the [1 2 1]/4 stencil over the compact
 //                  vertex list: one cooperative launch with grid barriers
 //                  between passes
-//   k_slice        barycentric gather back to the pixels and normalisation
+//   k_slice_pipe   barycentric gather back to the pixels and normalisation;
+//                  persistent CTAs that stream the tiles' slot records into
+//                  shared memory (k_slice for tiles of fewer than 256 pixels)
 // Backward reuses the lattice: k_splat of grad * weight, k_blur_all in
-// reverse axis order, k_slice without normalisation.
+// reverse axis order, the slice without normalisation.
 //
 // The float steps that decide the lattice keys (elevation, greedy rounding,
 // rank, barycentric weights) reproduce the reference's operation order,
