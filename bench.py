@@ -729,6 +729,10 @@ def main():
             "measured": atomics_from_profiles() if args.workload == "voronoi1024_pd5_vd3" else {},
             "measured_source": "profiles/atomics.txt (ncu, one launch each, this workload)"}
         res["gpu_launches"] = int(round(launches_per_step * args.steps * launch_mult))
+        from plattice_pytorch_b200 import PLOO as _P
+        cap, rep = _P.graph_cache_stats()
+        res["call_graphs"] = {"captured": cap, "replayed": rep,
+                              "note": "calls repeated with the same buffers run as one CUDA graph launch"}
 
     if rank == 0 and world_eff == 1 and not args.no_cpu_baseline:
         im = imgs[0]

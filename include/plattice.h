@@ -45,7 +45,7 @@
 extern "C" {
 #endif
 
-#define PLATTICE_ABI_VERSION 4
+#define PLATTICE_ABI_VERSION 5
 
 /* status codes */
 #define PLATTICE_OK 0
@@ -190,6 +190,22 @@ int plattice_poll_status(void);
  * module loading each kernel is otherwise loaded at its first launch).  Call it before any stream capture, or before real-time work that
  * must not pay these costs.  No reference counterpart. */
 int plattice_prepare(int pd, int vd);
+
+/* Call graphs (no reference counterpart; the reference launches every kernel
+ * from the host on every call, permutohedral.cu:549-596).  A forward or
+ * backward call whose buffers, sizes and settings equal those of an earlier
+ * call in the same CUDA context is run as a CUDA graph: the second such call
+ * captures its launches into a graph (captured on a private stream of the
+ * context, in thread-local capture mode), later ones launch that graph on
+ * their stream -- one launch instead of seven (forward) or three (backward)
+ * on the host.  Results are the same either way.  `entries` graphs per
+ * context are kept (least recently used evicted; default 16, or 0 when the
+ * environment variable PLATTICE_GRAPHS is "0"); 0 turns graphs off.  Changing
+ * the setting releases every cached graph.  While profiling is enabled, and
+ * for plattice_forward_noalloc, calls run without graphs. */
+int plattice_set_graph_cache(int entries);
+/* Graphs captured and graph launches made so far (process-wide counts). */
+void plattice_graph_cache_stats(long long* captures, long long* replays);
 
 /* Test support: force the hash-table capacity to 2^log2 cells (0 = automatic,
  * >= twice the staged keys).  A capacity below the vertex count makes the

@@ -37,7 +37,7 @@ from . import _lib
 __all__ = ["forward", "backward", "Lattice", "lattice_forward", "lattice_backward",
            "lattice_filter", "lattice_filter_backward", "feature_grad", "BatchLattice", "batch_forward",
            "batch_backward", "forward_batch", "backward_batch", "lattice_info", "vertex_keys",
-           "check_device_status", "prepare"]
+           "check_device_status", "prepare", "set_graph_cache", "graph_cache_stats"]
 
 _CHECK = os.environ.get("PLATTICE_CHECK", "0") not in ("", "0")
 
@@ -485,7 +485,7 @@ def check_device_status():
 
 def prepare(pd, vd, device=None):
     """Do once, on ``device``'s context, what a first call for (pd, vd) would
-    do besides filtering: kernel attributes, the side stream, kernel loading."""
+    do besides filtering: kernel attributes, occupancy queries, kernel loading."""
     _check_dims(pd, vd)
     idx = torch.cuda.current_device() if device is None else torch.device(device).index
     rc = _call(idx, _lib_h().plattice_prepare, pd, vd)
@@ -535,3 +535,22 @@ def set_lattice_precision(precision):
 def get_lattice_precision():
     """``"fp32"`` or ``"bf16"``: the setting of set_lattice_precision."""
     return "bf16" if _lib_h().plattice_get_lattice_precision() == 16 else "fp32"
+
+
+def set_graph_cache(entries):
+    """Graphs kept per CUDA context for calls repeated with the same buffers
+    (``plattice_set_graph_cache``): such a call is captured into a CUDA graph
+    the second time and replayed afterwards, one launch on the host instead of
+    one per kernel.  0 turns it off; the default is 16 (0 when the
+    environment variable PLATTICE_GRAPHS is "0").  Results do not depend on it."""
+    _require(isinstance(entries, int) and entries >= 0, "entries must be a non-negative int")
+    rc = _lib_h().plattice_set_graph_cache(entries)
+    if rc != _lib.OK:
+        _raise("plattice_set_graph_cache", rc, "")
+
+
+def graph_cache_stats():
+    """``(captures, replays)`` of call graphs so far, process-wide."""
+    c, r = ctypes.c_longlong(0), ctypes.c_longlong(0)
+    _lib_h().plattice_graph_cache_stats(ctypes.byref(c), ctypes.byref(r))
+    return c.value, r.value

@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(HERE, "libplattice_b200.so")
 
 OK, ERR_INVALID, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
 DEV_TABLE_FULL, DEV_WAIT_LIMIT, DEV_ROUND_LIMIT = 2, 4, 8
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _lock = threading.Lock()
 _lib = None
@@ -77,6 +77,10 @@ def lib():
         L.plattice_poll_status.argtypes = []
         L.plattice_prepare.restype = I
         L.plattice_prepare.argtypes = [I, I]
+        L.plattice_set_graph_cache.restype = I
+        L.plattice_set_graph_cache.argtypes = [I]
+        L.plattice_graph_cache_stats.restype = None
+        L.plattice_graph_cache_stats.argtypes = [ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_longlong)]
         L.plattice_forward_noalloc.restype = I
         L.plattice_forward_noalloc.argtypes = [P, P, P, P, I, I, I, I, P]
         L.plattice_noalloc_capacity.restype = S

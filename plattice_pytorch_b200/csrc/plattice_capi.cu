@@ -4,6 +4,10 @@
 #include <limits.h>
 #include <stdio.h>
 
+#include <stdlib.h>
+#include <string.h>
+
+#include <initializer_list>
 #include <mutex>
 #include <vector>
 
@@ -142,6 +146,164 @@ static int sm_count_current() {
     return n;
 }
 
+// ---------------------------------------------------------------- call graphs
+
+// A call whose launch sequence has been seen before with exactly the same
+// buffers, sizes and settings is replayed as one CUDA graph: the second such
+// call captures its launches (on a private stream of the context, in
+// thread-local capture mode) into a graph, and every later one launches that
+// graph on the caller's stream after pointing the status-reporting kernel at
+// the call's status-ring slot.  One graph launch replaces the seven launches
+// of a forward (three of a backward) on the host.  Graphs are kept per CUDA
+// context in a small least-recently-used cache; calls that profile, and the
+// no-allocation entry point (instantiating a graph allocates), run directly.
+namespace {
+
+struct GraphKey {
+    int kind;
+    const void* p[8];
+    size_t n[2];
+    int v[12];
+    bool operator==(const GraphKey& o) const {
+        if (kind != o.kind || n[0] != o.n[0] || n[1] != o.n[1]) return false;
+        for (int i = 0; i < 8; ++i)
+            if (p[i] != o.p[i]) return false;
+        for (int i = 0; i < 12; ++i)
+            if (v[i] != o.v[i]) return false;
+        return true;
+    }
+};
+
+struct GraphEntry {
+    GraphKey key;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    pl::StatusNode sn;
+    unsigned long long used = 0;
+};
+
+struct GraphCache {
+    cudaStream_t capture = nullptr;
+    std::vector<GraphEntry*> entries;
+    std::vector<GraphKey> seen;   // keys called once, most recent last
+    unsigned long long clock = 0;
+};
+
+std::mutex g_graph_mu;
+std::vector<std::pair<pl::CtxState*, GraphCache*>> g_graph_caches;
+int g_graph_cap = -1;   // entries per context; 0 = off; -1: read PLATTICE_GRAPHS on first use
+long long g_graph_captures = 0, g_graph_replays = 0;
+
+int graph_capacity() {
+    if (g_graph_cap < 0) {
+        const char* e = getenv("PLATTICE_GRAPHS");
+        g_graph_cap = (e && e[0] == '0' && e[1] == '\0') ? 0 : 16;
+    }
+    return g_graph_cap;
+}
+
+GraphCache* graph_cache() {
+    cudaError_t e;
+    pl::CtxState* c = pl::ctx_state(&e);
+    if (!c) return nullptr;
+    for (auto& pc : g_graph_caches)
+        if (pc.first == c) return pc.second;
+    g_graph_caches.emplace_back(c, new GraphCache());
+    return g_graph_caches.back().second;
+}
+
+void graph_free(GraphEntry* g) {
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    delete g;
+}
+
+}  // namespace
+
+// Runs `dispatch(a)` directly, or as a captured graph (see above).
+static cudaError_t run_call(const GraphKey& key, pl::CallArgs& a, cudaError_t (*dispatch)(const pl::CallArgs&)) {
+    const int cap = graph_capacity();
+    if (cap <= 0 || pl::prof_enabled()) return dispatch(a);
+    std::lock_guard<std::mutex> lk(g_graph_mu);
+    GraphCache* gc = graph_cache();
+    if (!gc) return dispatch(a);
+    ++gc->clock;
+    for (GraphEntry* g : gc->entries) {
+        if (g->key == key) {
+            g->used = gc->clock;
+            cudaError_t e = g->sn.retarget(g->exec, a.st.slot, a.st.seq);
+            if (e == cudaSuccess) e = cudaGraphLaunch(g->exec, a.stream);
+            if (e == cudaSuccess) ++g_graph_replays;
+            return e;
+        }
+    }
+    bool again = false;
+    for (size_t i = 0; i < gc->seen.size(); ++i) {
+        if (gc->seen[i] == key) {
+            again = true;
+            gc->seen.erase(gc->seen.begin() + (long)i);
+            break;
+        }
+    }
+    if (!again) {   // first sighting: run directly, remember the key
+        gc->seen.push_back(key);
+        if (gc->seen.size() > 32) gc->seen.erase(gc->seen.begin());
+        return dispatch(a);
+    }
+    // second sighting: capture, instantiate, launch
+    cudaError_t e = cudaSuccess;
+    if (!gc->capture) e = cudaStreamCreateWithFlags(&gc->capture, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return e;
+    GraphEntry* g = new GraphEntry();
+    g->key = key;
+    pl::CallArgs c = a;
+    c.stream = gc->capture;
+    c.status_node = &g->sn;
+    e = cudaStreamBeginCapture(gc->capture, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) {
+        delete g;
+        return e;
+    }
+    const cudaError_t ed = dispatch(c);
+    const cudaError_t ee = cudaStreamEndCapture(gc->capture, &g->graph);
+    if (ed == cudaSuccess && ee == cudaSuccess && g->graph && g->sn.retarget)
+        e = cudaGraphInstantiate(&g->exec, g->graph, 0);
+    else
+        e = ed != cudaSuccess ? ed : (ee != cudaSuccess ? ee : cudaErrorStreamCaptureInvalidated);
+    if (e != cudaSuccess) {   // capture did not produce a usable graph: run directly
+        cudaGetLastError();
+        graph_free(g);
+        return dispatch(a);
+    }
+    if ((int)gc->entries.size() >= cap) {   // evict the least recently used graph
+        size_t lru = 0;
+        for (size_t i = 1; i < gc->entries.size(); ++i)
+            if (gc->entries[i]->used < gc->entries[lru]->used) lru = i;
+        graph_free(gc->entries[lru]);
+        gc->entries.erase(gc->entries.begin() + (long)lru);
+    }
+    g->used = gc->clock;
+    gc->entries.push_back(g);
+    ++g_graph_captures;
+    e = g->sn.retarget(g->exec, a.st.slot, a.st.seq);
+    if (e == cudaSuccess) e = cudaGraphLaunch(g->exec, a.stream);
+    return e;
+}
+
+static GraphKey call_key(int kind, const pl::CallArgs& a, std::initializer_list<const void*> ptrs, size_t n0, size_t n1) {
+    GraphKey k;
+    memset(&k, 0, sizeof(k));
+    k.kind = kind;
+    int i = 0;
+    for (const void* q : ptrs) k.p[i++] = q;
+    k.n[0] = n0;
+    k.n[1] = n1;
+    k.v[0] = a.lay.b; k.v[1] = a.lay.h; k.v[2] = a.lay.w; k.v[3] = a.lay.pd; k.v[4] = a.lay.vd;
+    k.v[5] = a.lattice_state; k.v[6] = a.cap_override_log2; k.v[7] = a.filter_min_log2; k.v[8] = a.blur_flags;
+    k.v[9] = a.sm_count;
+    return k;
+}
+
 static cudaError_t dispatch_prepare(const pl::CallArgs& a) {
 #define PL_PREP(N) pl::run_prepare<N>(a)
     PL_PD_SWITCH(a.lay.pd, PL_PREP)
@@ -224,7 +386,10 @@ int forward_images(float* weight_out, float* out, const float* values, const flo
     rows_in_scratch(a, scratch);
     a.lattice_state = 0;
     common_args(a, stream, track, call);
-    return cuda_status(dispatch_forward(a), call);
+    if (!track) return cuda_status(dispatch_forward(a), call);   // allocates nothing: no graph
+    const GraphKey key = call_key(0, a, {weight_out, out, values, features, lattice, scratch}, lattice_bytes,
+                                  scratch_bytes);
+    return cuda_status(run_call(key, a, dispatch_forward), call);
 }
 
 }  // namespace pl
@@ -253,7 +418,9 @@ static int backward_images(float* grad_values_out, const float* grad, const floa
     a.v0 = pl::lattice_vb0(a);   // the splat target; the scratch's v1 is its ping-pong partner
     a.lattice_state = lattice_state;
     common_args(a, stream, true, call);
-    return cuda_status(dispatch_backward(a), call);
+    const GraphKey key = call_key(1, a, {grad_values_out, grad, weight_in, features, lattice, scratch},
+                                  lattice_bytes, scratch_bytes);
+    return cuda_status(run_call(key, a, dispatch_backward), call);
 }
 
 extern "C" {
@@ -563,5 +730,24 @@ int plattice_set_lattice_precision(int bits) {
 int plattice_get_lattice_precision(void) { return g_blur_half ? 16 : 32; }
 
 void plattice_debug_set_blur_streaming(int on) { g_blur_stream = on ? 1 : 0; }
+
+
+int plattice_set_graph_cache(int entries) {
+    if (entries < 0) return PLATTICE_ERR_INVALID;
+    std::lock_guard<std::mutex> lk(g_graph_mu);
+    g_graph_cap = entries;
+    for (auto& pc : g_graph_caches) {   // graphs of every context are released
+        for (GraphEntry* g : pc.second->entries) graph_free(g);
+        pc.second->entries.clear();
+        pc.second->seen.clear();
+    }
+    return PLATTICE_OK;
+}
+
+void plattice_graph_cache_stats(long long* captures, long long* replays) {
+    std::lock_guard<std::mutex> lk(g_graph_mu);
+    if (captures) *captures = g_graph_captures;
+    if (replays) *replays = g_graph_replays;
+}
 
 }  // extern "C"

@@ -4,6 +4,7 @@
 #pragma once
 #include <math.h>
 
+#include <functional>
 #include <utility>
 
 #include "plattice_kernels.cuh"
@@ -11,6 +12,14 @@
 #include "plattice_runtime.h"
 
 namespace pl {
+
+// The kernel node of a captured call that writes the call's status word to
+// its status-ring slot (the call's last kernel), and how to point it at the
+// slot and sequence number of a later replay of the graph.
+struct StatusNode {
+    cudaGraphNode_t node = nullptr;
+    std::function<cudaError_t(cudaGraphExec_t, unsigned long long*, unsigned)> retarget;
+};
 
 struct CallArgs {
     const float* features;
@@ -39,6 +48,7 @@ struct CallArgs {
     float* evec;
     int* flags;
     StatusTicket st;         // where the call's last kernel reports the status word
+    StatusNode* status_node; // set while the call is being captured into a graph
 };
 
 inline LatView lat_view(void* base, const PlLayout& L) {
@@ -267,19 +277,52 @@ template <int PD, int V, bool FWD>
 cudaError_t launch_slice(const CallArgs& a, const Geo& geo, const LatView& Lv, float* out, float* wout,
                          const float* r0, const float* r1) {
     cudaError_t e;
+    void (*kern)(float*, float*, Geo, LatView, const float*, const float*, unsigned long long*, unsigned);
+    dim3 grid, block(Cfg<PD>::P);
+    size_t smem = 0;
     if constexpr (kSlicePiped<PD>) {
         int per_sm = 0;
         e = kernel_once(reinterpret_cast<const void*>(k_slice_pipe<PD, V, FWD>), slice_attr<PD, V, FWD>, &per_sm);
         if (e != cudaSuccess) return e;
         const int want = a.sm_count * per_sm;
-        const int grid = want < a.lay.tiles ? want : a.lay.tiles;
-        PL_LAUNCH(FWD ? STAGE_SLICE_FWD : STAGE_SLICE_BWD, a.stream,
-                  e = launch_k(k_slice_pipe<PD, V, FWD>, dim3(grid), dim3(Cfg<PD>::P), slice_pipe_smem_bytes<PD>(),
-                               a.stream, false, out, wout, geo, Lv, r0, r1, a.st.slot, a.st.seq));
+        kern = k_slice_pipe<PD, V, FWD>;
+        grid = dim3(want < a.lay.tiles ? want : a.lay.tiles);
+        smem = slice_pipe_smem_bytes<PD>();
     } else {
-        PL_LAUNCH(FWD ? STAGE_SLICE_FWD : STAGE_SLICE_BWD, a.stream,
-                  e = launch_k(k_slice<PD, V, FWD>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false, out, wout,
-                               geo, Lv, r0, r1, a.st.slot, a.st.seq));
+        kern = k_slice<PD, V, FWD>;
+        grid = tile_grid(a);
+    }
+    PL_LAUNCH(FWD ? STAGE_SLICE_FWD : STAGE_SLICE_BWD, a.stream,
+              e = launch_k(kern, grid, block, smem, a.stream, false, out, wout, geo, Lv, r0, r1, a.st.slot,
+                           a.st.seq));
+    if (e == cudaSuccess && a.status_node) {   // being captured: remember the node and its arguments
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        const cudaGraphNode_t* deps = nullptr;
+        size_t nd = 0;
+        e = cudaStreamGetCaptureInfo(a.stream, &cs, nullptr, nullptr, &deps, &nd);
+        if (e != cudaSuccess) return e;
+        if (cs == cudaStreamCaptureStatusActive && nd == 1) {
+            const cudaGraphNode_t node = deps[0];
+            a.status_node->node = node;
+            a.status_node->retarget = [=](cudaGraphExec_t ex, unsigned long long* slot, unsigned seq) {
+                float* o = out;
+                float* wo = wout;
+                Geo g = geo;
+                LatView lv = Lv;
+                const float* x0 = r0;
+                const float* x1 = r1;
+                unsigned long long* sl = slot;
+                unsigned sq = seq;
+                void* args[] = {&o, &wo, &g, &lv, &x0, &x1, &sl, &sq};
+                cudaKernelNodeParams p = {};
+                p.func = reinterpret_cast<void*>(kern);
+                p.gridDim = grid;
+                p.blockDim = block;
+                p.sharedMemBytes = (unsigned)smem;
+                p.kernelParams = args;
+                return cudaGraphExecKernelNodeSetParams(ex, node, &p);
+            };
+        }
     }
     return e;
 }

@@ -1,0 +1,148 @@
+"""Call graphs: a forward or backward repeated with the same buffers runs as
+a captured CUDA graph from its second occurrence on (plattice_set_graph_cache).
+
+The checker is the reference-generated golden case (and the direct launches
+with graphs turned off): every call of a sequence on fixed buffers -- the
+first run directly, the second captured and launched, the later ones
+replayed -- gives the
+golden output, normaliser and value gradient within 1e-5 relative + 5e-6
+absolute; replays are counted; a device failure of a replayed call is still
+reported on the next call, since the replay points the status-reporting
+kernel at the call's own status slot.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, allclose_report
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 5e-6
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    from plattice_pytorch_b200 import _lib
+    return _lib.lib()
+
+
+class Buffers:
+    """Fixed device buffers of one golden case, for calls through the C ABI."""
+
+    def __init__(self, name, dev):
+        from plattice_pytorch_b200 import _lib
+        d = np.load(os.path.join(GOLDEN, name))
+        self.d = d
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+        self.f, self.v, self.g = t(d["features"]), t(d["values"]), t(d["grad"])
+        self.h, self.w, self.pd = self.f.shape
+        self.vd = self.v.shape[2]
+        self.lb, self.sb = _lib.workspace_sizes(self.h, self.w, self.pd, self.vd)
+        self.lat = torch.empty(self.lb, dtype=torch.uint8, device=dev)
+        self.scr = torch.empty(self.sb, dtype=torch.uint8, device=dev)
+        self.out = torch.empty((self.h, self.w, self.vd), device=dev)
+        self.wo = torch.empty((self.h, self.w, 1), device=dev)
+        self.gout = torch.empty((self.h, self.w, self.vd), device=dev)
+        self.stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def forward(self, L):
+        return L.plattice_forward(self.wo.data_ptr(), self.out.data_ptr(), self.v.data_ptr(), self.f.data_ptr(),
+                                  self.lat.data_ptr(), self.lb, self.scr.data_ptr(), self.sb, self.pd, self.vd,
+                                  self.w, self.h, self.stream)
+
+    def backward(self, L, state):
+        return L.plattice_backward(self.gout.data_ptr(), self.g.data_ptr(), self.wo.data_ptr(), self.f.data_ptr(),
+                                   self.lat.data_ptr(), self.lb, state, self.scr.data_ptr(), self.sb, self.pd,
+                                   self.vd, self.w, self.h, self.stream)
+
+    def check(self):
+        torch.cuda.synchronize()
+        assert allclose_report(self.out.cpu().numpy(), self.d["out"], RTOL, ATOL) <= 1.0
+        assert allclose_report(self.wo.cpu().numpy(), self.d["weight"], RTOL, ATOL) <= 1.0
+        assert allclose_report(self.gout.cpu().numpy(), self.d["grad_out"], RTOL, ATOL) <= 1.0
+
+
+def _stats(L):
+    c, r = ctypes.c_longlong(0), ctypes.c_longlong(0)
+    L.plattice_graph_cache_stats(ctypes.byref(c), ctypes.byref(r))
+    return c.value, r.value
+
+
+@pytest.mark.parametrize("name", ["ref_blobs64_pd5_vd3.npz", "ref_randn24x20_pd16_vd1.npz",
+                                  "ref_ragged13x29_pd5_vd3.npz"])
+def test_repeated_calls_are_replayed_and_exact(lib, name):
+    from plattice_pytorch_b200 import PLOO
+    dev = torch.device("cuda:0")
+    assert lib.plattice_set_graph_cache(16) == 0
+    try:
+        b = Buffers(name, dev)
+        c0, r0 = _stats(lib)
+        for i in range(5):
+            b.out.fill_(float("nan"))
+            b.gout.fill_(float("nan"))
+            assert b.forward(lib) == 0
+            assert b.backward(lib, 1) == 0
+            b.check()
+        c1, r1 = _stats(lib)
+        assert c1 - c0 == 2                  # the forward and the backward, captured once each
+        assert r1 - r0 == 2 * 3              # calls 3..5 of each replayed the graph call 2 captured
+        PLOO.check_device_status()
+        # the same calls without graphs give the same result
+        assert lib.plattice_set_graph_cache(0) == 0
+        b.out.fill_(float("nan"))
+        b.gout.fill_(float("nan"))
+        assert b.forward(lib) == 0 and b.backward(lib, 1) == 0
+        b.check()
+        assert _stats(lib)[1] == r1
+    finally:
+        lib.plattice_set_graph_cache(16)
+
+
+def test_backward_states_and_other_buffers_get_their_own_graphs(lib):
+    dev = torch.device("cuda:0")
+    lib.plattice_set_graph_cache(16)
+    a = Buffers("ref_blobs64_pd5_vd3.npz", dev)
+    b = Buffers("ref_blobs64_pd5_vd3.npz", dev)   # same shapes, other buffers
+    for _ in range(3):
+        for x in (a, b):
+            x.gout.fill_(float("nan"))
+            assert x.forward(lib) == 0
+            assert x.backward(lib, 1) == 0
+            assert x.backward(lib, 2) == 0      # a repeated backward re-zeroes its rows
+            assert x.backward(lib, 0) == 0      # a rebuild
+            x.check()
+
+
+def test_device_failure_of_a_replayed_call_is_reported(lib):
+    from plattice_pytorch_b200 import PLOO, _lib
+    dev = torch.device("cuda:0")
+    lib.plattice_set_graph_cache(16)
+    PLOO.check_device_status()
+    b = Buffers("ref_blobs64_pd5_vd3.npz", dev)
+    try:
+        lib.plattice_debug_set_table_cap_log2(6)   # 64 cells for 1225 vertices
+        c0, r0 = _stats(lib)
+        assert b.forward(lib) == 0                 # direct
+        torch.cuda.synchronize()
+        assert lib.plattice_poll_status() == _lib.ERR_DEVICE
+        assert b.forward(lib) == 0                 # captured and launched
+        torch.cuda.synchronize()
+        assert lib.plattice_poll_status() == _lib.ERR_DEVICE
+        assert b.forward(lib) == 0                 # replayed
+        torch.cuda.synchronize()
+        assert lib.plattice_poll_status() == _lib.ERR_DEVICE
+        c1, r1 = _stats(lib)
+        assert c1 - c0 == 1 and r1 - r0 == 1
+    finally:
+        lib.plattice_debug_set_table_cap_log2(0)
+    PLOO.check_device_status()
+    assert b.forward(lib) == 0 and b.backward(lib, 1) == 0
+    b.check()
+    torch.cuda.synchronize()
+    PLOO.check_device_status()
