@@ -154,7 +154,7 @@ static int sm_count_current() {
 // thread-local capture mode) into a graph, and every later one launches that
 // graph on the caller's stream after pointing the status-reporting kernel at
 // the call's status-ring slot.  One graph launch replaces the seven launches
-// of a forward (three of a backward) on the host.  Graphs are kept per CUDA
+// of a forward (three of a backward or of a kept-lattice filter) on the host.  Graphs are kept per CUDA
 // context in a small least-recently-used cache; calls that profile, and the
 // no-allocation entry point (instantiating a graph allocates), run directly.
 namespace {
@@ -545,7 +545,8 @@ int plattice_filter(float* weight_out, float* out, const float* values, void* la
     a.out = out;
     a.wout = weight_out;
     a.lattice = lattice;
-    return cuda_status(dispatch_filter(a), "plattice_filter");
+    const GraphKey key = call_key(2, a, {weight_out, out, values, lattice, values_ws}, lattice_bytes, values_ws_bytes);
+    return cuda_status(run_call(key, a, dispatch_filter), "plattice_filter");
 }
 
 int plattice_filter_backward(float* grad_values_out, const float* grad, const float* weight_in, void* lattice,
@@ -564,7 +565,9 @@ int plattice_filter_backward(float* grad_values_out, const float* grad, const fl
     a.out = grad_values_out;
     a.lattice = lattice;
     a.lattice_state = 2;   // kept lattice: zero the value rows, no rebuild
-    return cuda_status(dispatch_backward(a), "plattice_filter_backward");
+    const GraphKey key = call_key(3, a, {grad_values_out, grad, weight_in, lattice, values_ws}, lattice_bytes,
+                                  values_ws_bytes);
+    return cuda_status(run_call(key, a, dispatch_backward), "plattice_filter_backward");
 }
 
 // ---------------------------------------------------------------- feature gradient

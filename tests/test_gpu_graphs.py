@@ -146,3 +146,27 @@ def test_device_failure_of_a_replayed_call_is_reported(lib):
     b.check()
     torch.cuda.synchronize()
     PLOO.check_device_status()
+
+
+def test_kept_lattice_filter_loop_replays(lib):
+    """Five rounds of filter + filter backward on one kept lattice with fixed
+    buffers (a mean-field loop): every round equals the golden forward output,
+    normaliser and value gradient; rounds 3..5 replay the captured graphs."""
+    from plattice_pytorch_b200 import _lib
+    dev = torch.device("cuda:0")
+    lib.plattice_set_graph_cache(16)
+    b = Buffers("ref_blobs64_pd5_vd3.npz", dev)
+    assert b.forward(lib) == 0
+    wsb = _lib.filter_workspace_size(b.h, b.w, b.pd, b.vd)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    c0, r0 = _stats(lib)
+    for _ in range(5):
+        b.out.fill_(float("nan"))
+        b.gout.fill_(float("nan"))
+        assert lib.plattice_filter(b.wo.data_ptr(), b.out.data_ptr(), b.v.data_ptr(), b.lat.data_ptr(), b.lb,
+                                   ws.data_ptr(), wsb, b.pd, b.vd, b.w, b.h, b.stream) == 0
+        assert lib.plattice_filter_backward(b.gout.data_ptr(), b.g.data_ptr(), b.wo.data_ptr(), b.lat.data_ptr(),
+                                            b.lb, ws.data_ptr(), wsb, b.pd, b.vd, b.w, b.h, b.stream) == 0
+        b.check()
+    c1, r1 = _stats(lib)
+    assert c1 - c0 == 2 and r1 - r0 == 6
