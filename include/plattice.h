@@ -263,14 +263,19 @@ const char* plattice_noalloc_error_detail(void);
  * PLATTICE_ERR_DEVICE when the status word is non-zero. */
 int plattice_noalloc_status(int* status, int* m, void* stream);
 
-/* Profiling (no reference counterpart): when enabled, every kernel launch is
- * bracketed by CUDA events recorded on its stream.  plattice_profile_read
- * waits for the recorded events, writes per stage the summed milliseconds and
- * the launch count (stage order as plattice_profile_stage_name), and clears
- * the record.  Stages: 0 tile_build, 1 clear, 2 insert (and compaction),
- * 3 neighbors, 4 blur_fwd, 5 slice_fwd, 6 zero, 7 splat_bwd, 8 blur_bwd,
- * 9 slice_bwd, 10 splat_fwd. */
-#define PLATTICE_PROFILE_STAGES 11
+/* Profiling (no reference counterpart).  plattice_profile_enable(1): every
+ * kernel launch is bracketed by CUDA events recorded on its stream (stages
+ * 0-10); plattice_profile_enable(2): only launch groups are (stages 11-13),
+ * so that fewer events sit between the kernels; 0 turns it off.  While it is
+ * on, calls run without call graphs.  plattice_profile_read waits for the
+ * recorded events, writes per stage the summed milliseconds and the count
+ * (stage order as plattice_profile_stage_name), and clears the record.
+ * Stages: 0 tile_build, 1 clear, 2 insert (and compaction), 3 neighbors,
+ * 4 blur_fwd, 5 slice_fwd, 6 zero, 7 splat_bwd, 8 blur_bwd, 9 slice_bwd,
+ * 10 splat_fwd; groups: 11 build (header memset .. insert), 12 filter_fwd (a
+ * forward's launches after the build), 13 filter_bwd (a backward's splat,
+ * blur and slice). */
+#define PLATTICE_PROFILE_STAGES 14
 void plattice_profile_enable(int on);
 int plattice_profile_read(double* ms_total, int* launches, int n_stages);
 const char* plattice_profile_stage_name(int stage);

@@ -172,12 +172,14 @@ def filter_workspace_size(h, w, pd, vd):
     return b.value
 
 
-PROFILE_STAGES = 11
+PROFILE_STAGES = 14
 
 
-def profile_enable(on=True):
-    """Bracket every kernel launch with CUDA events (see profile_read)."""
-    lib().plattice_profile_enable(1 if on else 0)
+def profile_enable(on=True, groups=False):
+    """Bracket every kernel launch with CUDA events, or with ``groups=True``
+    only the launch groups (build, forward filter, backward filter); see
+    profile_read."""
+    lib().plattice_profile_enable((2 if groups else 1) if on else 0)
 
 
 def profile_read():

@@ -45,7 +45,7 @@ struct ProfRec {
     cudaEvent_t begin, end;
 };
 std::mutex g_prof_mu;
-bool g_prof_on = false;
+int g_prof_mode = 0;
 std::vector<cudaEvent_t> g_prof_pool;
 std::vector<ProfRec> g_prof_done;
 ProfRec g_prof_open[pl::STAGE_COUNT];
@@ -63,11 +63,11 @@ cudaEvent_t prof_event() {
 }  // namespace
 
 namespace pl {
-bool prof_enabled() { return g_prof_on; }
+int prof_mode() { return g_prof_mode; }
 
 void prof_mark(int stage, cudaStream_t s, bool begin) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
-    if (!g_prof_on || stage < 0 || stage >= STAGE_COUNT) return;
+    if (!g_prof_mode || stage < 0 || stage >= STAGE_COUNT) return;
     cudaEvent_t e = prof_event();
     if (!e) return;
     cudaEventRecord(e, s);
@@ -684,7 +684,7 @@ int plattice_vertex_keys(const void* lattice, const void* scratch, int pd, int v
 
 void plattice_profile_enable(int on) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
-    g_prof_on = on != 0;
+    g_prof_mode = (on == 1 || on == 2) ? on : 0;
 }
 
 int plattice_profile_read(double* ms_total, int* launches, int n_stages) {
@@ -712,7 +712,8 @@ int plattice_profile_read(double* ms_total, int* launches, int n_stages) {
 const char* plattice_profile_stage_name(int stage) {
     static const char* names[pl::STAGE_COUNT] = {
         "tile_build", "clear", "insert", "neighbors", "blur_fwd", "slice_fwd",
-        "zero", "splat_bwd", "blur_bwd", "slice_bwd", "splat_fwd"};
+        "zero", "splat_bwd", "blur_bwd", "slice_bwd", "splat_fwd",
+        "build", "filter_fwd", "filter_bwd"};
     return (stage >= 0 && stage < pl::STAGE_COUNT) ? names[stage] : "";
 }
 

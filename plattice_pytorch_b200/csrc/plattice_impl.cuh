@@ -175,6 +175,7 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     const int grid = a.sm_count * 8;
     cudaError_t e = prepare_tile_build<PD>();
     if (e != cudaSuccess) return e;
+    PL_GROUP(STAGE_GROUP_BUILD, s, true);
     e = cudaMemsetAsync(Lv.hdr, 0, sizeof(LatticeHeader), s);
     if (e != cudaSuccess) return e;
     const EmbedConsts ec = embed_consts(PD);
@@ -185,6 +186,7 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     PL_LAUNCH(STAGE_CLEAR, s, e = launch_k(k_clear, dim3(grid), dim3(256), 0, s, false, geo, Lv, Sv));
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_INSERT, s, e = launch_k(k_insert<PD>, dim3(grid * 2), dim3(256), 0, s, false, geo, Lv, Sv));
+    PL_GROUP(STAGE_GROUP_BUILD, s, false);
     return e;
 }
 
@@ -336,13 +338,16 @@ cudaError_t forward_v(const CallArgs& a) {
     // zeroes the forward's rows and the lattice's rows for the first backward
     cudaError_t e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPF, lattice_vb0(a), CPB);
     if (e != cudaSuccess) return e;
+    PL_GROUP(STAGE_GROUP_FILTER_FWD, a.stream, true);
     // neighbour lookups (L2-latency-bound) alongside the splat (HBM-bound)
     e = splat_with_neighbors<PD, V, true>(a, geo, Lv, Sv, a.values, nullptr, a.v0, STAGE_SPLAT_FWD);
     if (e != cudaSuccess) return e;
     // blur in axis order 0..pd (permutohedral.cu:585)
     e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0);
     if (e != cudaSuccess) return e;
-    return launch_slice<PD, V, true>(a, geo, Lv, a.out, a.wout, a.v0, a.v1);
+    e = launch_slice<PD, V, true>(a, geo, Lv, a.out, a.wout, a.v0, a.v1);
+    PL_GROUP(STAGE_GROUP_FILTER_FWD, a.stream, false);
+    return e;
 }
 
 template <int PD, int V>
@@ -355,19 +360,24 @@ cudaError_t backward_v(const CallArgs& a) {
     if (a.lattice_state == 0) {   // rebuild (permutohedral.cu:615-635); the tile build zeroes the rows
         e = build_lattice<PD>(a, geo, Lv, Sv, a.v0, CPB);
         if (e != cudaSuccess) return e;
+        PL_GROUP(STAGE_GROUP_FILTER_BWD, a.stream, true);
         e = splat_with_neighbors<PD, V, false>(a, geo, Lv, Sv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
     } else if (a.lattice_state == 1) {   // rows zeroed by the forward's tile build
+        PL_GROUP(STAGE_GROUP_FILTER_BWD, a.stream, true);
         PL_LAUNCH(STAGE_SPLAT_BWD, a.stream,
                   e = launch_k(k_splat<PD, V, false>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false,
                                a.values, a.weight_in, geo, Lv, Sv, 0, a.v0));
     } else {   // used by an earlier backward: zero the rows and splat in one launch
+        PL_GROUP(STAGE_GROUP_FILTER_BWD, a.stream, true);
         e = splat_zeroed<PD, V, false>(a, geo, Lv, a.values, a.weight_in, a.v0, STAGE_SPLAT_BWD);
     }
     if (e != cudaSuccess) return e;
     // blur in axis order pd..0 (permutohedral.cu:647)
     e = launch_blur_all<PD, CPB>(a, Lv, a.v0, a.v1, 1);
     if (e != cudaSuccess) return e;
-    return launch_slice<PD, V, false>(a, geo, Lv, a.out, nullptr, a.v0, a.v1);
+    e = launch_slice<PD, V, false>(a, geo, Lv, a.out, nullptr, a.v0, a.v1);
+    PL_GROUP(STAGE_GROUP_FILTER_BWD, a.stream, false);
+    return e;
 }
 
 // Forward filter of new values on a kept lattice (built by a forward call on

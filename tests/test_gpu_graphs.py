@@ -170,3 +170,34 @@ def test_kept_lattice_filter_loop_replays(lib):
         b.check()
     c1, r1 = _stats(lib)
     assert c1 - c0 == 2 and r1 - r0 == 6
+
+
+def test_profiling_runs_without_graphs_and_times_groups(lib):
+    """Profiling (per launch, or per launch group) runs the calls directly and
+    records one interval per launch or per group."""
+    from plattice_pytorch_b200 import _lib
+    dev = torch.device("cuda:0")
+    lib.plattice_set_graph_cache(16)
+    b = Buffers("ref_blobs64_pd5_vd3.npz", dev)
+    for _ in range(2):   # a graph exists for these buffers from here on
+        assert b.forward(lib) == 0 and b.backward(lib, 1) == 0
+    _lib.profile_read()
+    try:
+        c0, r0 = _stats(lib)
+        _lib.profile_enable(True)
+        assert b.forward(lib) == 0 and b.backward(lib, 1) == 0
+        per = _lib.profile_read()
+        _lib.profile_enable(True, groups=True)
+        assert b.forward(lib) == 0 and b.backward(lib, 1) == 0
+        grp = _lib.profile_read()
+        assert _stats(lib) == (c0, r0)   # no graph launched while profiling
+    finally:
+        _lib.profile_enable(False)
+    b.check()
+    for st in ("tile_build", "clear", "insert", "splat_fwd", "blur_fwd", "slice_fwd", "splat_bwd", "blur_bwd",
+               "slice_bwd"):
+        assert per[st][1] == 1 and per[st][0] > 0.0, st
+    assert all(per[g][1] == 0 for g in ("build", "filter_fwd", "filter_bwd"))
+    for g in ("build", "filter_fwd", "filter_bwd"):
+        assert grp[g][1] == 1 and grp[g][0] > 0.0, g
+    assert all(grp[st][1] == 0 for st in ("tile_build", "splat_fwd", "slice_bwd"))
