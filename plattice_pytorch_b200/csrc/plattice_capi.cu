@@ -155,8 +155,9 @@ static int sm_count_current() {
 // graph on the caller's stream after pointing the status-reporting kernel at
 // the call's status-ring slot.  One graph launch replaces the seven launches
 // of a forward (three of a backward or of a kept-lattice filter) on the host.  Graphs are kept per CUDA
-// context in a small least-recently-used cache; calls that profile, and the
-// no-allocation entry point (instantiating a graph allocates), run directly.
+// context in a small least-recently-used cache; calls that profile, calls on
+// a stream the caller is capturing, and the no-allocation entry point
+// (instantiating a graph allocates) run directly.
 namespace {
 
 struct GraphKey {
@@ -224,6 +225,14 @@ void graph_free(GraphEntry* g) {
 static cudaError_t run_call(const GraphKey& key, pl::CallArgs& a, cudaError_t (*dispatch)(const pl::CallArgs&)) {
     const int cap = graph_capacity();
     if (cap <= 0 || pl::prof_enabled()) return dispatch(a);
+    // a caller that captures its own stream (e.g. into a CUDA graph of its
+    // own) gets the launches themselves in its capture
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(a.stream, &cs) != cudaSuccess) {
+        cudaGetLastError();
+        return dispatch(a);
+    }
+    if (cs != cudaStreamCaptureStatusNone) return dispatch(a);
     std::lock_guard<std::mutex> lk(g_graph_mu);
     GraphCache* gc = graph_cache();
     if (!gc) return dispatch(a);

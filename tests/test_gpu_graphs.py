@@ -201,3 +201,45 @@ def test_profiling_runs_without_graphs_and_times_groups(lib):
     for g in ("build", "filter_fwd", "filter_bwd"):
         assert grp[g][1] == 1 and grp[g][0] > 0.0, g
     assert all(grp[st][1] == 0 for st in ("tile_build", "splat_fwd", "slice_bwd"))
+
+
+def test_capture_in_a_torch_cuda_graph(lib):
+    """Forward + backward captured by the caller in a torch.cuda.CUDAGraph
+    (the library records its launches into the caller's capture, no graph of
+    its own) and replayed: the replay on the golden inputs gives the golden
+    results, and after new values are copied into the captured input the
+    replay equals an eager call on them."""
+    from plattice_pytorch_b200 import PLOO
+    dev = torch.device("cuda:0")
+    lib.plattice_set_graph_cache(16)
+    d = np.load(os.path.join(GOLDEN, "ref_blobs64_pd5_vd3.npz"))
+    f = torch.from_numpy(d["features"]).to(dev)
+    v = torch.from_numpy(d["values"]).to(dev)
+    g = torch.from_numpy(d["grad"]).to(dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):   # warm-up outside the capture (kernel attributes, lazy loading)
+        for _ in range(2):
+            wo, out, lat = PLOO.lattice_forward(f, v)
+            PLOO.lattice_backward(f, g, wo, lat)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    cg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(cg):
+        wo_c, out_c, lat_c = PLOO.lattice_forward(f, v)
+        gr_c = PLOO.lattice_backward(f, g, wo_c, lat_c)
+    cg.replay()
+    torch.cuda.synchronize()
+    assert allclose_report(out_c.cpu().numpy(), d["out"], RTOL, ATOL) <= 1.0
+    assert allclose_report(wo_c.cpu().numpy(), d["weight"], RTOL, ATOL) <= 1.0
+    assert allclose_report(gr_c.cpu().numpy(), d["grad_out"], RTOL, ATOL) <= 1.0
+    v2 = torch.rand_like(v)
+    v.copy_(v2)
+    cg.replay()
+    wo_e, out_e, lat_e = PLOO.lattice_forward(f, v2)
+    gr_e = PLOO.lattice_backward(f, g, wo_e, lat_e)
+    torch.cuda.synchronize()
+    assert allclose_report(out_c.cpu().numpy(), out_e.cpu().numpy(), RTOL, ATOL) <= 1.0
+    assert allclose_report(gr_c.cpu().numpy(), gr_e.cpu().numpy(), RTOL, ATOL) <= 1.0
+    del cg
+    PLOO.check_device_status()
