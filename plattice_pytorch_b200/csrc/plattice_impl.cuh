@@ -164,6 +164,14 @@ cudaError_t blur_attr(int* per_sm) {
     return *per_sm < 1 ? cudaErrorLaunchOutOfResources : cudaSuccess;
 }
 
+// co-resident CTAs per SM of the insert
+template <int PD>
+cudaError_t insert_attr(int* per_sm) {
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k_insert<PD>, 256, 0);
+    if (e != cudaSuccess) return e;
+    return *per_sm < 1 ? cudaErrorLaunchOutOfResources : cudaSuccess;
+}
+
 // Build the lattice: tile dedup (which also zeroes the lattice value rows
 // `zero` of cp floats each, and `zero_b` of cpb floats when set), table clear,
 // global insert, vertex ids.  Blur neighbours follow, with the first splat.
@@ -185,7 +193,11 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_CLEAR, s, e = launch_k(k_clear, dim3(grid), dim3(256), 0, s, false, geo, Lv, Sv));
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_INSERT, s, e = launch_k(k_insert<PD>, dim3(grid * 2), dim3(256), 0, s, false, geo, Lv, Sv));
+    int per_sm = 0;   // the insert's co-resident CTAs per SM
+    e = kernel_once(reinterpret_cast<const void*>(k_insert<PD>), insert_attr<PD>, &per_sm);
+    if (e != cudaSuccess) return e;
+    PL_LAUNCH(STAGE_INSERT, s,
+              e = launch_k(k_insert<PD>, dim3(grid * 2), dim3(256), 0, s, false, geo, Lv, Sv, a.sm_count * per_sm));
     PL_GROUP(STAGE_GROUP_BUILD, s, false);
     return e;
 }
@@ -434,6 +446,7 @@ cudaError_t prepare_v(const CallArgs&) {
     int n = 0;
     if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CPF>), blur_attr<PD, CPF>, &n);
     if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CPB>), blur_attr<PD, CPB>, &n);
+    if (e == cudaSuccess) e = kernel_once(reinterpret_cast<const void*>(k_insert<PD>), insert_attr<PD>, &n);
     const void* fns[] = {reinterpret_cast<const void*>(k_tile_build<PD>), reinterpret_cast<const void*>(k_clear),
                          reinterpret_cast<const void*>(k_insert<PD>),
                          Cfg<PD>::P == 256 ? reinterpret_cast<const void*>(k_splat_nbr<PD, V, true>)

@@ -939,8 +939,15 @@ __device__ __forceinline__ int neighbour_find(const uint32_t* __restrict__ table
 // the staged index, and lookups map it to the vertex id through vid_of.
 constexpr int kInsertKpt = 4;
 
+//
+// The launch is oversubscribed (more CTAs than are co-resident).  When the
+// co-resident CTAs (`resident`) can hold every key with two per thread, only
+// they work, each key in flight at once (one wave); otherwise every CTA takes
+// chunks of one key per thread, or of KPT keys per thread when the keys
+// outnumber the grid's threads KPT to one (many short-lived CTAs, so that a
+// CTA waiting on a long probe leaves its SM to others).
 template <int PD>
-__global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
+__global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S, int resident) {
     constexpr int CW = Cfg<PD>::CW, NW = Cfg<PD>::NW, KPT = kInsertKpt;
     __shared__ int s_wcnt[8], s_base;
     const int U = L.hdr->u_total;
@@ -948,10 +955,14 @@ __global__ void __launch_bounds__(256) k_insert(Geo geo, LatView L, ScrView S) {
     const bool use_filter = L.hdr->cap_log2 >= geo.filter_min_log2;
     const TableFmt f = table_fmt(geo);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    // KPT keys per thread only when there are enough keys to occupy the grid that way
-    const int kpt = U >= gridDim.x * blockDim.x * KPT ? KPT : 1;
+    const int res = resident < (int)gridDim.x ? resident : (int)gridDim.x;
+    const bool one_wave = U <= 2 * res * (int)blockDim.x;
+    const int ctas = one_wave ? res : (int)gridDim.x;
+    if ((int)blockIdx.x >= ctas) return;
+    const int kpt = one_wave ? (U > res * (int)blockDim.x ? 2 : 1)
+                             : (U >= (int)gridDim.x * (int)blockDim.x * KPT ? KPT : 1);
     const int chunk = blockDim.x * kpt;
-    for (int i0 = blockIdx.x * chunk; i0 < U; i0 += gridDim.x * chunk) {   // block-uniform
+    for (int i0 = blockIdx.x * chunk; i0 < U; i0 += ctas * chunk) {   // block-uniform
         uint32_t h[KPT], c0[KPT];
         int owner[KPT];
 #pragma unroll
