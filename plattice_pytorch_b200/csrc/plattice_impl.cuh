@@ -203,14 +203,15 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
 }
 
 // The splat right after a build, with the blur-neighbour lookups in the same
-// launch (as many lookup threads as a k_neighbors grid of 8 x 256 threads
-// per SM).
+// launch.
 template <int PD, int V, bool FWD>
 cudaError_t splat_with_neighbors(const CallArgs& a, const Geo& geo, const LatView& Lv, const ScrView& Sv,
                                  const float* vals, const float* wt, float* rows, int stage) {
     cudaError_t e;
     if constexpr (Cfg<PD>::P == 256) {
-        const int nbr_blocks = a.sm_count * 8 * kNbrThreads / Cfg<PD>::P;
+        // lookup CTAs: as many threads as four 256-thread CTAs per SM, so that
+        // the first wave leaves room for splat tiles beside them
+        const int nbr_blocks = a.sm_count * 4 * kNbrThreads / Cfg<PD>::P;
         PL_LAUNCH(stage, a.stream,
                   e = launch_k(k_splat_nbr<PD, V, FWD>, dim3(nbr_blocks + a.lay.tiles), dim3(Cfg<PD>::P), 0,
                                a.stream, false, vals, wt, geo, Lv, Sv, rows, nbr_blocks));
