@@ -400,6 +400,14 @@ def timed_e2e(fn, host, steps, dev):
     return e0.elapsed_time(e1)
 
 
+def graph_stats(impl):
+    """(captures, replays) of the library's call graphs so far ((0, 0) for the reference)."""
+    if impl != "ours":
+        return 0, 0
+    from plattice_pytorch_b200 import PLOO
+    return PLOO.graph_cache_stats()
+
+
 def hbm_peak():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -623,7 +631,9 @@ def main():
     barrier(world_eff)
     torch.cuda.synchronize()
     host_us = []
+    graphs0 = graph_stats(args.impl)
     per_step = timed_device(fn, batch, args.steps, flush, host_us)
+    graphs1 = graph_stats(args.impl)
     torch.cuda.synchronize()
     barrier(world_eff)
     # the median step when there are enough steps for it to mean something,
@@ -739,9 +749,10 @@ def main():
             "measured": atomics_from_profiles() if args.workload == "voronoi1024_pd5_vd3" else {},
             "measured_source": "profiles/atomics.txt (ncu, one launch each, this workload)"}
         res["gpu_launches"] = int(round(launches_per_step * args.steps * launch_mult))
-        from plattice_pytorch_b200 import PLOO as _P
-        cap, rep = _P.graph_cache_stats()
+        cap, rep = graph_stats(args.impl)
         res["call_graphs"] = {"captured": cap, "replayed": rep,
+                              "captured_in_timed_steps": graphs1[0] - graphs0[0],
+                              "replayed_in_timed_steps": graphs1[1] - graphs0[1],
                               "note": "calls repeated with the same buffers run as one CUDA graph launch"}
 
     if rank == 0 and world_eff == 1 and not args.no_cpu_baseline:
