@@ -259,10 +259,16 @@ static cudaError_t run_call(const GraphKey& key, pl::CallArgs& a, cudaError_t (*
         if (gc->seen.size() > 32) gc->seen.erase(gc->seen.begin());
         return dispatch(a);
     }
-    // second sighting: capture, instantiate, launch
+    // second sighting: capture, instantiate, launch; anything that fails on
+    // the way (e.g. while another thread captures in global mode) leaves the
+    // call to run directly
     cudaError_t e = cudaSuccess;
     if (!gc->capture) e = cudaStreamCreateWithFlags(&gc->capture, cudaStreamNonBlocking);
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess) {
+        gc->capture = nullptr;
+        cudaGetLastError();
+        return dispatch(a);
+    }
     GraphEntry* g = new GraphEntry();
     g->key = key;
     pl::CallArgs c = a;
@@ -271,7 +277,8 @@ static cudaError_t run_call(const GraphKey& key, pl::CallArgs& a, cudaError_t (*
     e = cudaStreamBeginCapture(gc->capture, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) {
         delete g;
-        return e;
+        cudaGetLastError();
+        return dispatch(a);
     }
     const cudaError_t ed = dispatch(c);
     const cudaError_t ee = cudaStreamEndCapture(gc->capture, &g->graph);
