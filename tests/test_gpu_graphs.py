@@ -243,3 +243,58 @@ def test_capture_in_a_torch_cuda_graph(lib):
     assert allclose_report(gr_c.cpu().numpy(), gr_e.cpu().numpy(), RTOL, ATOL) <= 1.0
     del cg
     PLOO.check_device_status()
+
+
+def test_eviction_keeps_results_exact(lib):
+    """A cache of two graphs cycled through three sets of buffers: graphs are
+    evicted and captured again, and every call still gives the golden result."""
+    dev = torch.device("cuda:0")
+    assert lib.plattice_set_graph_cache(2) == 0
+    try:
+        sets = [Buffers("ref_blobs64_pd5_vd3.npz", dev) for _ in range(3)]
+        c0, _ = _stats(lib)
+        for _ in range(4):
+            for b in sets:
+                b.out.fill_(float("nan"))
+                b.gout.fill_(float("nan"))
+                assert b.forward(lib) == 0 and b.backward(lib, 1) == 0
+                b.check()
+        assert _stats(lib)[0] - c0 >= 4   # more captures than the cache holds: evictions happened
+    finally:
+        lib.plattice_set_graph_cache(16)
+
+
+def test_two_host_threads(lib):
+    """Two host threads, each with its own buffers and stream, call forward and
+    backward concurrently (ctypes releases the GIL during the calls); every
+    result equals the golden one."""
+    import threading
+    dev = torch.device("cuda:0")
+    lib.plattice_set_graph_cache(16)
+    errors = []
+
+    def worker(name):
+        try:
+            torch.cuda.set_device(dev)
+            s = torch.cuda.Stream(dev)
+            with torch.cuda.stream(s):
+                b = Buffers(name, dev)
+                b.stream = s.cuda_stream
+                for _ in range(6):
+                    b.out.fill_(float("nan"))
+                    b.gout.fill_(float("nan"))
+                    assert b.forward(lib) == 0 and b.backward(lib, 1) == 0
+                    s.synchronize()
+                    assert allclose_report(b.out.cpu().numpy(), b.d["out"], RTOL, ATOL) <= 1.0
+                    assert allclose_report(b.gout.cpu().numpy(), b.d["grad_out"], RTOL, ATOL) <= 1.0
+        except BaseException as e:   # reported by the main thread
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=worker, args=(n,))
+               for n in ("ref_blobs64_pd5_vd3.npz", "ref_randn24x20_pd16_vd1.npz")]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=120)
+    assert not any(th.is_alive() for th in threads)
+    assert not errors, errors
