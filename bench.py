@@ -343,26 +343,30 @@ def feature_grad_line(args, dev):
                        "vd": int(v.shape[2]), "l2": "flushed between timed steps"}}
 
 
+RING = 3   # steps of the end-to-end pipeline in flight
+
+
 def timed_e2e(fn, host, steps, dev):
     """Whole-loop CUDA-event time (ms) of `steps` end-to-end steps from pinned
-    host buffers, including H2D of the inputs and D2H of out and grad.
+    host buffers, including H2D of the inputs (features, values, upstream
+    gradient) and D2H of the step's result, the value gradient.  The forward
+    output stays on the device, where it feeds the loss that the upstream
+    gradient stands for.
 
     The same pipeline serves both arms: each step's inputs are copied in on an
     input stream, the filter runs on the default stream (where the reference
-    launches its kernels whatever the current stream is), and out and grad are
+    launches its kernels whatever the current stream is), and the gradient is
     copied back on an output stream, with events ordering the three.  The two
     copy directions and the kernels of different steps overlap; every step
-    still moves its own inputs and results."""
+    still moves its own inputs and result."""
     s_in = torch.cuda.Stream(dev)
     s_out = torch.cuda.Stream(dev)
     comp = torch.cuda.default_stream(dev)
-    outs = [[(torch.empty(h[1].shape, pin_memory=True), torch.empty(h[1].shape, pin_memory=True))
-             for h in host] for _ in range(2)]
-    # device input buffers of RING steps, reused once the step that read them
-    # has finished; the host waits for that step before reusing its slot, so it
-    # runs at most RING steps ahead (a bounded queue, as in a serving loop, and
-    # no allocator growth inside the timed loop)
-    RING = 3
+    outs = [[torch.empty(h[1].shape, pin_memory=True) for h in host] for _ in range(RING)]
+    # device input buffers of RING steps (and host result buffers), reused once
+    # the step that used them has finished; the host waits for that step
+    # before reusing its slot, so it runs at most RING steps ahead (a bounded
+    # queue, as in a serving loop, and no allocator growth inside the timed loop)
     dins = [[tuple(torch.empty(x.shape, dtype=x.dtype, device=dev) for x in hh) for hh in host]
             for _ in range(RING)]
     freed = [None] * RING
@@ -375,7 +379,7 @@ def timed_e2e(fn, host, steps, dev):
         if freed[r] is not None:
             freed[r].synchronize()
         for k, (hf, hv, hg) in enumerate(host):
-            ho, hgr = outs[i % 2][k]
+            hgr = outs[r][k]
             f, v, g = dins[r][k]
             with torch.cuda.stream(s_in):
                 f.copy_(hf, non_blocking=True)
@@ -384,15 +388,12 @@ def timed_e2e(fn, host, steps, dev):
             comp.wait_stream(s_in)
             with torch.cuda.stream(comp):
                 out, gv = step(fn, f, v.detach().requires_grad_(True), g)
-                out = out.detach()
             s_out.wait_stream(comp)
-            out.record_stream(s_out)
             gv.record_stream(s_out)
             with torch.cuda.stream(s_out):
-                ho.copy_(out, non_blocking=True)
                 hgr.copy_(gv, non_blocking=True)
         freed[r] = torch.cuda.Event()
-        freed[r].record(comp)
+        freed[r].record(s_out)   # the step's inputs are read and its result copied out
     comp.wait_stream(s_in)
     comp.wait_stream(s_out)
     e1.record(comp)
@@ -660,7 +661,7 @@ def main():
     px_total = imgs_job * n * args.steps
     value = px_total / (t_dev * 1e-3) / 1e6
     h2d = sum(int(x.numel()) * 4 for hh in host for x in hh)
-    d2h = sum(2 * int(hh[1].numel()) * 4 for hh in host)
+    d2h = sum(int(hh[1].numel()) * 4 for hh in host)   # the value gradient
     res = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world_eff, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": t_dev / args.steps, "higher_is_better": True,
@@ -682,7 +683,8 @@ def main():
                            "PermutoLatticeFunction forward") + " + torch.autograd.grad backward"},
         "e2e": {"value": px_total / (t_e2e * 1e-3) / 1e6, "unit": UNIT,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "pipeline": "H2D on an input stream, filter on the default stream, D2H on an output "
+                "pipeline": "H2D of features, values and upstream gradient on an input stream, filter on "
+                            "the default stream, D2H of the value gradient (the step's result) on an output "
                             "stream, ordered by events (identical for both arms)"},
         "clocks": clk,
     }
