@@ -81,6 +81,27 @@ def build(jobs=None, verbose_ptxas=False, force=False):
     return LIB
 
 
+TORCH_EXT = os.path.join(HERE, "_plattice_torch.so")
+
+
+def build_torch_extension(force=False):
+    """Compile csrc/plattice_torch.cpp (PermutoLatticeFunction in C++) as the
+    torch extension module _plattice_torch, next to this file; returns its path."""
+    src = os.path.join(CSRC, "plattice_torch.cpp")
+    deps = [src, os.path.join(ROOT, "include", "plattice.h"), os.path.abspath(__file__)]
+    if not force and not _stale(TORCH_EXT, deps):
+        return TORCH_EXT
+    from torch.utils.cpp_extension import load
+    bdir = os.path.join(BUILD, "torch_ext")
+    os.makedirs(bdir, exist_ok=True)
+    load(name="_plattice_torch", sources=[src], build_directory=bdir, extra_cflags=["-O3"],
+         extra_include_paths=[os.path.join(ROOT, "include")], with_cuda=True, verbose=False)
+    built = os.path.join(bdir, "_plattice_torch.so")
+    shutil.copyfile(built, TORCH_EXT + ".tmp")
+    os.replace(TORCH_EXT + ".tmp", TORCH_EXT)
+    return TORCH_EXT
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--jobs", type=int, default=None)
@@ -88,6 +109,7 @@ def main():
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
     print(build(a.jobs, a.verbose_ptxas, a.force))
+    print(build_torch_extension(a.force))
 
 
 if __name__ == "__main__":

@@ -21,18 +21,59 @@ values on a kept lattice -- the ``PLOO.Lattice`` of an earlier forward on the
 same features -- without rebuilding it, as the iterations of a mean-field CRF
 do; its backward is the value gradient on the same lattice.
 """
+import ctypes
+
 import torch
 from torch.autograd import Function
 from torch.autograd.function import once_differentiable
 from torch.nn import Module
 
-from . import PLOO
+from . import PLOO, _lib
+
+_UNSET = object()
+_EXT = _UNSET
+
+
+def _cpp_function():
+    """The C++ build of PermutoLatticeFunction (extension module _plattice_torch,
+    built next to the library), pointed at the loaded library's entry points;
+    None when the extension is not built."""
+    global _EXT
+    if _EXT is _UNSET:
+        try:
+            from . import _plattice_torch as m
+        except ImportError:
+            _EXT = None
+            return None
+        L = _lib.lib()
+        addr = lambda f: ctypes.cast(f, ctypes.c_void_p).value
+        m.set_entry_points(addr(L.plattice_forward), addr(L.plattice_backward), addr(L.plattice_workspace_sizes),
+                           addr(L.plattice_reuse_scratch_size), addr(L.plattice_error_string),
+                           addr(L.plattice_last_error_detail))
+        _EXT = m.permuto_lattice
+    return _EXT
 
 __all__ = ["PermutoLatticeFunction", "PermutoLattice", "LatticeFilterFunction", "PermutoLatticeBatchFunction",
            "PermutoLatticeFeatureFunction"]
 
 
 class PermutoLatticeFunction(Function):
+    """``PermutoLatticeFunction.apply(feature, values) -> out``.
+
+    ``apply`` runs the C++ build of this Function (the same checks, messages,
+    kept lattice and library calls as forward / backward below, without the
+    Python interpreter between the autograd engine and the library) when the
+    extension is built and PLATTICE_CHECK is off; otherwise, and for arguments
+    that are not tensors, the Python Function below.  Either way the filter
+    runs in libplattice_b200.so."""
+
+    @classmethod
+    def apply(cls, feature, values):
+        fn = None if PLOO._CHECK else _cpp_function()
+        if fn is not None and type(feature) is torch.Tensor and type(values) is torch.Tensor:
+            return fn(feature, values)
+        return super().apply(feature, values)
+
     @staticmethod
     def forward(ctx, feature, values):
         weight, out, lat = PLOO.lattice_forward(feature, values)

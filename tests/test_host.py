@@ -220,3 +220,18 @@ def test_shard_range_partitions_any_batch():
             assert parts[0][0] == 0 and parts[-1][1] == n
             assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
             assert max(p[1] - p[0] for p in parts) - min(p[1] - p[0] for p in parts) <= 1
+
+
+def test_cpp_function_extension_loads_and_checks_inputs(lib):
+    """The C++ build of PermutoLatticeFunction (extension _plattice_torch) loads,
+    takes the library's entry points, and rejects bad inputs with the
+    reference's messages before any device work (CPU tensors here)."""
+    from plattice_pytorch_b200 import plattice
+    if not os.path.exists(os.path.join(ROOT, "plattice_pytorch_b200", "_plattice_torch.so")):
+        pytest.skip("_plattice_torch.so not built (python -m plattice_pytorch_b200.build)")
+    fn = plattice._cpp_function()
+    assert fn is not None
+    with pytest.raises(RuntimeError, match="features must be CUDA"):
+        fn(torch.zeros(4, 4, 5), torch.zeros(4, 4, 3))
+    with pytest.raises(RuntimeError, match="features must be CUDA"):
+        plattice.PermutoLatticeFunction.apply(torch.zeros(4, 4, 5), torch.zeros(4, 4, 3))
