@@ -153,6 +153,13 @@ cudaError_t prepare_tile_build() {
     return kernel_once(reinterpret_cast<const void*>(k_tile_build<PD>), tile_build_attr<PD>, &v);
 }
 
+// a grid of `want` CTAs, or fewer when `need` (at least 1) cover the work:
+// small images then launch no CTAs that would exit at once
+inline int capped_grid(long long want, long long need) {
+    if (need < 1) need = 1;
+    return (int)(want < need ? want : need);
+}
+
 // the blur kernel's dynamic shared memory and its co-resident CTAs per SM
 template <int PD, int CP>
 cudaError_t blur_attr(int* per_sm) {
@@ -191,13 +198,18 @@ cudaError_t build_lattice(const CallArgs& a, const Geo& geo, const LatView& Lv, 
               e = launch_k(k_tile_build<PD>, tile_grid(a), dim3(C::P), tile_build_smem_bytes<PD>(), s, false,
                              a.features, geo, ec, Lv, Sv, zero, cp, zero_b, cpb));
     if (e != cudaSuccess) return e;
-    PL_LAUNCH(STAGE_CLEAR, s, e = launch_k(k_clear, dim3(grid), dim3(256), 0, s, false, geo, Lv, Sv));
+    // no more CTAs than the largest table needs (2^cap_max_log2 cells, four a
+    // thread); the insert no more than the staged keys (at most slots)
+    PL_LAUNCH(STAGE_CLEAR, s,
+              e = launch_k(k_clear, dim3(capped_grid(grid, ((1ll << a.lay.cap_max_log2) / 4 + 255) / 256)), dim3(256),
+                           0, s, false, geo, Lv, Sv));
     if (e != cudaSuccess) return e;
     int per_sm = 0;   // the insert's co-resident CTAs per SM
     e = kernel_once(reinterpret_cast<const void*>(k_insert<PD>), insert_attr<PD>, &per_sm);
     if (e != cudaSuccess) return e;
     PL_LAUNCH(STAGE_INSERT, s,
-              e = launch_k(k_insert<PD>, dim3(grid * 2), dim3(256), 0, s, false, geo, Lv, Sv, a.sm_count * per_sm));
+              e = launch_k(k_insert<PD>, dim3(capped_grid(grid * 2, (a.lay.slots + 255) / 256)), dim3(256), 0, s, false,
+                           geo, Lv, Sv, a.sm_count * per_sm));
     PL_GROUP(STAGE_GROUP_BUILD, s, false);
     return e;
 }
@@ -240,7 +252,8 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
     int n = 0;
     cudaError_t e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CP>), blur_attr<PD, CP>, &n);
     if (e != cudaSuccess) return e;
-    const int blocks = a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm);
+    const int blocks = capped_grid((long long)a.sm_count * (n < kCoopPerSm ? n : kCoopPerSm),
+                                   (a.lay.slots + kBlurThreads - 1) / kBlurThreads);
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
               e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), kBlurQueueBytes, a.stream, true, Lv,
                            b0, b1, a.bstate, reverse, final_flag, a.blur_flags));
