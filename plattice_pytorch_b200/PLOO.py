@@ -37,9 +37,19 @@ from . import _lib
 __all__ = ["forward", "backward", "Lattice", "lattice_forward", "lattice_backward",
            "lattice_filter", "lattice_filter_backward", "feature_grad", "BatchLattice", "batch_forward",
            "batch_backward", "forward_batch", "backward_batch", "lattice_info", "vertex_keys",
-           "check_device_status", "prepare", "set_graph_cache", "graph_cache_stats"]
+           "check_device_status", "prepare", "set_graph_cache", "graph_cache_stats", "set_keep_lattice",
+           "get_keep_lattice"]
 
 _CHECK = os.environ.get("PLATTICE_CHECK", "0") not in ("", "0")
+
+# Whether the autograd Functions (PermutoLatticeFunction and its batch form)
+# and forward / forward_batch keep the forward's lattice for the backward (the
+# default: the backward skips the rebuild) or keep nothing and rebuild it in
+# the backward, as the reference does (plattice.py:11-19,
+# permutohedral.cu:615-635).  Off, a forward retains no device memory beyond
+# its outputs, and the backward allocates the full lattice and scratch for its
+# duration.  PLATTICE_KEEP_LATTICE=0 or set_keep_lattice(False).
+_KEEP = os.environ.get("PLATTICE_KEEP_LATTICE", "1") not in ("", "0")
 
 _F32 = torch.float32
 _cur_dev = torch._C._cuda_getDevice
@@ -448,7 +458,7 @@ def forward_batch(features, values):
     """``forward`` over ``[B,H,W,...]`` -> ``[weight [B,H,W,1], out [B,H,W,vd]]``."""
     global _last_batch
     weight, out, lat = batch_forward(features, values)
-    _last_batch = lat
+    _last_batch = lat if _KEEP else None
     return [weight, out]
 
 
@@ -466,7 +476,7 @@ def forward(features, values):
     """``PLOO.forward(features, values) -> [weight_out [H,W,1], out [H,W,vd]]``."""
     global _last
     weight, out, lat = lattice_forward(features, values)
-    _last = lat
+    _last = lat if _KEEP else None
     return [weight, out]
 
 
@@ -530,6 +540,24 @@ def set_lattice_precision(precision):
     rc = _lib_h().plattice_set_lattice_precision(bits)
     if rc != _lib.OK:
         _raise("plattice_set_lattice_precision", rc, "")
+
+
+def set_keep_lattice(keep):
+    """Keep the forward's lattice for the backward (``True``, the default) or,
+    as the reference does, keep nothing and rebuild it in the backward
+    (``False``): no device memory retained between the two (482 MiB at
+    1024 x 1024 pd 5 otherwise), for a rebuild in every backward.  Applies to
+    the forwards made after it: PermutoLatticeFunction,
+    PermutoLatticeBatchFunction, forward and forward_batch.  Results do not
+    depend on it (within the float tolerance of the splat's summation order)."""
+    global _KEEP
+    _require(isinstance(keep, bool), "keep must be a bool")
+    _KEEP = keep
+
+
+def get_keep_lattice():
+    """The setting of :func:`set_keep_lattice`."""
+    return _KEEP
 
 
 def get_lattice_precision():

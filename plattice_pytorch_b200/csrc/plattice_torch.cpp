@@ -95,7 +95,10 @@ using torch::autograd::AutogradContext;
 using torch::autograd::variable_list;
 
 struct PermutoLatticeFn : public torch::autograd::Function<PermutoLatticeFn> {
-    static at::Tensor forward(AutogradContext* ctx, const at::Tensor& features, const at::Tensor& values) {
+    // keep: the lattice stays on the context for the backward; otherwise
+    // nothing is kept and the backward rebuilds it, as the reference does
+    static at::Tensor forward(AutogradContext* ctx, const at::Tensor& features, const at::Tensor& values,
+                              bool keep) {
         TORCH_CHECK(g_fn.forward, "the plattice library's entry points are not set");
         check_input(features, "features");
         check_input(values, "values");
@@ -124,13 +127,15 @@ struct PermutoLatticeFn : public torch::autograd::Function<PermutoLatticeFn> {
             TORCH_CHECK(rc == 0, failure("plattice_forward", rc, h, w, pd, vd));
         }
         ctx->save_for_backward({weight, features});
-        ctx->saved_data["lattice"] = lattice;
+        ctx->saved_data["keep"] = keep;
+        if (keep) ctx->saved_data["lattice"] = lattice;
         ctx->saved_data["used"] = false;
         return out;
     }
 
     // value gradient on the kept lattice (the reference rebuilds it,
-    // permutohedral.cu:615-635); no gradient for the features (plattice.py:19)
+    // permutohedral.cu:615-635, as this does when the forward kept nothing);
+    // no gradient for the features (plattice.py:19)
     static variable_list backward(AutogradContext* ctx, variable_list grads) {
         const auto saved = ctx->get_saved_variables();
         const at::Tensor& weight = saved[0];
@@ -148,25 +153,31 @@ struct PermutoLatticeFn : public torch::autograd::Function<PermutoLatticeFn> {
         const int pd = (int)features.size(2), vd = (int)grad.size(2);
         const c10::cuda::CUDAGuard guard(features.device());
         const auto opts = features.options();
-        at::Tensor lattice = ctx->saved_data["lattice"].toTensor();
+        const bool keep = ctx->saved_data["keep"].toBool();
         const bool used = ctx->saved_data["used"].toBool();
         const Sizes s = sizes_of(h, w, pd, vd);
+        // kept: the lattice and the reuse scratch (state 1, or 2 after an
+        // earlier backward); else a lattice built here (state 0), full scratch
+        at::Tensor lattice =
+            keep ? ctx->saved_data["lattice"].toTensor() : at::empty({(int64_t)s.lattice}, opts.dtype(at::kByte));
+        const int state = keep ? (used ? 2 : 1) : 0;
+        const size_t sbytes = keep ? s.reuse : s.scratch;
         at::Tensor grad_values = at::empty({h, w, vd}, opts);
         {
-            at::Tensor scratch = at::empty({(int64_t)s.reuse}, opts.dtype(at::kByte));
+            at::Tensor scratch = at::empty({(int64_t)sbytes}, opts.dtype(at::kByte));
             const int rc = g_fn.backward(grad_values.data_ptr<float>(), grad.data_ptr<float>(),
                                          weight.data_ptr<float>(), features.data_ptr<float>(), lattice.data_ptr(),
-                                         (size_t)lattice.numel(), used ? 2 : 1, scratch.data_ptr(), s.reuse, pd, vd,
-                                         w, h, at::cuda::getCurrentCUDAStream(features.device().index()).stream());
+                                         (size_t)lattice.numel(), state, scratch.data_ptr(), sbytes, pd, vd, w, h,
+                                         at::cuda::getCurrentCUDAStream(features.device().index()).stream());
             TORCH_CHECK(rc == 0, failure("plattice_backward", rc, h, w, pd, vd));
         }
         ctx->saved_data["used"] = true;
-        return {at::Tensor(), grad_values};
+        return {at::Tensor(), grad_values, at::Tensor()};
     }
 };
 
-at::Tensor permuto_lattice(const at::Tensor& features, const at::Tensor& values) {
-    return PermutoLatticeFn::apply(features, values);
+at::Tensor permuto_lattice(const at::Tensor& features, const at::Tensor& values, bool keep) {
+    return PermutoLatticeFn::apply(features, values, keep);
 }
 
 }  // namespace
@@ -176,6 +187,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("set_entry_points", &set_entry_points,
           "addresses of plattice_forward, plattice_backward, plattice_workspace_sizes, "
           "plattice_reuse_scratch_size, plattice_error_string, plattice_last_error_detail");
-    m.def("permuto_lattice", &permuto_lattice, "forward of PermutoLatticeFunction (out); backward by autograd",
-          py::call_guard<py::gil_scoped_release>());
+    m.def("permuto_lattice", &permuto_lattice,
+          "forward of PermutoLatticeFunction (out); backward by autograd, on the kept lattice (keep) or on one "
+          "rebuilt there",
+          py::arg("features"), py::arg("values"), py::arg("keep") = true, py::call_guard<py::gil_scoped_release>());
 }

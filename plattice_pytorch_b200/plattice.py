@@ -6,7 +6,9 @@ filtered values and saves ``(weight, feature)``; backward returns
 reference (plattice.py:19).  ``PermutoLattice`` is the nn.Module wrapper.
 
 Unlike the reference, the lattice that forward builds is kept on the autograd
-context and reused by backward (no rebuild).
+context and reused by backward (no rebuild), unless ``PLOO.set_keep_lattice(False)``
+(or PLATTICE_KEEP_LATTICE=0) asks for the reference's behaviour: nothing kept,
+the lattice rebuilt in backward.
 
 ``PermutoLatticeBatchFunction`` (no counterpart in the reference) is
 ``PermutoLatticeFunction`` over a batch ``[B,H,W,...]`` in one library call,
@@ -71,14 +73,14 @@ class PermutoLatticeFunction(Function):
     def apply(cls, feature, values):
         fn = None if PLOO._CHECK else _cpp_function()
         if fn is not None and type(feature) is torch.Tensor and type(values) is torch.Tensor:
-            return fn(feature, values)
+            return fn(feature, values, PLOO._KEEP)
         return super().apply(feature, values)
 
     @staticmethod
     def forward(ctx, feature, values):
         weight, out, lat = PLOO.lattice_forward(feature, values)
         ctx.save_for_backward(weight, feature)
-        ctx.lattice = lat
+        ctx.lattice = lat if PLOO._KEEP else None
         return out
 
     @staticmethod
@@ -120,7 +122,7 @@ class PermutoLatticeBatchFunction(Function):
     def forward(ctx, feature, values):
         weight, out, lat = PLOO.batch_forward(feature, values)
         ctx.save_for_backward(weight, feature)
-        ctx.lattice = lat
+        ctx.lattice = lat if PLOO._KEEP else None
         return out
 
     @staticmethod
