@@ -1781,6 +1781,8 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
 
 constexpr int kBlurHalf = 1;     // flags of k_blur_all: bfloat16 rows in the streaming passes
 constexpr int kBlurStream = 2;   // the streaming passes whatever the lattice's size (tests)
+constexpr int kBlurExit = 4;     // the blur resets the grid-barrier counters itself at its exit (no
+                                 // kernel of the call that follows it does)
 
 // The resident blur: every vertex's row stays in a register of one thread
 // for the K passes, passes in fused pairs (one grid barrier per pair).  CTA b
@@ -1872,7 +1874,21 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
         blur_streaming<PD, CP, false>(L.nbr, bstate, L.hdr, buf0, buf1, reverse, final_flag, M, tid, stride,
                                       blur_queue, phase);
     }
-    grid_exit(L.hdr, nullptr, 0u);
+    // The barrier counters must be zero when the next cooperative kernel on
+    // this lattice starts.  The kernel that follows a blur in stream order
+    // (the slice, or the feature-gradient kernels) zeroes them when it starts
+    // (reset_barrier), after every CTA of the blur has finished; so the blur
+    // ends without the exit protocol's fence and atomics, unless asked for it.
+    if (flags & kBlurExit) grid_exit(L.hdr, nullptr, 0u);
+}
+
+// Zeroes the grid-barrier counters of the lattice (one thread): called at the
+// start of the kernel that follows a blur, whose CTAs have all finished.
+__device__ __forceinline__ void reset_barrier(LatticeHeader* hdr) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        hdr->bar_count = 0u;
+        hdr->bar_gen = 0u;
+    }
 }
 
 // ---------------------------------------------------------------- status
@@ -1907,6 +1923,7 @@ k_slice(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView L, c
     constexpr int CP = FWD ? pad_ch(V + 1) : pad_ch(V);
     constexpr int NC = FWD ? V + 1 : V;
     report_status(st_slot, st_seq, L.hdr);
+    reset_barrier(L.hdr);
     const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
     const int t = threadIdx.x;
     int tile;
@@ -1989,6 +2006,7 @@ k_slice_pipe(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView
     __shared__ uint64_t full[ST];
     __shared__ int vshift[ST];
     report_status(st_slot, st_seq, L.hdr);
+    reset_barrier(L.hdr);
     const float* __restrict__ lat = L.hdr->blur_final ? lat1 : lat0;
     const int t = threadIdx.x;
     const int first = blockIdx.x, stride = gridDim.x;
