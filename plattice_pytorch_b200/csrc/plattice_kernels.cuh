@@ -1232,16 +1232,18 @@ __global__ void __launch_bounds__(kNbrThreads, PD <= 6 ? 8 : 4) k_neighbors(Geo 
 // ---------------------------------------------------------------- grid barrier
 
 // Grid barrier over the CTAs of a cooperative launch (all co-resident): one
-// release-add per CTA on a counter that only grows during the launch (it is
-// zeroed by the kernel before), then acquire polls until all CTAs of this
-// phase have arrived.  The wait is bounded: a CTA that polls kBarrierSpin
-// times records PL_ST_SPIN and continues, so a failure shows in the status
-// word instead of a hang.
+// acquire-release add per CTA on a counter that only grows during the launch
+// (it is zero when the launch starts), then acquire polls until all CTAs of
+// this phase have arrived.  The CTA whose add completes the phase learns it
+// from the add's result and does not poll (one L2 round trip less on the
+// barrier's critical path).  The wait is bounded: a CTA that polls
+// kBarrierSpin times records PL_ST_SPIN and continues, so a failure shows in
+// the status word instead of a hang.
 constexpr int kBarrierSpin = 1 << 22;
 
-__device__ __forceinline__ unsigned atom_add_release(unsigned* p, unsigned v) {
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
     unsigned old;
-    asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
 
@@ -1250,9 +1252,9 @@ __device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase
     ++phase;
     if (threadIdx.x == 0) {
         const unsigned target = phase * gridDim.x;
-        atom_add_release(&hdr->bar_count, 1u);
+        const unsigned arrived = atom_add_acq_rel(&hdr->bar_count, 1u) + 1u;
         int spins = 0;
-        while (ld_acquire(&hdr->bar_count) < target) {
+        while (arrived < target && ld_acquire(&hdr->bar_count) < target) {
             if (++spins > kBarrierSpin) {
                 atomicOr(&hdr->status, PL_ST_SPIN);
                 break;
