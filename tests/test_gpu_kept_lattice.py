@@ -139,3 +139,44 @@ def test_filter_checks_shapes(dev):
         PLOO.lattice_filter(lat, torch.zeros((8, 8, 3), device=dev))
     with pytest.raises(RuntimeError, match="value dimension"):
         PLOO.lattice_filter(lat, torch.zeros((64, 64, 9), device=dev))
+
+
+@pytest.mark.parametrize("streaming", [False, True])
+def test_every_call_kind_in_turn_on_one_lattice(streaming, dev):
+    """The cooperative kernels of a call (the blur; the zero-then-splat of a
+    call on a used lattice) share the lattice's grid-barrier counters, which
+    every call must leave at zero for the next: forward, backward (fresh and
+    used lattice), filter, filter backward and feature gradient in turn on one
+    kept lattice, twice over, each against the same call on a freshly built
+    lattice; the status word stays clear.  Both blur paths (rows in registers,
+    and the streaming passes)."""
+    from plattice_pytorch_b200 import PLOO, _lib
+    from plattice_pytorch_b200.workloads import make_workload
+    L = _lib.lib()
+    wl = make_workload("crf512_pd5_vd3", seed=5)
+    f = torch.from_numpy(wl["features"]).to(dev)
+    v = torch.from_numpy(wl["values"]).to(dev)
+    g = torch.from_numpy(wl["grad"]).to(dev)
+    v2 = torch.roll(v, 7, dims=1).contiguous()
+    g2 = torch.roll(g, 11, dims=0).contiguous()
+    try:
+        L.plattice_debug_set_blur_streaming(1 if streaming else 0)
+        w, out, lat = PLOO.lattice_forward(f, v)
+        wf, outf, _ = PLOO.lattice_forward(f, v)
+        assert _close(out, outf) and _close(w, wf)
+        for _ in range(2):
+            assert _close(PLOO.lattice_backward(f, g, w, lat), PLOO.lattice_backward(f, g, w))
+            assert _close(PLOO.lattice_backward(f, g2, w, lat), PLOO.lattice_backward(f, g2, w))
+            w2, m2 = PLOO.lattice_filter(lat, v2)
+            w2f, m2f = PLOO.forward(f, v2)
+            assert _close(m2, m2f) and _close(w2, w2f)
+            assert _close(PLOO.lattice_filter_backward(lat, g2, w2), PLOO.lattice_backward(f, g2, w2f))
+            _, _, latf = PLOO.lattice_forward(f, v)
+            a = PLOO.feature_grad(lat, f, v, g, w, out).cpu().numpy()
+            b = PLOO.feature_grad(latf, f, v, g, wf, outf).cpu().numpy()
+            # the feature gradient's own tolerance (differences of nearby rows)
+            assert np.all(np.abs(a - b) <= 2e-3 * np.abs(b) + 1e-4 * max(float(np.abs(b).max()), 1e-12))
+        torch.cuda.synchronize()
+        assert PLOO.lattice_info(lat)["status"] == 0
+    finally:
+        L.plattice_debug_set_blur_streaming(0)
