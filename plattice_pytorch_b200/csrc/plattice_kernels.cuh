@@ -1247,14 +1247,16 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
     return old;
 }
 
-__device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase) {
+// (`counter`: the lattice's bar_count unless the kernel has its own)
+__device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase, unsigned* counter = nullptr) {
     __syncthreads();
     ++phase;
     if (threadIdx.x == 0) {
+        unsigned* const cnt = counter ? counter : &hdr->bar_count;
         const unsigned target = phase * gridDim.x;
-        const unsigned arrived = atom_add_acq_rel(&hdr->bar_count, 1u) + 1u;
+        const unsigned arrived = atom_add_acq_rel(cnt, 1u) + 1u;
         int spins = 0;
-        while (arrived < target && ld_acquire(&hdr->bar_count) < target) {
+        while (arrived < target && ld_acquire(cnt) < target) {
             if (++spins > kBarrierSpin) {
                 atomicOr(&hdr->status, PL_ST_SPIN);
                 break;
@@ -1266,7 +1268,7 @@ __device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase
 }
 
 // At the end of a kernel with grid barriers: the last CTA to leave resets
-// the barrier counter (and this exit counter) for the next launch on the
+// the barrier counters (and this exit counter) for the next launch on the
 // lattice, and reports the status word of the call when `slot` is set.  Every
 // CTA has passed its last barrier by then.
 __device__ __forceinline__ void grid_exit(LatticeHeader* hdr, unsigned long long* slot, unsigned seq) {
@@ -1281,6 +1283,7 @@ __device__ __forceinline__ void grid_exit(LatticeHeader* hdr, unsigned long long
                 *reinterpret_cast<volatile unsigned long long*>(slot) = ((unsigned long long)seq << 32) | st;
             }
             atomicExch(&hdr->bar_count, 0u);
+            atomicExch(&hdr->bar_zero, 0u);
             atomicExch(&hdr->bar_gen, 0u);
         }
     }
@@ -1516,7 +1519,10 @@ k_splat_nbr(const float* __restrict__ vals, const float* __restrict__ wt, Geo ge
 // The splat of a call on a kept lattice, whose value rows must start at zero:
 // one cooperative launch that zeroes the first m rows (cp floats each, float4
 // stores), waits at one grid barrier, then takes the tiles in turn -- in place
-// of a separate zeroing kernel, whose launch costs more than its stores.
+// of a separate zeroing kernel, whose launch costs more than its stores.  Its
+// barrier counts on bar_zero, which the blur that follows leaves alone; the
+// kernel after that blur (the slice), or that blur's own exit, zeroes it, so
+// this kernel ends without an exit protocol.
 template <int PD, int V, bool FWD>
 __global__ void __launch_bounds__(Cfg<PD>::P)
 k_splat_zeroed(const float* __restrict__ vals, const float* __restrict__ wt, Geo geo, LatView L, float* lat,
@@ -1532,11 +1538,10 @@ k_splat_zeroed(const float* __restrict__ vals, const float* __restrict__ wt, Geo
         for (size_t i = i0; i < n / 4; i += stride) b4[i] = z;
         for (size_t i = (n & ~(size_t)3) + i0; i < n; i += stride) lat[i] = 0.0f;
     }
-    grid_barrier(L.hdr, phase);
+    grid_barrier(L.hdr, phase, &L.hdr->bar_zero);
     for (int tile = blockIdx.x; tile < geo.tiles; tile += gridDim.x)
         splat_tile<PD, V, FWD>(tile, tile_pos<Cfg<PD>::TW, Cfg<PD>::TH>(geo, tile), threadIdx.x, vals, wt, geo, L,
                                ScrView{}, 0, lat, sm, CtaSync{});
-    grid_exit(L.hdr, nullptr, 0u);
 }
 
 // ---------------------------------------------------------------- bulk copies
@@ -1885,11 +1890,13 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
 }
 
 // Zeroes the grid-barrier counters of the lattice (one thread): called at the
-// start of the kernel that follows a blur, whose CTAs have all finished.
+// start of the kernel that follows a blur, whose CTAs (and those of the
+// zero-then-splat kernel before it) have all finished.
 __device__ __forceinline__ void reset_barrier(LatticeHeader* hdr) {
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         hdr->bar_count = 0u;
         hdr->bar_gen = 0u;
+        hdr->bar_zero = 0u;
     }
 }
 

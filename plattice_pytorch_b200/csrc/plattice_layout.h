@@ -71,7 +71,8 @@ typedef struct {
     int n, pd, vd, tiles;
     unsigned bar_count, bar_gen;   /* grid barrier of the cooperative blur kernel */
     int blur_final;  /* which value buffer (0/1) holds the last blur's result */
-    int pad[53];     /* header is 256 bytes */
+    unsigned bar_zero;   /* grid barrier of the zero-then-splat kernel */
+    int pad[52];     /* header is 256 bytes */
 } LatticeHeader;
 
 typedef char pl_header_is_256_bytes[(sizeof(LatticeHeader) == 256) ? 1 : -1];
