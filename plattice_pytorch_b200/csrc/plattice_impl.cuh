@@ -247,7 +247,7 @@ constexpr int kCoopPerSm = 1;
 
 template <int PD, int CP>
 cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1, int reverse,
-                            int* final_flag = nullptr, int extra_flags = 0) {
+                            int* final_flag = nullptr) {
     if (!final_flag) final_flag = &Lv.hdr->blur_final;
     int n = 0;
     cudaError_t e = kernel_once(reinterpret_cast<const void*>(k_blur_all<PD, CP>), blur_attr<PD, CP>, &n);
@@ -256,7 +256,7 @@ cudaError_t launch_blur_all(const CallArgs& a, LatView Lv, float* b0, float* b1,
                                    (a.lay.slots + kBlurThreads - 1) / kBlurThreads);
     PL_LAUNCH(reverse ? STAGE_BLUR_BWD : STAGE_BLUR_FWD, a.stream,
               e = launch_k(k_blur_all<PD, CP>, dim3(blocks), dim3(kBlurThreads), kBlurQueueBytes, a.stream, true, Lv,
-                           b0, b1, a.bstate, reverse, final_flag, a.blur_flags | extra_flags));
+                           b0, b1, a.bstate, reverse, final_flag, a.blur_flags));
     return e;
 }
 
@@ -433,16 +433,16 @@ cudaError_t fgrad_v(const CallArgs& a) {
     // R: the forward's lattice values
     e = splat_zeroed<PD, V, true>(a, geo, Lv, a.values, nullptr, a.v0, STAGE_SPLAT_FWD);
     if (e != cudaSuccess) return e;
-    // (both blurs reset the barrier counters themselves: no slice follows them)
-    e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0, a.flags, kBlurExit);
+    e = launch_blur_all<PD, CPF>(a, Lv, a.v0, a.v1, 0, a.flags);
     if (e != cudaSuccess) return e;
     // H: the lattice gradient, V+1 channels of (G, -G.out) weighted by 1/Z
     const size_t n = (size_t)a.lay.b * (size_t)a.lay.n_img;
-    e = launch_k(k_fgrad_prep<V>, dim3(grid), dim3(256), 0, a.stream, false, a.evec, a.grad_in, a.out_in, n);
+    e = launch_k(k_fgrad_prep<V>, dim3(grid), dim3(256), 0, a.stream, false, a.evec, a.grad_in, a.out_in, n,
+                 Lv.hdr);
     if (e != cudaSuccess) return e;
     e = splat_zeroed<PD, V + 1, false>(a, geo, Lv, a.evec, a.weight_in, a.hbuf0, STAGE_SPLAT_BWD);
     if (e != cudaSuccess) return e;
-    e = launch_blur_all<PD, CPF>(a, Lv, a.hbuf0, a.hbuf1, 1, a.flags + 1, kBlurExit);
+    e = launch_blur_all<PD, CPF>(a, Lv, a.hbuf0, a.hbuf1, 1, a.flags + 1);
     if (e != cudaSuccess) return e;
     return launch_k(k_fgrad<PD, V>, tile_grid(a), dim3(Cfg<PD>::P), 0, a.stream, false, a.out, a.features,
                     a.values, a.grad_in, a.out_in, a.weight_in, geo, embed_consts(PD), Lv, (const float*)a.v0,

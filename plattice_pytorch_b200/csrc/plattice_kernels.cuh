@@ -1267,28 +1267,6 @@ __device__ __forceinline__ void grid_barrier(LatticeHeader* hdr, unsigned& phase
     __syncthreads();
 }
 
-// At the end of a kernel with grid barriers: the last CTA to leave resets
-// the barrier counters (and this exit counter) for the next launch on the
-// lattice, and reports the status word of the call when `slot` is set.  Every
-// CTA has passed its last barrier by then.
-__device__ __forceinline__ void grid_exit(LatticeHeader* hdr, unsigned long long* slot, unsigned seq) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&hdr->bar_gen, 1u);
-        if (prev == gridDim.x - 1) {
-            __threadfence();
-            if (slot) {
-                const unsigned st = (unsigned)atomicOr(&hdr->status, 0);
-                *reinterpret_cast<volatile unsigned long long*>(slot) = ((unsigned long long)seq << 32) | st;
-            }
-            atomicExch(&hdr->bar_count, 0u);
-            atomicExch(&hdr->bar_zero, 0u);
-            atomicExch(&hdr->bar_gen, 0u);
-        }
-    }
-}
-
 // ---------------------------------------------------------------- splat
 
 // FWD: [v*w, w] per slot (permutohedral.cu:286-293); otherwise
@@ -1788,8 +1766,6 @@ __device__ __noinline__ void blur_streaming(const int2* nbr, uint8_t* bstate, La
 
 constexpr int kBlurHalf = 1;     // flags of k_blur_all: bfloat16 rows in the streaming passes
 constexpr int kBlurStream = 2;   // the streaming passes whatever the lattice's size (tests)
-constexpr int kBlurExit = 4;     // the blur resets the grid-barrier counters itself at its exit (no
-                                 // kernel of the call that follows it does)
 
 // The resident blur: every vertex's row stays in a register of one thread
 // for the K passes, passes in fused pairs (one grid barrier per pair).  CTA b
@@ -1885,8 +1861,7 @@ __global__ void __launch_bounds__(kBlurThreads) k_blur_all(LatView L, float* buf
     // this lattice starts.  The kernel that follows a blur in stream order
     // (the slice, or the feature-gradient kernels) zeroes them when it starts
     // (reset_barrier), after every CTA of the blur has finished; so the blur
-    // ends without the exit protocol's fence and atomics, unless asked for it.
-    if (flags & kBlurExit) grid_exit(L.hdr, nullptr, 0u);
+    // ends without an exit protocol (a fence and counter atomics per CTA).
 }
 
 // Zeroes the grid-barrier counters of the lattice (one thread): called at the
@@ -2135,7 +2110,8 @@ k_slice_pipe(float* __restrict__ out, float* __restrict__ wout, Geo geo, LatView
 // e_p = (G_p, -(G_p . out_p)): the V+1 channels splatted (times 1/Z_p) for H
 template <int V>
 static __global__ void k_fgrad_prep(float* __restrict__ ev, const float* __restrict__ grad,
-                                    const float* __restrict__ out, size_t n) {
+                                    const float* __restrict__ out, size_t n, LatticeHeader* hdr) {
+    reset_barrier(hdr);   // (it follows a blur)
     for (size_t p = (size_t)blockIdx.x * blockDim.x + threadIdx.x; p < n; p += (size_t)gridDim.x * blockDim.x) {
         float dot = 0.0f;
 #pragma unroll
@@ -2156,6 +2132,7 @@ k_fgrad(float* __restrict__ gfeat, const float* __restrict__ feat, const float* 
         const int* flags, unsigned long long* st_slot, unsigned st_seq) {
     using C = Cfg<PD>;
     report_status(st_slot, st_seq, L.hdr);
+    reset_barrier(L.hdr);   // (it follows a blur)
     constexpr int K = C::K, P = C::P, SLOTS = C::SLOTS;
     constexpr int CP = pad_ch(V + 1);
     __shared__ int svid[SLOTS];

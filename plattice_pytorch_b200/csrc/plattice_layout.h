@@ -69,7 +69,7 @@ typedef struct {
     int u_total;     /* staged (tile-unique) keys */
     int cap_log2;    /* hash table capacity in use (log2 of cells) */
     int n, pd, vd, tiles;
-    unsigned bar_count, bar_gen;   /* grid barrier of the cooperative blur kernel */
+    unsigned bar_count, bar_gen;   /* grid barrier of the cooperative blur kernel; bar_gen spare (zero) */
     int blur_final;  /* which value buffer (0/1) holds the last blur's result */
     unsigned bar_zero;   /* grid barrier of the zero-then-splat kernel */
     int pad[52];     /* header is 256 bytes */
