@@ -97,8 +97,10 @@ int plattice_forward(float* weight_out, float* out, const float* values, const f
  * "not yet used by a backward" and "used", are treated alike).  `features` is
  * read only by a rebuild and may be NULL otherwise.  `scratch` is always
  * required: scratch_bytes from plattice_workspace_sizes for a rebuild, at
- * least plattice_reuse_scratch_size otherwise.  Replaces permuto_filter_grad
- * (permutohedral.cu:717), which always rebuilds. */
+ * least plattice_reuse_scratch_size otherwise.  After any call on a kept
+ * lattice returns an error, build the lattice again (plattice_forward) before
+ * the next call on it.  Replaces permuto_filter_grad (permutohedral.cu:717),
+ * which always rebuilds. */
 int plattice_backward(float* grad_values_out, const float* grad, const float* weight_in,
                       const float* features, void* lattice, size_t lattice_bytes,
                       int lattice_state, void* scratch, size_t scratch_bytes, int pd, int vd,
