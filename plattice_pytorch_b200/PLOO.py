@@ -129,9 +129,12 @@ class Lattice:
     """A lattice built on the device for one ``features`` tensor.
 
     Holds the lattice buffer (kept for backward calls) and optionally the
-    scratch buffer of the build (needed by :func:`vertex_keys`)."""
+    scratch buffer of the build (needed by :func:`vertex_keys`).  A call on it
+    that returns an error marks it ``broken`` (the call may have stopped part
+    way, with the lattice's header in between two states): a backward then
+    rebuilds, and the calls that need a kept lattice refuse it."""
 
-    __slots__ = ("buf", "scratch", "h", "w", "pd", "vd", "device", "used", "_feat_ref",
+    __slots__ = ("buf", "scratch", "h", "w", "pd", "vd", "device", "used", "broken", "_feat_ref",
                  "_feat_version", "_feat_ptr", "__weakref__")
 
     def __init__(self, features, vd, buf, scratch, shape=None):
@@ -141,16 +144,18 @@ class Lattice:
         self.vd = int(vd)
         self.device = features.device
         self.used = False
+        self.broken = False
         self._feat_ref = weakref.ref(features)
         self._feat_version = features._version
         self._feat_ptr = features.data_ptr()
 
     def matches(self, features, vd, same_object=True):
-        """True when this lattice was built from ``features`` as it is now.
-        ``same_object=False`` drops the identity test, for callers (autograd's
-        saved tensors) that hand back a new tensor object over the same,
-        version-checked storage.  A lattice serves every vd."""
-        if same_object and self._feat_ref() is not features:
+        """True when this lattice was built from ``features`` as it is now
+        (and no call on it has failed since).  ``same_object=False`` drops the
+        identity test, for callers (autograd's saved tensors) that hand back a
+        new tensor object over the same, version-checked storage.  A lattice
+        serves every vd."""
+        if self.broken or (same_object and self._feat_ref() is not features):
             return False
         return (features.data_ptr() == self._feat_ptr
                 and tuple(features.shape) == (self.h, self.w, self.pd)
@@ -261,6 +266,8 @@ def lattice_backward(features, grad_values, weight_saved, lattice=None, saved=Fa
                weight_saved.data_ptr(), features.data_ptr(), buf.data_ptr(), lb, state, scratch.data_ptr(),
                sbytes, pd, vd, w, h, _raw_stream(dev.index))
     if rc:
+        if lattice is not None:
+            lattice.broken = True
         _raise("plattice_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
     if lattice is not None:
         lattice.used = True
@@ -272,6 +279,7 @@ def lattice_backward(features, grad_values, weight_saved, lattice=None, saved=Fa
 
 def _check_kept(lattice, t, name):
     _require(isinstance(lattice, Lattice), "lattice must be a Lattice from lattice_forward")
+    _require(not lattice.broken, "lattice is unusable after a failed call on it: build it again")
     _check_input(t, name)
     _require(t.dim() == 3, f"{name} must be [H, W, vd]")
     _require(t.dtype == torch.float32, f"{name} must be float32")
@@ -299,6 +307,7 @@ def lattice_filter(lattice, values):
                lattice.buf.data_ptr(), lattice.buf.numel(), ws.data_ptr(), wsb, pd, vd, w, h,
                _raw_stream(dev.index))
     if rc:
+        lattice.broken = True
         _raise("plattice_filter", rc, f"h={h} w={w} pd={pd} vd={vd}")
     if _CHECK and h * w > 0:
         _sync_check(lattice, "plattice_filter")
@@ -321,6 +330,7 @@ def lattice_filter_backward(lattice, grad_values, weight_saved):
                weight_saved.data_ptr(), lattice.buf.data_ptr(), lattice.buf.numel(), ws.data_ptr(), wsb,
                pd, vd, w, h, _raw_stream(dev.index))
     if rc:
+        lattice.broken = True
         _raise("plattice_filter_backward", rc, f"h={h} w={w} pd={pd} vd={vd}")
     if _CHECK and h * w > 0:
         _sync_check(lattice, "plattice_filter_backward")
@@ -334,6 +344,7 @@ def feature_grad(lattice, features, values, grad_out, weight, out):
     (the reference returns no feature gradient).  The slope is that of the
     piecewise-linear filter inside each pixel's simplex."""
     _require(isinstance(lattice, Lattice), "lattice must be a Lattice from lattice_forward")
+    _require(not lattice.broken, "lattice is unusable after a failed call on it: build it again")
     _require(lattice.matches(features, lattice.vd, same_object=False),
              "lattice was not built from these features")
     for t, name in ((values, "values"), (grad_out, "grad_out"), (out, "out")):
@@ -350,6 +361,7 @@ def feature_grad(lattice, features, values, grad_out, weight, out):
                weight.data_ptr(), values.data_ptr(), features.data_ptr(), lattice.buf.data_ptr(),
                lattice.buf.numel(), ws.data_ptr(), wsb, pd, vd, w, h, _raw_stream(dev.index))
     if rc:
+        lattice.broken = True
         _raise("plattice_feature_grad", rc, f"h={h} w={w} pd={pd} vd={vd}")
     if _CHECK and h * w > 0:
         _sync_check(lattice, "plattice_feature_grad")
@@ -361,7 +373,7 @@ class BatchLattice:
     for the batch's backward (one buffer; the images' vertices are kept apart
     by the image index in the key hash)."""
 
-    __slots__ = ("buf", "shape", "vd", "device", "used", "_feat_ref", "_feat_version", "_feat_ptr",
+    __slots__ = ("buf", "shape", "vd", "device", "used", "broken", "_feat_ref", "_feat_version", "_feat_ptr",
                  "__weakref__")
 
     def __init__(self, features, vd, buf):
@@ -370,12 +382,13 @@ class BatchLattice:
         self.vd = int(vd)
         self.device = features.device
         self.used = False
+        self.broken = False   # a call on it returned an error: the backward rebuilds
         self._feat_ref = weakref.ref(features)
         self._feat_version = features._version
         self._feat_ptr = features.data_ptr()
 
     def matches(self, features, vd, same_object=True):
-        if same_object and self._feat_ref() is not features:
+        if self.broken or (same_object and self._feat_ref() is not features):
             return False
         return (features.data_ptr() == self._feat_ptr
                 and tuple(features.shape) == self.shape and features.device == self.device
@@ -442,6 +455,8 @@ def batch_backward(features, grad_values, weight_saved, lattice=None, saved=Fals
                weight_saved.data_ptr(), features.data_ptr(), buf.data_ptr(), lb, state, scratch.data_ptr(),
                sbytes, b, pd, vd, w, h, _raw_stream(dev.index))
     if rc:
+        if lattice is not None:
+            lattice.broken = True
         _raise("plattice_backward_batch", rc, f"b={b} h={h} w={w} pd={pd} vd={vd}")
     if lattice is not None:
         lattice.used = True

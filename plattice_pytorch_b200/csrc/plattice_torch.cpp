@@ -169,6 +169,9 @@ struct PermutoLatticeFn : public torch::autograd::Function<PermutoLatticeFn> {
                                          weight.data_ptr<float>(), features.data_ptr<float>(), lattice.data_ptr(),
                                          (size_t)lattice.numel(), state, scratch.data_ptr(), sbytes, pd, vd, w, h,
                                          at::cuda::getCurrentCUDAStream(features.device().index()).stream());
+            // a failed call may have stopped part way: a later backward on
+            // this graph rebuilds the lattice instead of reusing it
+            if (rc != 0) ctx->saved_data["keep"] = false;
             TORCH_CHECK(rc == 0, failure("plattice_backward", rc, h, w, pd, vd));
         }
         ctx->saved_data["used"] = true;

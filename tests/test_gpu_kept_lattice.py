@@ -180,3 +180,33 @@ def test_every_call_kind_in_turn_on_one_lattice(streaming, dev):
         assert PLOO.lattice_info(lat)["status"] == 0
     finally:
         L.plattice_debug_set_blur_streaming(0)
+
+
+def test_a_failed_call_marks_its_lattice_broken(dev):
+    """A device failure of the build (a hash table forced below the vertex
+    count) is reported by the next call, a backward on that lattice, which
+    marks the lattice broken: the backward after it rebuilds (the golden value
+    gradient), and the calls that need a kept lattice refuse it."""
+    from plattice_pytorch_b200 import PLOO, _lib
+    d = np.load(os.path.join(GOLDEN, "ref_blobs64_pd5_vd3.npz"))
+    ft, vt, gt, wt = (torch.from_numpy(d[k]).to(dev) for k in ("features", "values", "grad", "weight"))
+    L = _lib.lib()
+    check = PLOO._CHECK
+    PLOO.check_device_status()   # nothing pending from earlier tests
+    try:
+        PLOO._CHECK = False
+        L.plattice_debug_set_table_cap_log2(6)   # 64 cells for 1225 vertices
+        _, _, lat = PLOO.lattice_forward(ft, vt)
+        PLOO.lattice_info(lat)                   # synchronises: the build's failure is recorded
+        L.plattice_debug_set_table_cap_log2(0)
+        with pytest.raises(_lib.PlatticeError) as ei:
+            PLOO.lattice_backward(ft, gt, wt, lat)
+        assert ei.value.status == _lib.ERR_DEVICE
+        assert lat.broken
+        gv = PLOO.lattice_backward(ft, gt, wt, lat)   # rebuilds
+        assert _close(gv, torch.from_numpy(d["grad_out"]))
+        with pytest.raises(RuntimeError, match="unusable"):
+            PLOO.lattice_filter(lat, vt)
+    finally:
+        L.plattice_debug_set_table_cap_log2(0)
+        PLOO._CHECK = check

@@ -235,3 +235,22 @@ def test_cpp_function_extension_loads_and_checks_inputs(lib):
         fn(torch.zeros(4, 4, 5), torch.zeros(4, 4, 3))
     with pytest.raises(RuntimeError, match="features must be CUDA"):
         plattice.PermutoLatticeFunction.apply(torch.zeros(4, 4, 5), torch.zeros(4, 4, 3))
+
+
+def test_a_broken_lattice_no_longer_matches_and_is_refused():
+    """Host logic of a lattice after a failed call on it (CPU tensors stand in
+    for the device buffers; no library call): it stops matching its features,
+    so a backward rebuilds, and the kept-lattice calls refuse it."""
+    from plattice_pytorch_b200 import PLOO
+    f = torch.zeros(4, 5, 3)
+    lat = PLOO.Lattice(f, 2, torch.empty(16, dtype=torch.uint8), None)
+    assert lat.matches(f, 2) and not lat.broken
+    lat.broken = True
+    assert not lat.matches(f, 2) and not lat.matches(f, 2, same_object=False)
+    with pytest.raises(RuntimeError, match="unusable"):
+        PLOO._check_kept(lat, torch.zeros(4, 5, 2), "values")
+    fb = torch.zeros(2, 4, 5, 3)
+    b = PLOO.BatchLattice(fb, 2, torch.empty(16, dtype=torch.uint8))
+    assert b.matches(fb, 2)
+    b.broken = True
+    assert not b.matches(fb, 2)
